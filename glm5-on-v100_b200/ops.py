@@ -1,0 +1,398 @@
+"""Torch-facing operators of the DSA hot path — a drop-in for the reference's
+``vllm._sm70_ops`` wrappers (reference/_sm70_ops.py:1848-1991) and the
+``torch.ops._C.sm70_*`` schemas they call (csrc/torch_bindings.cpp hunk of
+patches/glm5-v100-sm70-full.patch), plus the upstream ``persistent_topk`` op
+the SM70 indexer uses (reference/sparse_attn_indexer.py:632-639).
+
+Every operator is registered under the ``dsa_b200`` torch library namespace with
+the reference's schema (same argument names, order, mutability and return
+type) and a fake implementation, and every wrapper below has the reference's
+Python signature. The CUDA implementation is the C ABI of libdsa_b200.so,
+called on the current stream with raw device pointers; argument checks mirror
+the reference's TORCH_CHECKs and raise RuntimeError.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+import torch
+
+from . import _lib as L
+
+NAMESPACE = "dsa_b200"
+
+# Device-side waits of the P2P shard exchange give up after this long and
+# report DSA_ERR_TIMEOUT instead of hanging (the reference's spins are
+# unbounded, csrc/attention/sm70_mla_decode.cu:2196).
+P2P_TIMEOUT_NS = int(float(os.environ.get("DSA_B200_P2P_TIMEOUT_S", "5")) * 1e9)
+
+_DTYPE = {torch.float16: L.DSA_F16, torch.bfloat16: L.DSA_BF16, torch.float32: L.DSA_F32}
+DSMLA_ROW_BYTES = 656
+IDXK_FP8_ROW_BYTES = 132
+
+
+def _check(cond, msg):
+    if not cond:
+        raise RuntimeError(msg)
+
+
+def _vp(t):
+    return ctypes.c_void_p(t.data_ptr()) if t is not None else None
+
+
+def _stream(dev):
+    return ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+
+
+def _rowmajor(t, name):
+    _check(t.dim() == 2 and t.stride(1) == 1, f"{name} must be 2-D with unit inner stride")
+
+
+def _int32(t, name):
+    _check(t.dtype == torch.int32, f"{name} must be int32")
+
+
+# ----------------------------------------------------------------- impls
+def _sparse_mla_decode_impl(o, lse, q, kv_cache, idx, block_table, seq_lens, scale):
+    _check(q.is_cuda and kv_cache.is_cuda, "q and kv_cache must be CUDA tensors")
+    _check(q.dtype in (torch.float16, torch.bfloat16), "q must be fp16 or bf16")
+    _check(o.dtype in (torch.float16, torch.bfloat16), "o must be fp16 or bf16")
+    _check(lse.dtype == torch.float32, "lse must be fp32")
+    _int32(idx, "idx")
+    _int32(block_table, "block_table")
+    _int32(seq_lens, "seq_lens")
+    if kv_cache.dtype == torch.uint8:
+        _check(kv_cache.size(-1) == DSMLA_ROW_BYTES, "fp8 kv_cache last dim must be 656 (fp8_ds_mla layout)")
+        fmt, row = L.DSA_FP8_DS_MLA, DSMLA_ROW_BYTES
+    else:
+        _check(kv_cache.dtype in (torch.float16, torch.bfloat16) and kv_cache.size(-1) == 576,
+               "kv_cache must be fp16/bf16 [.., page, 576] or uint8 fp8_ds_mla [.., page, 656]")
+        fmt, row = _DTYPE[kv_cache.dtype], 576
+    _check(q.dim() == 3 and q.size(2) == 576, "q last dim must be 576")
+    _check(o.dim() == 3 and o.size(2) == 512, "o last dim must be 512")
+    _check(q.is_contiguous() and o.is_contiguous() and lse.is_contiguous() and kv_cache.is_contiguous(),
+           "q, o, lse and kv_cache must be contiguous")
+    B, H = q.size(0), q.size(1)
+    _check(tuple(o.shape[:2]) == (B, H) and tuple(lse.shape) == (B, H), "o/lse shape mismatch with q")
+    _rowmajor(idx, "idx")
+    _rowmajor(block_table, "block_table")
+    _check(idx.size(0) >= B and block_table.size(0) >= B and seq_lens.numel() >= B,
+           "idx/block_table/seq_lens have fewer rows than q")
+    topk = idx.size(1)
+    page = kv_cache.size(-2)
+    n_rows = kv_cache.numel() // row
+    with torch.cuda.device(q.device):
+        ws_bytes = L.lib().dsa_sparse_mla_decode_workspace_bytes(B, H, topk)
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=q.device) if ws_bytes else None
+        L.call("dsa_sparse_mla_decode", _vp(o), _DTYPE[o.dtype], _vp(lse), _vp(q), _DTYPE[q.dtype],
+               _vp(kv_cache), fmt, n_rows, page, _vp(idx), idx.stride(0), _vp(block_table),
+               block_table.stride(0), block_table.size(1), _vp(seq_lens.contiguous()), B, H, topk,
+               float(scale), _vp(ws), ws_bytes, _stream(q.device))
+
+
+def _k_cache_format(k_cache):
+    if k_cache.dtype == torch.uint8:
+        _check(k_cache.size(-1) == IDXK_FP8_ROW_BYTES, "fp8 indexer k_cache last dim must be 132")
+        return L.DSA_FP8_IDXK, IDXK_FP8_ROW_BYTES
+    _check(k_cache.dtype in (torch.float16, torch.bfloat16), "k_cache must be fp16, bf16 or uint8 (fp8)")
+    _check(k_cache.size(-1) == 128, "indexer head_dim must be 128")
+    return _DTYPE[k_cache.dtype], 128
+
+
+def _logits_common(score, k_cache, weights, block_table, seq_lens):
+    _check(score.dtype == torch.float32, "score must be fp32")
+    _check(weights.dtype in _DTYPE, "weights must be fp16, bf16 or fp32")
+    _int32(block_table, "block_table")
+    _int32(seq_lens, "seq_lens")
+    _rowmajor(score, "score")
+    _rowmajor(block_table, "block_table")
+    _check(k_cache.is_contiguous() and weights.is_contiguous(), "k_cache and weights must be contiguous")
+    fmt, row = _k_cache_format(k_cache)
+    page = k_cache.size(-2)
+    _check(page > 0 and (page & (page - 1)) == 0, "indexer cache page size must be a power of two")
+    return fmt, k_cache.numel() // row, page
+
+
+def _indexer_logits_impl(score, q, k_cache, weights, block_table, seq_lens, hist):
+    _check(q.dtype in (torch.float16, torch.bfloat16), "q must be fp16 or bf16")
+    _check(q.dim() == 3 and q.size(2) == 128, "indexer head_dim must be 128")
+    _check(q.is_contiguous(), "q must be contiguous")
+    fmt, n_rows, page = _logits_common(score, k_cache, weights, block_table, seq_lens)
+    B, Hi = q.size(0), q.size(1)
+    _check(tuple(weights.shape) == (B, Hi), "weights must be [B, n_ihead]")
+    hp = None
+    if hist is not None:
+        _check(hist.dtype == torch.int32 and hist.is_contiguous() and tuple(hist.shape) == (B, 4096),
+               "hist must be contiguous int32 [B, 4096]")
+        hp = _vp(hist)
+    with torch.cuda.device(q.device):
+        L.call("dsa_indexer_logits", _vp(score), score.stride(0), score.size(1), _vp(q), _DTYPE[q.dtype],
+               _vp(k_cache), fmt, n_rows, page, _vp(weights), _DTYPE[weights.dtype], _vp(block_table),
+               block_table.stride(0), block_table.size(1), _vp(seq_lens.contiguous()), B, Hi, hp,
+               _stream(q.device))
+
+
+def _indexer_logits_packed_impl(score, q_packed, k_cache, weights, block_table, seq_lens):
+    _check(q_packed.dtype in (torch.float16, torch.bfloat16) and q_packed.is_contiguous(),
+           "q_packed must be contiguous fp16/bf16")
+    fmt, n_rows, page = _logits_common(score, k_cache, weights, block_table, seq_lens)
+    B = score.size(0)
+    nqt = (B + 15) // 16
+    _check(tuple(q_packed.shape) == (32, nqt, 8, 16, 16), "q_packed must be [32, ceil(B/16), 8, 16, 16]")
+    _check(tuple(weights.shape) == (B, 32), "weights must be [B, 32]")
+    with torch.cuda.device(score.device):
+        L.call("dsa_indexer_logits_packed", _vp(score), score.stride(0), score.size(1), _vp(q_packed),
+               _DTYPE[q_packed.dtype], _vp(k_cache), fmt, n_rows, page, _vp(weights), _DTYPE[weights.dtype],
+               _vp(block_table), block_table.stride(0), block_table.size(1), _vp(seq_lens.contiguous()), B,
+               _stream(score.device))
+
+
+def _decode_topk_impl(idx, score, seq_lens, hist, k):
+    _check(score.dtype == torch.float32, "score must be fp32")
+    _int32(idx, "idx")
+    _int32(seq_lens, "seq_lens")
+    _rowmajor(idx, "idx")
+    _rowmajor(score, "score")
+    B = score.size(0)
+    _check(idx.size(0) == B and idx.size(1) == k, "idx must be [B, K]")
+    _check(hist.dtype == torch.int32 and hist.is_contiguous() and tuple(hist.shape) == (B, 4096),
+           "hist must be contiguous int32 [B, 4096]")
+    with torch.cuda.device(score.device):
+        L.call("dsa_decode_topk", _vp(idx), idx.stride(0), _vp(score), score.stride(0), score.size(1),
+               _vp(seq_lens.contiguous()), _vp(hist), B, int(k), _stream(score.device))
+
+
+def _persistent_topk_impl(score, lens, topk_idx, workspace, k, max_seq_len):
+    _check(score.dtype == torch.float32, "score must be fp32")
+    _int32(topk_idx, "topk_idx")
+    _int32(lens, "lengths")
+    _rowmajor(score, "score")
+    _rowmajor(topk_idx, "topk_idx")
+    n = score.size(0)
+    _check(lens.numel() == n and topk_idx.size(0) == n and topk_idx.size(1) >= k, "topk shape mismatch")
+    with torch.cuda.device(score.device):
+        L.call("dsa_topk_rows", _vp(topk_idx), topk_idx.stride(0), _vp(score), score.stride(0), score.size(1),
+               _vp(lens.reshape(-1).contiguous()), n, int(k), _stream(score.device))
+
+
+def _indexer_k_store_impl(kv_cache, k, slot_mapping):
+    _check(kv_cache.is_cuda and k.is_cuda, "kv_cache and k must be CUDA tensors")
+    _check(k.dtype in (torch.float16, torch.bfloat16), "k must be fp16 or bf16")
+    _int32(slot_mapping, "slot_mapping")
+    _check(kv_cache.is_contiguous() and k.is_contiguous(), "kv_cache and k must be contiguous")
+    head_dim = k.size(-1)
+    n_tok = k.size(0)
+    if kv_cache.dtype == torch.uint8:
+        _check(head_dim == 128, "fp8 indexer store requires head_dim == 128")
+        _check(kv_cache.size(-1) == IDXK_FP8_ROW_BYTES, "fp8 indexer kv_cache last dim must be 132")
+        fmt, row = L.DSA_FP8_IDXK, IDXK_FP8_ROW_BYTES
+    else:
+        _check(kv_cache.dtype in (torch.float16, torch.bfloat16), "kv_cache must be fp16, bf16 or uint8 (fp8)")
+        fmt, row = _DTYPE[kv_cache.dtype], head_dim
+    if n_tok == 0:
+        return
+    with torch.cuda.device(k.device):
+        L.call("dsa_indexer_k_store", _vp(kv_cache), fmt, kv_cache.numel() // row, _vp(k), _DTYPE[k.dtype],
+               head_dim, _vp(slot_mapping.contiguous()), n_tok, _stream(k.device))
+
+
+def _shard_merge_impl(out, allf, dst_rows, dst_base, topk):
+    _check(allf.is_cuda and allf.is_contiguous() and allf.dim() == 3, "allf must be contiguous [tp, R, 2K] cuda")
+    _check(allf.dtype == torch.float32, "allf must be fp32")
+    _check(out.dtype == torch.int32 and out.dim() == 2 and out.stride(1) == 1, "out must be int32 [rows, >=K]")
+    tp, R = allf.size(0), allf.size(1)
+    _check(allf.size(2) == 2 * topk, "allf last dim must be 2*topk")
+    _check(dst_base >= 0 or dst_rows.numel() == R, "need dst_rows when dst_base < 0")
+    dp = _vp(dst_rows.contiguous()) if dst_base < 0 else None
+    with torch.cuda.device(allf.device):
+        L.call("dsa_indexer_shard_merge", _vp(out), out.stride(0), _vp(allf), dp, int(dst_base), tp, R,
+               int(topk), _stream(allf.device))
+
+
+_ERR_FLAGS: dict = {}
+
+
+def p2p_error_flag(device) -> torch.Tensor:
+    """Per-device int32 word the bounded P2P waits set to DSA_ERR_TIMEOUT."""
+    device = torch.device(device)
+    t = _ERR_FLAGS.get(device)
+    if t is None:
+        t = torch.zeros(1, dtype=torch.int32, device=device)
+        _ERR_FLAGS[device] = t
+    return t
+
+
+def check_p2p_status(device) -> None:
+    """Raise if a bounded P2P wait on `device` timed out (synchronises)."""
+    f = p2p_error_flag(device)
+    v = int(f.item())
+    if v != 0:
+        f.zero_()
+        raise RuntimeError(f"P2P shard exchange wait failed on {device}: status {L.STATUS_NAMES.get(v, v)}")
+
+
+def _u64_array(t, tp):
+    _check(t.device.type == "cpu" and t.dtype == torch.int64 and t.numel() >= tp, "pointer tensors must be CPU int64")
+    arr = (ctypes.c_uint64 * tp)(*[int(x) for x in t.reshape(-1)[:tp].tolist()])
+    return arr
+
+
+def _shard_merge_p2p_impl(out, data_ptrs, flag_ptrs, dst_rows, dst_base, topk, tp, R, seq, slot_off):
+    _check(out.dtype == torch.int32 and out.dim() == 2 and out.stride(1) == 1, "out must be int32 2-D")
+    _check(dst_base >= 0 or dst_rows.numel() == R, "need dst_rows when dst_base < 0")
+    dptr = _u64_array(data_ptrs, tp)
+    fptr = _u64_array(flag_ptrs, tp)
+    dp = _vp(dst_rows.contiguous()) if dst_base < 0 else None
+    with torch.cuda.device(out.device):
+        L.call("dsa_indexer_shard_merge_p2p", _vp(out), out.stride(0), dptr, fptr, dp, int(dst_base), int(topk),
+               int(tp), int(R), int(seq), int(slot_off), P2P_TIMEOUT_NS, _vp(p2p_error_flag(out.device)),
+               _stream(out.device))
+
+
+class _IpcBuffer:
+    """Owns a cudaMalloc'd IPC-exportable allocation; exposed to torch via
+    __cuda_array_interface__ and freed when the last tensor view dies."""
+
+    def __init__(self, ptr: int, nbytes: int):
+        self.ptr = ptr
+        self.nbytes = nbytes
+        self.__cuda_array_interface__ = {"shape": (nbytes,), "typestr": "|u1", "data": (ptr, False),
+                                         "version": 3, "strides": None}
+
+    def __del__(self):
+        try:
+            L.lib().dsa_ipc_free(ctypes.c_void_p(self.ptr))
+        except Exception:
+            pass
+
+
+def _ipc_alloc_impl(nbytes):
+    ptr = ctypes.c_void_p()
+    handle = ctypes.create_string_buffer(64)
+    L.call("dsa_ipc_alloc", int(nbytes), ctypes.byref(ptr), handle)
+    buf = torch.as_tensor(_IpcBuffer(ptr.value, int(nbytes)), device=torch.device("cuda", torch.cuda.current_device()))
+    h = torch.frombuffer(bytearray(handle.raw), dtype=torch.uint8).clone()
+    return [buf, h]
+
+
+def _ipc_open_impl(handle):
+    _check(handle.device.type == "cpu" and handle.numel() == 64, "handle must be a 64-byte CPU tensor")
+    ptr = ctypes.c_void_p()
+    L.call("dsa_ipc_open", bytes(handle.to(torch.uint8).numpy().tobytes()), ctypes.byref(ptr))
+    return int(ptr.value)
+
+
+def _ipc_flag_set_impl(flag_ptr, which, seq):
+    L.call("dsa_ipc_flag_set", int(flag_ptr), int(which), int(seq),
+           _stream(torch.device("cuda", torch.cuda.current_device())))
+
+
+def _ipc_slot_wait_impl(flag_ptrs, tp, min_seq):
+    dev = torch.device("cuda", torch.cuda.current_device())
+    L.call("dsa_ipc_slot_wait", _u64_array(flag_ptrs, tp), int(tp), int(min_seq), P2P_TIMEOUT_NS,
+           _vp(p2p_error_flag(dev)), _stream(dev))
+
+
+# ------------------------------------------------------ torch registration
+_lib_def = torch.library.Library(NAMESPACE, "DEF")
+_SCHEMAS = {
+    "sm70_sparse_mla_decode": ("(Tensor! o, Tensor! lse, Tensor q, Tensor kv_cache, Tensor idx, "
+                               "Tensor block_table, Tensor seq_lens, float scale) -> ()",
+                               _sparse_mla_decode_impl, "CUDA"),
+    "sm70_indexer_logits": ("(Tensor! score, Tensor q, Tensor k_cache, Tensor weights, Tensor block_table, "
+                            "Tensor seq_lens, Tensor!? hist) -> ()", _indexer_logits_impl, "CUDA"),
+    "sm70_indexer_logits_packed": ("(Tensor! score, Tensor q_packed, Tensor k_cache, Tensor weights, "
+                                   "Tensor block_table, Tensor seq_lens) -> ()",
+                                   _indexer_logits_packed_impl, "CUDA"),
+    "sm70_decode_topk": ("(Tensor! idx, Tensor score, Tensor seq_lens, Tensor hist, int k) -> ()",
+                         _decode_topk_impl, "CUDA"),
+    "persistent_topk": ("(Tensor score, Tensor lengths, Tensor! output, Tensor workspace, int k, "
+                        "int max_seq_len) -> ()", _persistent_topk_impl, "CUDA"),
+    "sm70_indexer_k_store": ("(Tensor! kv_cache, Tensor k, Tensor slot_mapping) -> ()",
+                             _indexer_k_store_impl, "CUDA"),
+    "sm70_indexer_shard_merge": ("(Tensor! out, Tensor allf, Tensor dst_rows, int dst_base, int topk) -> ()",
+                                 _shard_merge_impl, "CUDA"),
+    "sm70_indexer_shard_merge_p2p": ("(Tensor! out, Tensor data_ptrs, Tensor flag_ptrs, Tensor dst_rows, "
+                                     "int dst_base, int topk, int tp, int R, int seq, int slot_off) -> ()",
+                                     _shard_merge_p2p_impl, "CUDA"),
+    "sm70_ipc_alloc": ("(int bytes) -> Tensor[]", _ipc_alloc_impl, "CompositeExplicitAutograd"),
+    "sm70_ipc_open": ("(Tensor handle) -> int", _ipc_open_impl, "CPU"),
+    "sm70_ipc_flag_set": ("(int flag_ptr, int which, int seq) -> ()", _ipc_flag_set_impl,
+                          "CompositeExplicitAutograd"),
+    "sm70_ipc_slot_wait": ("(Tensor flag_ptrs, int tp, int min_seq) -> ()", _ipc_slot_wait_impl, "CPU"),
+}
+for _name, (_schema, _fn, _key) in _SCHEMAS.items():
+    _lib_def.define(_name + _schema)
+    _lib_def.impl(_name, _fn, _key)
+
+
+def _noop_fake(*args, **kwargs):
+    return None
+
+
+for _name in ("sm70_sparse_mla_decode", "sm70_indexer_logits", "sm70_indexer_logits_packed", "sm70_decode_topk",
+              "persistent_topk", "sm70_indexer_k_store", "sm70_indexer_shard_merge",
+              "sm70_indexer_shard_merge_p2p"):
+    torch.library.register_fake(f"{NAMESPACE}::{_name}")(_noop_fake)
+
+
+def _op(name):
+    return getattr(getattr(torch.ops, NAMESPACE), name)
+
+
+# ---------------------------------------- reference-compatible wrappers
+def sm70_sparse_mla_decode(o, lse, q, kv_cache, idx, block_table, seq_lens, scale: float) -> None:
+    """Sparse (top-k) MLA decode/prefill: writes o [B,H,512] (fp16/bf16) and lse [B,H] fp32."""
+    _op("sm70_sparse_mla_decode")(o, lse, q, kv_cache, idx, block_table, seq_lens, scale)
+
+
+def sm70_indexer_logits(score, q, k_cache, weights, block_table, seq_lens, hist=None) -> None:
+    """DSA indexer logits -> score [B, max_kv] fp32 (pad = -inf); optional fused
+    level-1 top-k histogram into a pre-zeroed int32 [B, 4096] `hist`."""
+    _op("sm70_indexer_logits")(score, q, k_cache, weights, block_table, seq_lens, hist)
+
+
+def sm70_indexer_logits_packed(score, q_packed, k_cache, weights, block_table, seq_lens) -> None:
+    """Indexer logits from the packed q layout [32, ceil(B/16), 8, 16, 16]."""
+    _op("sm70_indexer_logits_packed")(score, q_packed, k_cache, weights, block_table, seq_lens)
+
+
+def sm70_decode_topk(idx, score, seq_lens, hist, k: int) -> None:
+    """Exact top-k positions of score rows (p < seq_lens), ascending, -1 padded."""
+    _op("sm70_decode_topk")(idx, score, seq_lens, hist, k)
+
+
+def persistent_topk(score, lengths, output, workspace, k: int, max_seq_len: int) -> None:
+    """Per-row top-k with the upstream persistent_topk signature (workspace unused)."""
+    _op("persistent_topk")(score, lengths, output, workspace, k, max_seq_len)
+
+
+def sm70_indexer_k_store(kv_cache, k, slot_mapping) -> None:
+    """Indexer-K scatter into the paged cache (skips slot < 0)."""
+    _op("sm70_indexer_k_store")(kv_cache, k, slot_mapping)
+
+
+def sm70_indexer_shard_merge(out, allf, dst_rows, dst_base: int, topk: int) -> None:
+    _op("sm70_indexer_shard_merge")(out, allf, dst_rows, dst_base, topk)
+
+
+def sm70_indexer_shard_merge_p2p(out, data_ptrs, flag_ptrs, dst_rows, dst_base: int, topk: int, tp: int, R: int,
+                                 seq: int, slot_off: int) -> None:
+    _op("sm70_indexer_shard_merge_p2p")(out, data_ptrs, flag_ptrs, dst_rows, dst_base, topk, tp, R, seq, slot_off)
+
+
+def sm70_ipc_alloc(nbytes: int):
+    return _op("sm70_ipc_alloc")(nbytes)
+
+
+def sm70_ipc_open(handle) -> int:
+    return _op("sm70_ipc_open")(handle)
+
+
+def sm70_ipc_flag_set(flag_ptr: int, which: int, seq: int) -> None:
+    _op("sm70_ipc_flag_set")(flag_ptr, which, seq)
+
+
+def sm70_ipc_slot_wait(flag_ptrs, tp: int, min_seq: int) -> None:
+    _op("sm70_ipc_slot_wait")(flag_ptrs, tp, min_seq)

@@ -1,0 +1,238 @@
+/*
+ * dsa_b200.h — C ABI of the B200 (sm_100a) DSA sparse-attention hot path.
+ *
+ * Every entry point takes plain device pointers, sizes and a cudaStream_t
+ * (passed as void*), launches on that stream, never synchronises the host,
+ * and returns an int status (DSA_OK on success). On failure the message is
+ * available from dsa_last_error() (thread-local). Outputs are caller-owned
+ * out-parameters, as in the reference's torch ops (`Tensor!` arguments).
+ *
+ * Each function names the reference interface it replaces (paths relative
+ * to the bayley/glm5-on-v100 project):
+ *   dsa.cu   = csrc/attention/sm70_mla_decode.cu
+ *   ops.py   = reference/_sm70_ops.py
+ *   sai.py   = reference/sparse_attn_indexer.py
+ *   tmla.py  = reference/triton_mla.py
+ *   binds    = patches/glm5-v100-sm70-full.patch (csrc/torch_bindings.cpp hunk)
+ */
+#ifndef DSA_B200_H_
+#define DSA_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes --------------------------------------------------- */
+enum {
+  DSA_OK = 0,
+  DSA_ERR_INVALID = 1,     /* bad argument: shape, dtype, pointer, size   */
+  DSA_ERR_UNSUPPORTED = 2, /* valid but not implemented (e.g. head_dim)   */
+  DSA_ERR_TIMEOUT = 3,     /* a bounded device wait expired (P2P flags)   */
+  DSA_ERR_CUDA = 4,        /* a CUDA runtime call failed                  */
+  DSA_ERR_WORKSPACE = 5    /* caller workspace too small                  */
+};
+
+/* ---- element / cache formats --------------------------------------- */
+enum {
+  DSA_F16 = 0,  /* IEEE half                                             */
+  DSA_BF16 = 1, /* bfloat16                                              */
+  DSA_F32 = 2,  /* float                                                 */
+  /* fp8_ds_mla latent row, 656 B: 512 e4m3 | 4 x f32 tile scale | 64 f16
+   * rope (dsa.cu:74-100). Used only as a latent-cache format.           */
+  DSA_FP8_DS_MLA = 3,
+  /* fp8 indexer-K row, 132 B: 128 e4m3 | f32 per-token scale
+   * (dsa.cu:102-115). Used only as an indexer-cache format.             */
+  DSA_FP8_IDXK = 4
+};
+
+/* Thread-local text of the last failure ("" when none). */
+const char* dsa_last_error(void);
+/* ABI version: (major << 16) | minor. */
+int dsa_version(void);
+
+/* =====================================================================
+ * Sparse MLA decode / prefill attention.
+ * Replaces sm70_sparse_mla_decode (dsa.cu:2457-2616; schema binds
+ * "sm70_sparse_mla_decode(Tensor! o, Tensor! lse, Tensor q, Tensor kv_cache,
+ * Tensor idx, Tensor block_table, Tensor seq_lens, float scale) -> ()";
+ * Python wrapper ops.py:1848-1866; callers tmla.py:292-301, :476-485).
+ *
+ *   o[b,h,:512]  = sum_j softmax_j(scale * q[b,h,:] . kv_j[:576]) kv_j[:512]
+ *   lse[b,h]     = log-sum-exp of the scaled scores (-inf when no j is valid)
+ * over j in idx[b, 0:topk] with 0 <= idx < seq_lens[b]; the logical position
+ * p resolves to cache row block_table[b, p / page] * page + p % page. A row
+ * outside [0, n_kv_rows) reads as zeros (still counted), as in dsa.cu:976-981.
+ *
+ * q      [B, n_head, 576]  f16 or bf16, contiguous
+ * kv     [n_kv_rows / page, page, 576] f16/bf16, or [.., page, 656] u8
+ *        (kv_format DSA_FP8_DS_MLA)
+ * idx    int32, row stride idx_stride (elements)
+ * block_table int32 [B, max_blocks], row stride bt_stride
+ * seq_lens int32 [B]
+ * o      [B, n_head, 512] f16 or bf16 (o_dtype), contiguous
+ * lse    [B, n_head] f32
+ * workspace: device scratch of at least
+ *   dsa_sparse_mla_decode_workspace_bytes(B, n_head, topk) bytes
+ *   (may be NULL when that size is 0).
+ * ===================================================================== */
+size_t dsa_sparse_mla_decode_workspace_bytes(int B, int n_head, int topk);
+
+int dsa_sparse_mla_decode(void* o, int o_dtype, float* lse, const void* q,
+                          int q_dtype, const void* kv_cache, int kv_format,
+                          int64_t n_kv_rows, int page_size,
+                          const int32_t* idx, int64_t idx_stride,
+                          const int32_t* block_table, int64_t bt_stride,
+                          int max_blocks, const int32_t* seq_lens, int B,
+                          int n_head, int topk, double scale,
+                          void* workspace, size_t workspace_bytes,
+                          void* stream);
+
+/* =====================================================================
+ * Lightning-indexer logits.
+ * Replaces sm70_indexer_logits (dsa.cu:2626-2764; schema binds
+ * "sm70_indexer_logits(Tensor! score, Tensor q, Tensor k_cache,
+ * Tensor weights, Tensor block_table, Tensor seq_lens, Tensor!? hist)";
+ * wrapper ops.py:1880-1896; callers sai.py:605-613, :622-629, :146-151).
+ *
+ *   score[b,p] = sum_h w[b,h] * relu(q[b,h,:] . k_p)   for p < seq_lens[b]
+ *   score[b,p] = -inf                                 for seq_lens[b] <= p < max_kv
+ * k_p is cache row block_table[b, p/page]*page + p%page (zeros when the row
+ * is outside [0, n_kv_rows)). page_size must be a power of two.
+ *
+ * q        [B, n_ihead, 128] f16 or bf16, contiguous (n_ihead 1..64)
+ * weights  [B, n_ihead] f16, bf16 or f32, contiguous
+ * k_cache  [.., page, 128] f16/bf16 (k_format) or [.., page, 132] u8
+ *          (DSA_FP8_IDXK)
+ * score    f32 [B, max_kv], row stride score_stride
+ * hist     optional (NULL) int32 [B, 4096], pre-zeroed by the caller: each
+ *          valid score adds 1 to bin (monotone32(score) >> 20), the level-1
+ *          histogram dsa_decode_topk consumes (dsa.cu:315-319).
+ * ===================================================================== */
+int dsa_indexer_logits(float* score, int64_t score_stride, int max_kv,
+                       const void* q, int q_dtype, const void* k_cache,
+                       int k_format, int64_t n_kv_rows, int page_size,
+                       const void* weights, int w_dtype,
+                       const int32_t* block_table, int64_t bt_stride,
+                       int max_blocks, const int32_t* seq_lens, int B,
+                       int n_ihead, int32_t* hist, void* stream);
+
+/* Packed-Q variant. Replaces sm70_indexer_logits_packed (dsa.cu:2771-2836;
+ * schema binds "sm70_indexer_logits_packed(Tensor! score, Tensor q_packed,
+ * ...)"; wrapper ops.py:1899-1915; packing sai.py:131-148). q_packed is
+ * [32, ceil(B/16), 8, 16, 16] f16/bf16: element (h, t, c, r, d) holds
+ * q[16t + r, h, 16c + d] (zero rows past B). Same scores as
+ * dsa_indexer_logits on the unpacked q. */
+int dsa_indexer_logits_packed(float* score, int64_t score_stride, int max_kv,
+                              const void* q_packed, int q_dtype,
+                              const void* k_cache, int k_format,
+                              int64_t n_kv_rows, int page_size,
+                              const void* weights, int w_dtype,
+                              const int32_t* block_table, int64_t bt_stride,
+                              int max_blocks, const int32_t* seq_lens, int B,
+                              void* stream);
+
+/* =====================================================================
+ * Top-k selection over score rows.
+ * dsa_decode_topk replaces sm70_decode_topk (dsa.cu:2844-2905; schema binds
+ * "sm70_decode_topk(Tensor! idx, Tensor score, Tensor seq_lens, Tensor hist,
+ * int k)"; wrapper ops.py:1918-1928; caller sai.py:614-620).
+ * dsa_topk_rows replaces the upstream persistent_topk op the SM70 indexer
+ * calls (sai.py:632-639, :841-848, :873-880; vLLM fork v1.2.1, not vendored).
+ *
+ * idx[b, 0:K] = positions of the K largest score[b, p] over p < len[b],
+ * exact on the 32-bit keys, ties broken towards the LOWER position, written
+ * in ASCENDING position order and padded with -1 when len[b] < K.
+ * hist (optional for dsa_decode_topk): the level-1 histogram built by
+ * dsa_indexer_logits for the same rows; NULL recomputes it.
+ * score  f32, row stride score_stride; lens int32 [B]; idx int32, row
+ * stride idx_stride. K <= 4096. Reads only p < min(len[b], max_kv).
+ * ===================================================================== */
+int dsa_decode_topk(int32_t* idx, int64_t idx_stride, const float* score,
+                    int64_t score_stride, int max_kv, const int32_t* lens,
+                    const int32_t* hist, int B, int K, void* stream);
+
+int dsa_topk_rows(int32_t* idx, int64_t idx_stride, const float* score,
+                  int64_t score_stride, int max_kv, const int32_t* lens,
+                  int B, int K, void* stream);
+
+/* =====================================================================
+ * Indexer-K cache scatter.
+ * Replaces sm70_indexer_k_store (dsa.cu:2910-2939, kernels :662-706; schema
+ * binds "sm70_indexer_k_store(Tensor! kv_cache, Tensor k, Tensor
+ * slot_mapping)"; wrapper ops.py:1944-1951; caller sai.py:552-555).
+ *
+ * For t < n_tok with 0 <= slot[t] < n_rows: cache row slot[t] = k[t].
+ * cache_format DSA_F16 / DSA_BF16: plain copy of head_dim elements (k is
+ * converted when its dtype differs). DSA_FP8_IDXK (head_dim 128): 128 e4m3
+ * (round-to-nearest-even, saturating) of k/scale then the f32 scale
+ * max(amax/448, FLT_MIN). Rows with slot < 0 or >= n_rows are skipped.
+ * k [n_tok, head_dim] f16/bf16 contiguous; slot int32 [n_tok].
+ * ===================================================================== */
+int dsa_indexer_k_store(void* kv_cache, int cache_format, int64_t n_rows,
+                        const void* k, int k_dtype, int head_dim,
+                        const int32_t* slot, int n_tok, void* stream);
+
+/* =====================================================================
+ * Exact shard merge of key-sharded indexer top-k candidates.
+ * Replaces sm70_indexer_shard_merge (dsa.cu:2411-2434, kernel :2054-2182;
+ * schema binds "sm70_indexer_shard_merge(Tensor! out, Tensor allf, Tensor
+ * dst_rows, int dst_base, int topk)"; caller sai.py:987-1006) and the
+ * torch.topk epilogue it fuses (sai.py:1007-1030).
+ *
+ * allf f32 [tp, R, 2K]: per shard s and row r, K values then K int32
+ * positions bit-cast to f32 (-1 / -inf = empty). Candidate column
+ * col = s*K + c is keyed by (monotone32(val) << 32) | (tp*K - 1 - col), so
+ * keys are distinct and ties go to the lower column (torch.topk order on the
+ * [R, tp*K] layout). The top K keys' positions (-1 for -inf values) are
+ * written ASCENDING to out row (dst_base >= 0 ? dst_base + r : dst_rows[r]).
+ * tp in [1, 8], K in [1, 2048]; out row stride out_stride.
+ * ===================================================================== */
+int dsa_indexer_shard_merge(int32_t* out, int64_t out_stride,
+                            const float* allf, const int32_t* dst_rows,
+                            int dst_base, int tp, int R, int K, void* stream);
+
+/* Same merge reading each shard's [R, 2K] slab directly from peer memory
+ * (CUDA IPC / peer mappings: shard s at data_ptrs[s] + slot_off bytes),
+ * after a bounded acquire-wait until every peer's staged flag
+ * (flag_ptrs[s][0]) >= seq. Replaces sm70_indexer_shard_merge_p2p
+ * (dsa.cu:2394-2409, kernel :2214-2329; caller sai.py:942-947). The wait
+ * gives up after timeout_ns of device time and sets *err_flag (device int,
+ * caller-zeroed) to DSA_ERR_TIMEOUT; the merge output is then undefined.
+ * data_ptrs / flag_ptrs are HOST arrays of tp device addresses. */
+int dsa_indexer_shard_merge_p2p(int32_t* out, int64_t out_stride,
+                                const uint64_t* data_ptrs,
+                                const uint64_t* flag_ptrs,
+                                const int32_t* dst_rows, int dst_base, int K,
+                                int tp, int R, int seq, int64_t slot_off,
+                                int64_t timeout_ns, int32_t* err_flag,
+                                void* stream);
+
+/* =====================================================================
+ * CUDA IPC helpers for the P2P shard exchange.
+ * Replace sm70_ipc_alloc / sm70_ipc_open / sm70_ipc_flag_set /
+ * sm70_ipc_slot_wait (dsa.cu:2331-2392; schemas binds; caller
+ * sai.py:44-106, :893-952).
+ * ===================================================================== */
+/* cudaMalloc + zero + cudaIpcGetMemHandle; handle_out gets 64 bytes. */
+int dsa_ipc_alloc(int64_t bytes, void** dev_ptr, uint8_t* handle_out);
+int dsa_ipc_free(void* dev_ptr);
+/* cudaIpcOpenMemHandle(LazyEnablePeerAccess) of a 64-byte handle. */
+int dsa_ipc_open(const uint8_t* handle, void** dev_ptr);
+int dsa_ipc_close(void* dev_ptr);
+/* Stream-ordered release store: ((int*)flag_ptr)[which] = seq after a
+ * system-scope fence. */
+int dsa_ipc_flag_set(uint64_t flag_ptr, int which, int seq, void* stream);
+/* Stream-ordered bounded wait until every ((int*)flag_ptrs[s])[1] >=
+ * min_seq (s < tp). On expiry (timeout_ns of device time) sets *err_flag
+ * to DSA_ERR_TIMEOUT and returns on the device; the host reads err_flag. */
+int dsa_ipc_slot_wait(const uint64_t* flag_ptrs, int tp, int min_seq,
+                      int64_t timeout_ns, int32_t* err_flag, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DSA_B200_H_ */

@@ -1,0 +1,442 @@
+"""GPU parity: every kernel of the DSA path against the CPU oracle (and the
+reference-generated golden fixtures) on identical seeded inputs, called through
+the C ABI via the torch-op wrappers.
+
+Tolerances: attention outputs within 2e-3 relative error per (row, head)
+(||o - o_ref||_2 / ||o_ref||_2, fp16/bf16 out, fp32 accumulate) and lse within
+2e-3 absolute; indexer scores within 1e-4 of the row's max |score| (inputs are
+exactly representable, accumulation is fp32); integer and byte outputs
+(top-k positions, cache rows, histograms, merges) bit-exact.
+"""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+import cases
+from oracle import dsa_oracle as O
+
+pytestmark = pytest.mark.gpu
+GOLD = os.path.join(os.path.dirname(__file__), "golden")
+DEV = "cuda"
+ATTN_RTOL = 2e-3
+
+
+def to_dev(a, dtype=None):
+    t = torch.from_numpy(np.ascontiguousarray(a))
+    if dtype is not None:
+        t = t.to(dtype)
+    return t.to(DEV)
+
+
+def kv_tensor(kv_f32, page, fmt):
+    """(device cache tensor, dequantised rows the oracle should see)."""
+    nb = kv_f32.shape[0] // page
+    if fmt == "fp8":
+        rows = O.dsmla_encode_rows(kv_f32)
+        return to_dev(rows.reshape(nb, page, 656)), O.dsmla_decode_rows(rows)
+    if fmt == "f16":
+        return to_dev(kv_f32.reshape(nb, page, 576), torch.float16), kv_f32.astype(np.float16).astype(np.float64)
+    t = torch.from_numpy(kv_f32.reshape(nb, page, 576)).to(torch.bfloat16)
+    return t.to(DEV), t.float().numpy().reshape(-1, 576).astype(np.float64)
+
+
+def run_decode(dsa, c, fmt="fp8", q_dtype=torch.bfloat16, o_dtype=torch.bfloat16, scale=1.0 / np.sqrt(192.0)):
+    kv_t, kv_ref = kv_tensor(c["kv"], c["page"], fmt)
+    q = to_dev(c["q"], q_dtype)
+    B, H = c["q"].shape[:2]
+    o = torch.full((B, H, 512), float("nan"), dtype=o_dtype, device=DEV)
+    lse = torch.full((B, H), float("nan"), dtype=torch.float32, device=DEV)
+    dsa.sm70_sparse_mla_decode(o, lse, q, kv_t, to_dev(c["idx"]), to_dev(c["block_table"]), to_dev(c["seq_lens"]),
+                               scale)
+    torch.cuda.synchronize()
+    o_ref, lse_ref = O.sparse_mla_decode(q.float().cpu().numpy(), kv_ref, c["idx"], c["block_table"], c["seq_lens"],
+                                         c["page"], scale)
+    return o.float().cpu().numpy(), lse.cpu().numpy(), o_ref, lse_ref
+
+
+def random_dsmla_cache(nb, page, seed):
+    """A device fp8_ds_mla cache of random valid rows, built on the GPU
+    (uniform e4m3 codes except NaN, scales in [0.5, 1.5)/448, N(0,1) rope)."""
+    g = torch.Generator(device=DEV).manual_seed(seed)
+    kv = torch.randint(0, 256, (nb, page, 656), dtype=torch.uint8, device=DEV, generator=g)
+    codes = kv[..., :512]
+    codes[(codes & 0x7F) == 0x7F] = 0x7E
+    sc = (torch.rand(nb, page, 4, device=DEV, generator=g) + 0.5) / 448.0
+    kv[..., 512:528] = sc.contiguous().view(torch.uint8).view(nb, page, 16)
+    rope = torch.randn(nb, page, 64, device=DEV, generator=g).to(torch.float16)
+    kv[..., 528:656] = rope.view(torch.uint8).view(nb, page, 128)
+    return kv
+
+
+def assert_attn_close(o, lse, o_ref, lse_ref, rtol=ATTN_RTOL):
+    assert np.isfinite(o).all()
+    empty = np.isneginf(lse_ref)
+    np.testing.assert_array_equal(np.isneginf(lse), empty)
+    assert np.all(o[empty] == 0)
+    num = np.linalg.norm(o - o_ref, axis=-1)
+    den = np.linalg.norm(o_ref, axis=-1)
+    rel = np.where(empty, 0.0, num / np.maximum(den, 1e-30))
+    assert rel.max() <= rtol, f"max per-row relative error {rel.max():.3e}"
+    np.testing.assert_allclose(lse[~empty], lse_ref[~empty], atol=2e-3, rtol=0)
+
+
+# ---------------------------------------------------------- sparse decode
+@pytest.mark.parametrize("name", ["config1", "ragged"])
+def test_decode_matches_reference_golden(dsa, name):
+    f = np.load(os.path.join(GOLD, f"mqa_decode_{name}.npz"))
+    c = cases.decode_case(int(f["seed"]), int(f["B"]), int(f["H"]), int(f["page"]), f["seq_lens"], int(f["topk"]),
+                          int(f["bps"]))
+    o, lse, o_ref, lse_ref = run_decode(dsa, c, "f16", torch.float16, torch.float16, float(f["scale"]))
+    assert_attn_close(o, lse, o_ref, lse_ref)
+    # and directly against the reference's own torch output
+    assert_attn_close(o, lse, f["o"].astype(np.float64), f["lse"].astype(np.float64))
+
+
+@pytest.mark.parametrize("fmt", ["fp8", "f16", "bf16"])
+@pytest.mark.parametrize("q_dtype,o_dtype", [(torch.bfloat16, torch.bfloat16), (torch.float16, torch.float16),
+                                             (torch.bfloat16, torch.float16)])
+def test_decode_formats(dsa, fmt, q_dtype, o_dtype):
+    c = cases.decode_case(21, B=4, H=64, page=64, seq_lens=[2048, 5000, 100, 9000], topk=2048, bps=160)
+    assert_attn_close(*run_decode(dsa, c, fmt, q_dtype, o_dtype))
+
+
+@pytest.mark.parametrize("B,H,topk", [(1, 8, 2048), (2, 16, 512), (3, 128, 256), (6, 72, 64), (200, 64, 96),
+                                      (64, 64, 2048)])
+def test_decode_shapes_and_splits(dsa, B, H, topk):
+    rng = np.random.default_rng(B * 1000 + H)
+    seq = rng.integers(1, 6000, size=B)
+    c = cases.decode_case(31 + B, B=B, H=H, page=64, seq_lens=seq, topk=topk, bps=94)
+    assert_attn_close(*run_decode(dsa, c, "fp8"))
+
+
+def test_decode_invalid_entries_and_empty_rows(dsa):
+    c = cases.decode_case(41, B=6, H=64, page=16, seq_lens=[300, 300, 0, 50, 300, 300], topk=128, bps=20)
+    idx = c["idx"]
+    idx[0, ::3] = -1                       # unused slots
+    idx[1, 5:40] = 299                     # duplicates count separately
+    idx[3, :] = np.arange(128) - 40        # negatives and >= seq_len mixed
+    idx[4, :] = -1                         # empty row -> o = 0, lse = -inf
+    c["block_table"][5, 2] = 10 ** 6       # resolves past the cache: zero row, still counted
+    c["block_table"][5, 3] = -7            # negative block id: zero row, still counted
+    o, lse, o_ref, lse_ref = run_decode(dsa, c, "fp8")
+    assert np.isneginf(lse[2]).all() and np.isneginf(lse[4]).all()
+    assert_attn_close(o, lse, o_ref, lse_ref)
+
+
+def test_decode_topk_zero(dsa):
+    B, H = 2, 64
+    q = torch.randn(B, H, 576, device=DEV, dtype=torch.bfloat16)
+    kv = torch.zeros(4, 64, 656, dtype=torch.uint8, device=DEV)
+    o = torch.full((B, H, 512), 7.0, dtype=torch.bfloat16, device=DEV)
+    lse = torch.zeros(B, H, device=DEV)
+    dsa.sm70_sparse_mla_decode(o, lse, q, kv, torch.zeros(B, 0, dtype=torch.int32, device=DEV),
+                               torch.zeros(B, 4, dtype=torch.int32, device=DEV),
+                               torch.full((B,), 100, dtype=torch.int32, device=DEV), 0.1)
+    torch.cuda.synchronize()
+    assert (o == 0).all() and torch.isneginf(lse).all()
+
+
+def test_decode_mtp_rows_and_sparse_equals_dense(dsa):
+    """Spec-as-decode: two query rows per sequence (tmla.py:261-279); with
+    seq_len <= topk the sparse op equals dense attention (INTEGRATION.md:124-128)."""
+    rng = np.random.default_rng(51)
+    n_req, next_n, H, page, topk = 3, 2, 64, 64, 2048
+    seq_req = np.array([700, 2048, 1500])
+    seq = (seq_req[:, None] - (next_n - 1) + np.arange(next_n)).reshape(-1).astype(np.int32)
+    c = cases.decode_case(52, B=n_req * next_n, H=H, page=page, seq_lens=seq, topk=topk, bps=32)
+    c["block_table"] = np.repeat(c["block_table"][::next_n], next_n, axis=0)  # rows of a request share blocks
+    c["idx"] = np.stack([np.where(np.arange(topk) < s, np.arange(topk), -1) for s in seq]).astype(np.int32)
+    o, lse, o_ref, lse_ref = run_decode(dsa, c, "f16", torch.float16, torch.float16)
+    assert_attn_close(o, lse, o_ref, lse_ref)
+
+
+def test_decode_full_size_sampled_rows(dsa):
+    """BASELINE config 2 at 128k context: B=64, H=64, topk=2048, fp8 cache."""
+    B, H, S, page, topk = 64, 64, 131072, 64, 2048
+    rng = np.random.default_rng(61)
+    nb = B * (S // page)
+    kv = random_dsmla_cache(nb, page, seed=61)
+    bt = rng.permutation(nb).reshape(B, S // page).astype(np.int32)
+    idx = np.stack([np.sort(rng.choice(S, topk, replace=False)) for _ in range(B)]).astype(np.int32)
+    seq = np.full(B, S, np.int32)
+    q = rng.standard_normal((B, H, 576)).astype(np.float32)
+    qt = to_dev(q, torch.bfloat16)
+    o = torch.empty(B, H, 512, dtype=torch.bfloat16, device=DEV)
+    lse = torch.empty(B, H, device=DEV)
+    scale = 1.0 / np.sqrt(192.0)
+    dsa.sm70_sparse_mla_decode(o, lse, qt, kv, to_dev(idx), to_dev(bt), to_dev(seq), scale)
+    torch.cuda.synchronize()
+    sample = [0, 17, 38, 63]
+    flat = kv.view(-1, 656)
+    for b in sample:
+        rows = bt[b][idx[b] // page].astype(np.int64) * page + idx[b] % page
+        kv_rows = O.dsmla_decode_rows(flat[torch.from_numpy(rows).to(DEV)].cpu().numpy())
+        local_bt = np.arange(topk // page + 1, dtype=np.int32)[None]
+        o_ref, lse_ref = O.sparse_mla_decode(qt[b:b + 1].float().cpu().numpy(),
+                                             np.concatenate([kv_rows, np.zeros((page, 576))]),
+                                             np.arange(topk, dtype=np.int32)[None], local_bt,
+                                             np.array([topk], np.int32), page, scale)
+        assert_attn_close(o[b:b + 1].float().cpu().numpy(), lse[b:b + 1].cpu().numpy(), o_ref, lse_ref)
+
+
+# ---------------------------------------------------------- indexer logits
+def idx_cache(k_rows_f32, page, fmt):
+    nb = k_rows_f32.shape[0] // page
+    if fmt == "fp8":
+        rows = O.idxk_encode_rows(k_rows_f32)
+        return to_dev(rows.reshape(nb, page, 132)), O.idxk_decode_rows(rows)
+    dt = torch.float16 if fmt == "f16" else torch.bfloat16
+    t = torch.from_numpy(k_rows_f32.reshape(nb, page, 128)).to(dt)
+    return t.to(DEV), t.float().numpy().reshape(-1, 128).astype(np.float64)
+
+
+def logits_case(seed, B, Hi, S, page, shared_bt=False, causal=False):
+    rng = np.random.default_rng(seed)
+    bps = (S + page - 1) // page
+    nb = (1 if shared_bt else B) * bps + 2
+    k = cases.f16_exact(rng.standard_normal((nb * page, 128)))
+    q = cases.f16_exact(rng.standard_normal((B, Hi, 128)))
+    w = cases.f16_exact(rng.standard_normal((B, Hi)) / np.sqrt(Hi))
+    if shared_bt:
+        bt = np.tile(rng.permutation(nb)[:bps], (B, 1)).astype(np.int32)
+    else:
+        bt = rng.permutation(nb)[:B * bps].reshape(B, bps).astype(np.int32)
+    if causal:
+        seq = (S - B + 1 + np.arange(B)).astype(np.int32)
+    else:
+        seq = rng.integers(1, S + 1, size=B).astype(np.int32)
+    return dict(k=k, q=q, w=w, bt=bt, seq=seq, page=page, max_kv=bps * page)
+
+
+def run_logits(dsa, c, fmt="f16", q_dtype=torch.float16, w_dtype=torch.float16, hist=False, packed=False):
+    kc, k_ref = idx_cache(c["k"], c["page"], fmt)
+    B = c["q"].shape[0]
+    q = to_dev(c["q"], q_dtype)
+    w = to_dev(c["w"], w_dtype)
+    score = torch.full((B, c["max_kv"]), float("nan"), device=DEV)
+    h = torch.zeros(B, 4096, dtype=torch.int32, device=DEV) if hist else None
+    if packed:
+        n16 = (B + 15) // 16 * 16
+        qp = torch.nn.functional.pad(q, (0, 0, 0, 0, 0, n16 - B))
+        qp = qp.view(n16 // 16, 16, 32, 8, 16).permute(2, 0, 3, 1, 4).contiguous()
+        dsa.sm70_indexer_logits_packed(score, qp, kc, w, to_dev(c["bt"]), to_dev(c["seq"]))
+    else:
+        dsa.sm70_indexer_logits(score, q, kc, w, to_dev(c["bt"]), to_dev(c["seq"]), h)
+    torch.cuda.synchronize()
+    ref = O.indexer_logits(q.float().cpu().numpy(), k_ref, w.float().cpu().numpy(), c["bt"], c["seq"], c["page"],
+                           c["max_kv"])
+    return score.cpu().numpy(), ref, (h.cpu().numpy() if hist else None)
+
+
+def assert_scores_close(s, ref):
+    inf = np.isneginf(ref)
+    np.testing.assert_array_equal(np.isneginf(s), inf)
+    for b in range(s.shape[0]):
+        fin = ~inf[b]
+        if fin.any():
+            scale = max(np.abs(ref[b, fin]).max(), 1e-6)
+            assert np.abs(s[b, fin] - ref[b, fin]).max() <= 1e-4 * scale, b
+
+
+@pytest.mark.parametrize("fmt", ["f16", "bf16", "fp8"])
+@pytest.mark.parametrize("Hi", [8, 32, 64])
+def test_indexer_rows_kernel(dsa, fmt, Hi):
+    c = logits_case(100 + Hi, B=3, Hi=Hi, S=5000, page=64)
+    qd = torch.bfloat16 if fmt == "bf16" else torch.float16
+    s, ref, h = run_logits(dsa, c, fmt, qd, torch.float32, hist=True)
+    assert_scores_close(s, ref)
+    np.testing.assert_array_equal(h, O.level1_hist(s, c["seq"]))
+
+
+@pytest.mark.parametrize("fmt", ["f16", "bf16", "fp8"])
+def test_indexer_tiles_kernel_causal(dsa, fmt):
+    c = logits_case(200, B=150, Hi=32, S=3000, page=64, shared_bt=True, causal=True)
+    qd = torch.bfloat16 if fmt == "bf16" else torch.float16
+    s, ref, _ = run_logits(dsa, c, fmt, qd, torch.float16)
+    assert_scores_close(s, ref)
+
+
+def test_indexer_packed_equals_unpacked(dsa):
+    c = logits_case(300, B=70, Hi=32, S=1500, page=64, shared_bt=True, causal=True)
+    s1, ref, _ = run_logits(dsa, c, "f16")
+    s2, _, _ = run_logits(dsa, c, "f16", packed=True)
+    np.testing.assert_array_equal(s1, s2)
+    assert_scores_close(s2, ref)
+
+
+def test_indexer_q_bf16_with_fp16_cache(dsa):
+    c = logits_case(310, B=5, Hi=32, S=700, page=16)
+    s, ref, _ = run_logits(dsa, c, "f16", torch.bfloat16, torch.bfloat16)
+    assert_scores_close(s, ref)
+
+
+# ------------------------------------------------------------------- top-k
+@pytest.mark.parametrize("K", [1, 7, 512, 2048])
+def test_topk_rows_exact_with_ties(dsa, K):
+    rng = np.random.default_rng(K)
+    B, S = 9, 9000
+    score = (np.round(rng.standard_normal((B, S)) * 8) / 8).astype(np.float32)  # heavy ties
+    score[2, :] = 1.5                                                              # all tied
+    score[3, 100:] = -np.inf
+    lens = np.array([S, S - 1, S, S, K, K - 1 if K > 1 else 0, 0, 2 * K + 1, S // 3], np.int32)
+    out = torch.full((B, K), -7, dtype=torch.int32, device=DEV)
+    dsa.persistent_topk(to_dev(score), to_dev(lens.reshape(-1, 1)), out, torch.empty(0, device=DEV), K, S)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(out.cpu().numpy(), O.topk_rows(score, lens, K))
+
+
+def test_decode_topk_with_fused_histogram_end_to_end(dsa):
+    """indexer logits (+hist) -> decode top-k: exact on the kernel's own scores;
+    against fp64 logits the sets differ only inside the rounding tie band."""
+    c = logits_case(400, B=4, Hi=32, S=20000, page=64)
+    c["seq"] = np.array([20000, 15000, 2048, 1000], np.int32)
+    kc, k_ref = idx_cache(c["k"], c["page"], "f16")
+    B, K = 4, 2048
+    score = torch.empty(B, c["max_kv"], device=DEV)
+    hist = torch.zeros(B, 4096, dtype=torch.int32, device=DEV)
+    q, w = to_dev(c["q"], torch.float16), to_dev(c["w"], torch.float16)
+    dsa.sm70_indexer_logits(score, q, kc, w, to_dev(c["bt"]), to_dev(c["seq"]), hist)
+    idx = torch.empty(B, K, dtype=torch.int32, device=DEV)
+    dsa.sm70_decode_topk(idx, score, to_dev(c["seq"]), hist, K)
+    torch.cuda.synchronize()
+    s = score.cpu().numpy()
+    got = idx.cpu().numpy()
+    np.testing.assert_array_equal(got, O.topk_rows(s, c["seq"], K))
+    ref = O.indexer_logits(c["q"], k_ref, c["w"], c["bt"], c["seq"], c["page"], c["max_kv"])
+    exp = O.topk_rows(ref.astype(np.float32), c["seq"], K)
+    band = 4 * np.nanmax(np.where(np.isfinite(ref), np.abs(s - ref), 0)) + 1e-6
+    for b in range(B):
+        diff = set(got[b].tolist()) ^ set(exp[b].tolist())
+        if diff:
+            n = min(int(c["seq"][b]), c["max_kv"])
+            kth = np.sort(ref[b, :n])[::-1][K - 1]
+            assert all(abs(ref[b, p] - kth) <= band for p in diff), b
+
+
+def test_topk_long_decode_row(dsa):
+    rng = np.random.default_rng(77)
+    S, K = 180224, 2048
+    score = rng.standard_normal((2, S)).astype(np.float32)
+    lens = np.array([S, 100000], np.int32)
+    out = torch.empty(2, K, dtype=torch.int32, device=DEV)
+    dsa.persistent_topk(to_dev(score), to_dev(lens), out, torch.empty(0, device=DEV), K, S)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(out.cpu().numpy(), O.topk_rows(score, lens, K))
+
+
+# -------------------------------------------------------------- K scatter
+@pytest.mark.parametrize("k_dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("fmt", ["fp8", "f16", "bf16"])
+def test_indexer_k_store_bit_exact(dsa, k_dtype, fmt):
+    rng = np.random.default_rng(5)
+    n_tok, n_rows = 300, 1000
+    k32 = (rng.standard_normal((n_tok, 128)) * np.exp2(rng.integers(-6, 6, (n_tok, 1)))).astype(np.float32)
+    k32[3] = 0.0                      # all-zero row -> scale FLT_MIN
+    k32[4, 7] = 1e4                   # large outlier
+    kt = torch.from_numpy(k32).to(k_dtype)
+    kin = kt.float().numpy()
+    slot = rng.permutation(n_rows)[:n_tok].astype(np.int32)
+    slot[::17] = -1
+    slot[5] = n_rows + 3              # out of range: skipped
+    if fmt == "fp8":
+        cache = torch.zeros(n_rows // 10, 10, 132, dtype=torch.uint8, device=DEV)
+        base = np.zeros((n_rows, 132), np.uint8)
+    elif fmt == "f16":
+        cache = torch.zeros(n_rows // 10, 10, 128, dtype=torch.float16, device=DEV)
+        base = np.zeros((n_rows, 128), np.float16)
+    else:
+        cache = torch.zeros(n_rows // 10, 10, 128, dtype=torch.bfloat16, device=DEV)
+        base = np.zeros((n_rows, 128), np.uint16)  # bf16 bit patterns
+    dsa.sm70_indexer_k_store(cache, kt.to(DEV), to_dev(slot))
+    torch.cuda.synchronize()
+    exp = O.indexer_k_store(base, kin, slot, fmt)
+    got = cache.cpu().view(torch.uint8).numpy().reshape(n_rows, -1)
+    np.testing.assert_array_equal(got, exp.view(np.uint8).reshape(n_rows, -1))
+
+
+# ------------------------------------------------------------ shard merge
+def merge_payload(rng, tp, R, K, n_pos=10 ** 6):
+    vals = (np.round(rng.standard_normal((tp, R, K)) * 4) / 4).astype(np.float32)
+    vals[0, 0, :K // 3] = -np.inf
+    if R > 1:
+        vals[:, 1, :] = -np.inf
+    pos = np.stack([rng.permutation(n_pos)[:tp * K].reshape(tp, K) for _ in range(R)], axis=1).astype(np.int32)
+    pos[vals == -np.inf] = -1
+    return np.concatenate([vals, pos.view(np.float32)], axis=2)
+
+
+@pytest.mark.parametrize("tp,K", [(1, 64), (2, 2048), (3, 100), (4, 2048), (8, 2048), (8, 1)])
+def test_shard_merge_exact(dsa, tp, K):
+    rng = np.random.default_rng(tp * 31 + K)
+    R = 5
+    allf = merge_payload(rng, tp, R, K)
+    out = torch.full((R + 3, K), -9, dtype=torch.int32, device=DEV)
+    dsa.sm70_indexer_shard_merge(out, to_dev(allf), torch.empty(0, dtype=torch.int32, device=DEV), 2, K)
+    dst = np.array([7, 0, 3, 1, 6], np.int32)
+    out2 = torch.full((R + 3, K), -9, dtype=torch.int32, device=DEV)
+    dsa.sm70_indexer_shard_merge(out2, to_dev(allf), to_dev(dst), -1, K)
+    torch.cuda.synchronize()
+    exp = O.shard_merge(allf, K)
+    np.testing.assert_array_equal(out.cpu().numpy()[2:2 + R], exp)
+    np.testing.assert_array_equal(out2.cpu().numpy()[dst], exp)
+
+
+def test_shard_merge_reference_fixture(dsa):
+    f = np.load(os.path.join(GOLD, "shard_merge.npz"))
+    allf, K = f["allf"], int(f["K"])
+    R = allf.shape[1]
+    out = torch.empty(R, K, dtype=torch.int32, device=DEV)
+    dsa.sm70_indexer_shard_merge(out, to_dev(allf), torch.empty(0, dtype=torch.int32, device=DEV), 0, K)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(out.cpu().numpy(), O.shard_merge(allf, K))
+
+
+def test_shard_merge_p2p_local_slots_and_timeout(dsa):
+    """The P2P merge over pointer arrays (two slabs on this GPU stand in for
+    peers), then a bounded wait on a flag nothing sets: the kernel returns,
+    reports TIMEOUT, and the context stays usable."""
+    rng = np.random.default_rng(9)
+    tp, R, K = 2, 4, 2048
+    allf = merge_payload(rng, tp, R, K)
+    slabs = [to_dev(allf[s]) for s in range(tp)]
+    flags = [torch.zeros(2, dtype=torch.int32, device=DEV) for _ in range(tp)]
+    for f in flags:
+        f[0] = 5
+    data_ptrs = torch.tensor([s.data_ptr() for s in slabs], dtype=torch.int64)
+    flag_ptrs = torch.tensor([f.data_ptr() for f in flags], dtype=torch.int64)
+    out = torch.empty(R, K, dtype=torch.int32, device=DEV)
+    dsa.sm70_indexer_shard_merge_p2p(out, data_ptrs, flag_ptrs, torch.empty(0, dtype=torch.int32, device=DEV), 0, K,
+                                     tp, R, 5, 0)
+    torch.cuda.synchronize()
+    dsa.ops.check_p2p_status(DEV)
+    np.testing.assert_array_equal(out.cpu().numpy(), O.shard_merge(allf, K))
+    # flag_set publishes, slot_wait sees it
+    dsa.sm70_ipc_flag_set(flags[0].data_ptr(), 1, 11)
+    dsa.sm70_ipc_flag_set(flags[1].data_ptr(), 1, 11)
+    dsa.sm70_ipc_slot_wait(flag_ptrs, tp, 11)
+    torch.cuda.synchronize()
+    dsa.ops.check_p2p_status(DEV)
+    # a wait that runs out: staged flag stays at 5 < 6
+    old = dsa.ops.P2P_TIMEOUT_NS
+    dsa.ops.P2P_TIMEOUT_NS = 50_000_000  # 50 ms
+    try:
+        dsa.sm70_indexer_shard_merge_p2p(out, data_ptrs, flag_ptrs, torch.empty(0, dtype=torch.int32, device=DEV),
+                                         0, K, tp, 1, 6, 0)
+        torch.cuda.synchronize()
+        with pytest.raises(RuntimeError, match="TIMEOUT"):
+            dsa.ops.check_p2p_status(DEV)
+    finally:
+        dsa.ops.P2P_TIMEOUT_NS = old
+    x = torch.ones(4, device=DEV) * 2
+    assert float(x.sum()) == 8.0
+
+
+def test_ipc_alloc_handle(dsa):
+    buf, handle = dsa.sm70_ipc_alloc(4096)
+    assert buf.is_cuda and buf.numel() == 4096 and handle.numel() == 64
+    assert int(buf.sum()) == 0
+    buf.fill_(3)
+    torch.cuda.synchronize()
+    assert int(buf.sum()) == 3 * 4096
