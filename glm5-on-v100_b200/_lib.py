@@ -39,6 +39,7 @@ _d = ctypes.c_double
 SIGNATURES = {
     "dsa_last_error": (ctypes.c_char_p, []),
     "dsa_version": (_i, []),
+    "dsa_device_error": (_i, [_i]),
     "dsa_sparse_mla_decode_workspace_bytes": (_sz, [_i, _i, _i]),
     "dsa_sparse_mla_decode": (_i, [_p, _i, _p, _p, _i, _p, _i, _i64, _i, _p, _i64, _p, _i64, _i, _p,
                                    _i, _i, _i, _d, _p, _sz, _p]),

@@ -17,9 +17,10 @@
 //   * With one slice per row the CTA normalises and writes o / lse directly;
 //     otherwise it writes an unnormalised partial (o, m, l) and a small merge
 //     kernel combines the slices.
+#include <algorithm>
 #include <cmath>
 
-#include "common.cuh"
+#include "sparse_mla.cuh"
 
 namespace dsa {
 namespace {
@@ -34,29 +35,10 @@ constexpr int PSTR = TN + 8;   // 80 B rows
 constexpr int SSTR = TN + 1;
 constexpr int DSMLA_ROW = 656;
 constexpr float kLn2 = 0.69314718055994530942f;
-constexpr float kLog2e = 1.44269504088896340736f;
 
 enum KvFmt { KV_F16 = 0, KV_BF16 = 1, KV_FP8 = 2 };
 
-struct DecodeParams {
-  const void* q;
-  const uint8_t* kv;
-  const int32_t* idx;
-  const int32_t* bt;
-  const int32_t* seq_lens;
-  void* o;
-  float* lse;
-  float* part_o;   // [B, n_head, n_splits, 512] when n_splits > 1
-  float* part_ml;  // [B, n_head, n_splits, 2]
-  int64_t n_kv_rows;
-  int64_t idx_stride;
-  int64_t bt_stride;
-  int page_size;
-  int max_blocks;
-  int B, n_head, topk, n_splits, span;
-  int q_bf16, o_bf16;
-  float scale_log2;  // softmax scale * log2(e)
-};
+using DecodeParams = SparseMlaArgs;
 
 constexpr size_t kSmemQ = (size_t)HT * QSTR * 2;
 constexpr size_t kSmemK = (size_t)TN * QSTR * 2;
@@ -461,11 +443,8 @@ int g_attr_status[kMaxDevices];
 int ensure_attrs(int dev) {
   if (dev < 0 || dev >= kMaxDevices) return DSA_OK;
   std::call_once(g_attr_once[dev], [dev] {
-    cudaError_t e = cudaFuncSetAttribute(sparse_mla_decode_kernel<KV_FP8>,
+    cudaError_t e = cudaFuncSetAttribute(sparse_mla_decode_kernel<KV_F16>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemDecode);
-    if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(sparse_mla_decode_kernel<KV_F16>,
-                               cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemDecode);
     if (e == cudaSuccess)
       e = cudaFuncSetAttribute(sparse_mla_decode_kernel<KV_BF16>,
                                cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemDecode);
@@ -484,10 +463,27 @@ int ensure_attrs(int dev) {
 
 using namespace dsa;
 
+namespace dsa {
+int launch_sparse_mla_merge(const SparseMlaArgs& a, cudaStream_t s) {
+  sparse_mla_merge_kernel<<<(unsigned)((int64_t)a.B * a.n_head), 128, 0, s>>>(a.part_o, a.part_ml, a.o, a.o_bf16,
+                                                                               a.lse, a.n_splits);
+  return check_launch("sparse_mla_merge_kernel");
+}
+}  // namespace dsa
+
+// Slice count of the kernel that serves kv_format (the workspace holds the
+// partial states of every slice).
+static int splits_for(int kv_format, int B, int n_head, int topk, int nsm) {
+  const int head_tiles = (n_head + HT - 1) / HT;
+  if (kv_format == DSA_FP8_DS_MLA) return tc_choose_splits(B, head_tiles, topk, nsm);
+  return choose_splits(B, head_tiles, topk, nsm);
+}
+
 extern "C" size_t dsa_sparse_mla_decode_workspace_bytes(int B, int n_head, int topk) {
   if (B <= 0 || n_head <= 0 || topk <= 0) return 0;
-  const int head_tiles = (n_head + HT - 1) / HT;
-  const int s = choose_splits(B, head_tiles, topk, sm_count(current_device()));
+  const int nsm = sm_count(current_device());
+  int s = 1;
+  for (int fmt : {DSA_FP8_DS_MLA, DSA_F16}) s = std::max(s, splits_for(fmt, B, n_head, topk, nsm));
   if (s <= 1) return 0;
   return (size_t)B * n_head * s * (DV + 2) * sizeof(float);
 }
@@ -527,8 +523,10 @@ extern "C" int dsa_sparse_mla_decode(void* o, int o_dtype, float* lse, const voi
   if (st != DSA_OK) return st;
 
   const int head_tiles = (n_head + HT - 1) / HT;
-  const int n_splits = choose_splits(B, head_tiles, topk, sm_count(dev));
-  const int ntiles = (topk + TN - 1) / TN;
+  const bool use_tc = kv_format == DSA_FP8_DS_MLA;
+  const int tile = use_tc ? kTcTileRows : TN;
+  const int n_splits = splits_for(kv_format, B, n_head, topk, sm_count(dev));
+  const int ntiles = (topk + tile - 1) / tile;
   const int per = n_splits > 0 ? (ntiles + n_splits - 1) / n_splits : ntiles;
 
   DecodeParams p{};
@@ -548,7 +546,7 @@ extern "C" int dsa_sparse_mla_decode(void* o, int o_dtype, float* lse, const voi
   p.n_head = n_head;
   p.topk = topk;
   p.n_splits = n_splits;
-  p.span = per * TN;
+  p.span = per * tile;
   p.q_bf16 = q_dtype == DSA_BF16;
   p.o_bf16 = o_dtype == DSA_BF16;
   p.scale_log2 = (float)(scale * 1.4426950408889634);
@@ -563,23 +561,16 @@ extern "C" int dsa_sparse_mla_decode(void* o, int o_dtype, float* lse, const voi
   }
   cudaStream_t s = as_stream(stream);
   const dim3 grid(B, head_tiles, n_splits);
-  switch (kv_format) {
-    case DSA_FP8_DS_MLA:
-      sparse_mla_decode_kernel<KV_FP8><<<grid, NTHR, kSmemDecode, s>>>(p);
-      break;
-    case DSA_BF16:
+  if (use_tc) {
+    st = launch_sparse_mla_tc(p, s);
+  } else {
+    if (kv_format == DSA_BF16)
       sparse_mla_decode_kernel<KV_BF16><<<grid, NTHR, kSmemDecode, s>>>(p);
-      break;
-    default:
+    else
       sparse_mla_decode_kernel<KV_F16><<<grid, NTHR, kSmemDecode, s>>>(p);
-      break;
+    st = check_launch("sparse_mla_decode_kernel");
   }
-  st = check_launch("sparse_mla_decode_kernel");
   if (st != DSA_OK) return st;
-  if (n_splits > 1) {
-    sparse_mla_merge_kernel<<<(unsigned)((int64_t)B * n_head), 128, 0, s>>>(
-        p.part_o, p.part_ml, o, p.o_bf16, lse, n_splits);
-    st = check_launch("sparse_mla_merge_kernel");
-  }
+  if (n_splits > 1) st = launch_sparse_mla_merge(p, s);
   return st;
 }

@@ -216,6 +216,8 @@ _ERR_FLAGS: dict = {}
 def p2p_error_flag(device) -> torch.Tensor:
     """Per-device int32 word the bounded P2P waits set to DSA_ERR_TIMEOUT."""
     device = torch.device(device)
+    if device.type == "cuda" and device.index is None:
+        device = torch.device("cuda", torch.cuda.current_device())
     t = _ERR_FLAGS.get(device)
     if t is None:
         t = torch.zeros(1, dtype=torch.int32, device=device)

@@ -52,6 +52,12 @@ enum {
 const char* dsa_last_error(void);
 /* ABI version: (major << 16) | minor. */
 int dsa_version(void);
+/* Sticky device-side status of the current device's tensor-core attention
+ * kernel: DSA_ERR_TIMEOUT after one of its bounded pipeline waits expired
+ * (the launch then returned without finishing its output), else DSA_OK.
+ * Synchronises with the device; reset != 0 clears it. A negative value is
+ * -DSA_ERR_CUDA. No counterpart in the reference, whose waits never expire. */
+int dsa_device_error(int reset);
 
 /* =====================================================================
  * Sparse MLA decode / prefill attention.

@@ -98,7 +98,7 @@ def test_decode_matches_reference_golden(dsa, name):
 @pytest.mark.parametrize("q_dtype,o_dtype", [(torch.bfloat16, torch.bfloat16), (torch.float16, torch.float16),
                                              (torch.bfloat16, torch.float16)])
 def test_decode_formats(dsa, fmt, q_dtype, o_dtype):
-    c = cases.decode_case(21, B=4, H=64, page=64, seq_lens=[2048, 5000, 100, 9000], topk=2048, bps=160)
+    c = cases.decode_case(21, B=4, H=64, page=64, seq_lens=[2048, 5000, 100, 9000], topk=2048, blocks_per_seq=160)
     assert_attn_close(*run_decode(dsa, c, fmt, q_dtype, o_dtype))
 
 
@@ -107,12 +107,26 @@ def test_decode_formats(dsa, fmt, q_dtype, o_dtype):
 def test_decode_shapes_and_splits(dsa, B, H, topk):
     rng = np.random.default_rng(B * 1000 + H)
     seq = rng.integers(1, 6000, size=B)
-    c = cases.decode_case(31 + B, B=B, H=H, page=64, seq_lens=seq, topk=topk, bps=94)
+    c = cases.decode_case(31 + B, B=B, H=H, page=64, seq_lens=seq, topk=topk, blocks_per_seq=94)
     assert_attn_close(*run_decode(dsa, c, "fp8"))
 
 
+@pytest.mark.parametrize("fmt", ["fp8", "f16"])
+def test_decode_growing_scores_rescale_path(dsa, fmt):
+    """Later tiles hold ever larger scores, so the running max grows by more
+    than 2^8 several times and the in-TMEM rescale of O is exercised."""
+    c = cases.decode_case(71, B=3, H=64, page=64, seq_lens=[4096, 4096, 3000], topk=2048, blocks_per_seq=64)
+    q = c["q"] * 4.0
+    c["q"] = cases.f16_exact(q)
+    grow = np.linspace(0.2, 3.0, c["kv"].shape[0]).astype(np.float32)[:, None]
+    for b in range(3):  # rows of each sequence grow with position
+        rows = c["block_table"][b][np.arange(4096) // 64].astype(np.int64) * 64 + np.arange(4096) % 64
+        c["kv"][rows] = cases.f16_exact(c["kv"][rows] * grow[:4096])
+    assert_attn_close(*run_decode(dsa, c, fmt, torch.bfloat16, torch.bfloat16, scale=0.5))
+
+
 def test_decode_invalid_entries_and_empty_rows(dsa):
-    c = cases.decode_case(41, B=6, H=64, page=16, seq_lens=[300, 300, 0, 50, 300, 300], topk=128, bps=20)
+    c = cases.decode_case(41, B=6, H=64, page=16, seq_lens=[300, 300, 0, 50, 300, 300], topk=128, blocks_per_seq=20)
     idx = c["idx"]
     idx[0, ::3] = -1                       # unused slots
     idx[1, 5:40] = 299                     # duplicates count separately
@@ -145,7 +159,7 @@ def test_decode_mtp_rows_and_sparse_equals_dense(dsa):
     n_req, next_n, H, page, topk = 3, 2, 64, 64, 2048
     seq_req = np.array([700, 2048, 1500])
     seq = (seq_req[:, None] - (next_n - 1) + np.arange(next_n)).reshape(-1).astype(np.int32)
-    c = cases.decode_case(52, B=n_req * next_n, H=H, page=page, seq_lens=seq, topk=topk, bps=32)
+    c = cases.decode_case(52, B=n_req * next_n, H=H, page=page, seq_lens=seq, topk=topk, blocks_per_seq=32)
     c["block_table"] = np.repeat(c["block_table"][::next_n], next_n, axis=0)  # rows of a request share blocks
     c["idx"] = np.stack([np.where(np.arange(topk) < s, np.arange(topk), -1) for s in seq]).astype(np.int32)
     o, lse, o_ref, lse_ref = run_decode(dsa, c, "f16", torch.float16, torch.float16)
