@@ -18,17 +18,18 @@
 // and MN-major A of PV; P^T (fp16) overwrites the tile's rope columns after QK
 // has consumed them, which keeps Q (72 KB) + tile (144 KB) within one SM.
 //
-// Warp roles (288 threads): warp 0 allocates TMEM and one lane issues all
-// MMAs; warps 1-8 are workers. As producers they gather the next tile's 656-B
-// rows with coalesced 16-byte loads into registers while the current tile is
-// in the tensor core, then dequantise (e4m3 x per-128 scale -> fp16) into the
-// swizzled tile. As softmax warps, each thread owns one latent row and 32
-// heads of S^T (tcgen05.ld), computes per-head tile maxima with warp
-// reductions, and keeps a lazily-updated running max: O^T is rescaled in TMEM
-// only when a head's max grows by more than 2^8, which keeps P <= 256 in fp16
-// while leaving o and lse exact. Row sums stay in registers per thread and
-// are reduced once at the end. Every wait is an mbarrier wait bounded by a
-// device-time limit that reports DSA_ERR_TIMEOUT instead of hanging.
+// Block of 8 warps (256 threads, so up to 255 registers per thread). Warp 0
+// allocates TMEM and its lane 0 issues the MMAs between block barriers. As
+// producers, all warps gather the next tile's 656-B rows with coalesced
+// 16-byte loads into registers while the current tile is in the tensor core,
+// then dequantise (e4m3 x per-128 scale -> fp16) into the swizzled tile. As
+// softmax warps, each thread owns one latent row and 32 heads of S^T
+// (tcgen05.ld), computes per-head tile maxima with warp reductions, and keeps
+// a lazily-updated running max: O^T is rescaled in TMEM only when a head's max
+// grows by more than 2^8, which keeps P <= 256 in fp16 while leaving o and lse
+// exact. Row sums accumulate per thread in spare TMEM columns and are reduced
+// once at the end. Every wait on the tensor core is an mbarrier wait bounded
+// by a device-time limit that reports DSA_ERR_TIMEOUT instead of hanging.
 #include "sparse_mla.cuh"
 #include "tc_common.cuh"
 
@@ -39,8 +40,8 @@ using namespace tc;
 
 constexpr int TM = kTcTileRows;   // 128 latent rows per tile (MMA M)
 constexpr int NH = 64;            // heads per CTA (MMA N)
-constexpr int NWORK = 8;          // worker warps
-constexpr int NTHREADS = 32 * (1 + NWORK);
+constexpr int NWORK = 8;          // warps; all of them produce tiles and run the softmax
+constexpr int NTHREADS = 32 * NWORK;
 constexpr int DV = 512;
 constexpr uint32_t KV_REGION = TM * 128;   // one 64-wide K block of the tile: 16 KB
 constexpr uint32_t Q_REGION = NH * 128;    // one 64-wide K block of Q: 8 KB
@@ -50,6 +51,7 @@ constexpr uint32_t SM_MISC = SM_Q + 9 * Q_REGION;
 constexpr uint32_t MISC_BYTES = 4096;
 constexpr uint32_t SMEM_BYTES = SM_MISC + MISC_BYTES + 1024;  // + alignment slack
 constexpr uint32_t S_COL = 256;            // S^T columns [256, 320); O^T tile j at [64j, 64j+64)
+constexpr uint32_t L_COL = 320;            // running row sums of P: columns [320, 384)
 constexpr uint32_t TMEM_COLS = 512;
 constexpr int ROW_BYTES = 656;
 constexpr float kLn2 = 0.69314718055994530942f;
@@ -67,7 +69,6 @@ __device__ __forceinline__ float unmono(uint32_t k) {
 
 struct Tile {
   uint4 nope[16];   // one 16-byte chunk of 16 rows (rotated row order)
-  float sc[16];     // the chunk's tile scale
   uint4 rope[4];    // 4 of the warp's 128 rope chunks
   int64_t my_row;   // lanes 0-15: byte offset of row (16*wid + lane), -1 if none
   int my_valid;     // lanes 0-15: position valid (counted in the softmax)
@@ -98,10 +99,10 @@ __device__ __forceinline__ void load_tile(Tile& T, const SparseMlaArgs& p, int b
     const int64_t off = __shfl_sync(0xffffffffu, T.my_row, rr);
     if (off >= 0) {
       T.nope[r] = ldg_nc16(p.kv + off + 16 * lane);
-      T.sc[r] = __ldg(reinterpret_cast<const float*>(p.kv + off + 512) + (lane >> 3));
+      // the tile scale is read again at store time: bring its line into L1 now
+      asm volatile("prefetch.global.L1 [%0];" ::"l"(p.kv + off + 512));
     } else {
       T.nope[r] = make_uint4(0, 0, 0, 0);
-      T.sc[r] = 0.f;
     }
   }
 #pragma unroll
@@ -138,16 +139,19 @@ __device__ __forceinline__ uint4 dequant8(uint32_t w0, uint32_t w1, float sc) {
   return o;
 }
 
-__device__ __forceinline__ void store_tile(const Tile& T, uint8_t* sm, uint8_t* valid, int wid, int lane) {
+__device__ __forceinline__ void store_tile(const Tile& T, const SparseMlaArgs& p, uint8_t* sm, uint8_t* valid,
+                                           int wid, int lane) {
 #pragma unroll
   for (int r = 0; r < 16; ++r) {
     const int rr = (r + (lane >> 2)) & 15;
     const int i = 16 * wid + rr;
     const int kb = lane >> 2;
     const int c0 = 2 * (lane & 3);
+    const int64_t off = __shfl_sync(0xffffffffu, T.my_row, rr);
+    const float sc = off >= 0 ? __ldg(reinterpret_cast<const float*>(p.kv + off + 512) + (lane >> 3)) : 0.f;
     uint8_t* region = sm + SM_KV + kb * KV_REGION;
-    *reinterpret_cast<uint4*>(region + sw128_off(i, c0)) = dequant8(T.nope[r].x, T.nope[r].y, T.sc[r]);
-    *reinterpret_cast<uint4*>(region + sw128_off(i, c0 + 1)) = dequant8(T.nope[r].z, T.nope[r].w, T.sc[r]);
+    *reinterpret_cast<uint4*>(region + sw128_off(i, c0)) = dequant8(T.nope[r].x, T.nope[r].y, sc);
+    *reinterpret_cast<uint4*>(region + sw128_off(i, c0 + 1)) = dequant8(T.nope[r].z, T.nope[r].w, sc);
   }
 #pragma unroll
   for (int m = 0; m < 4; ++m) {
@@ -157,25 +161,23 @@ __device__ __forceinline__ void store_tile(const Tile& T, uint8_t* sm, uint8_t* 
   if (lane < 16) valid[16 * wid + lane] = (uint8_t)T.my_valid;
 }
 
-__global__ void __maxnreg__(224) sparse_mla_decode_tc_kernel(const SparseMlaArgs p, int32_t* err) {
+__global__ void __launch_bounds__(NTHREADS, 1) sparse_mla_decode_tc_kernel(const SparseMlaArgs p, int32_t* err) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_base = smem_u32(smem_raw);
   const uint32_t base = (raw_base + 1023u) & ~1023u;
   uint8_t* sm = smem_raw + (base - raw_base);
   uint8_t* misc = sm + SM_MISC;
-  uint64_t* mbar = reinterpret_cast<uint64_t*>(misc);  // kv_full, s_full, p_full, kv_free, done
+  uint64_t* mbar = reinterpret_cast<uint64_t*>(misc);  // s_full, kv_free, done
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(misc + 64);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(misc + 68);
   int* any_rescale = reinterpret_cast<int*>(misc + 72);    // [2]
-  volatile int* decision = reinterpret_cast<volatile int*>(misc + 80);
   float* m_ref = reinterpret_cast<float*>(misc + 128);     // [64] running max (log2 units)
   float* alpha = m_ref + 64;                               // [64] this tile's rescale factors
   float* tmax = alpha + 64;                                // [2][4][32] per-warp tile maxima
   float* l_sum = tmax + 256;                               // [64]
   uint8_t* valid = reinterpret_cast<uint8_t*>(l_sum + 64); // [128]
 
-  const uint32_t mb_kv_full = smem_u32(&mbar[0]), mb_s_full = smem_u32(&mbar[1]);
-  const uint32_t mb_p_full = smem_u32(&mbar[2]), mb_kv_free = smem_u32(&mbar[3]), mb_done = smem_u32(&mbar[4]);
+  const uint32_t mb_s_full = smem_u32(&mbar[0]), mb_kv_free = smem_u32(&mbar[1]), mb_done = smem_u32(&mbar[2]);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int b = blockIdx.x;
@@ -185,12 +187,11 @@ __global__ void __maxnreg__(224) sparse_mla_decode_tc_kernel(const SparseMlaArgs
   const int lo = split * p.span;
   const int hi = min(lo + p.span, p.topk);
   const int ntiles = hi > lo ? (hi - lo + TM - 1) / TM : 0;
+  const bool issuer = threadIdx.x == 0;  // lane 0 of warp 0 issues every MMA
 
   if (warp == 0) {
     if (lane == 0) {
-      mbar_init(mb_kv_full, NWORK);
       mbar_init(mb_s_full, 1);
-      mbar_init(mb_p_full, NWORK);
       mbar_init(mb_kv_free, 1);
       mbar_init(mb_done, 1);
       mbar_init_fence();
@@ -198,10 +199,10 @@ __global__ void __maxnreg__(224) sparse_mla_decode_tc_kernel(const SparseMlaArgs
     }
     __syncwarp();
     tmem_alloc(smem_u32(tmem_slot), TMEM_COLS);
-  } else {
-    const int wt = threadIdx.x - 32;
+  }
+  {
     const int nheads = min(NH, p.n_head - h0);
-    for (int i = wt; i < NH * 72; i += 32 * NWORK) {
+    for (int i = threadIdx.x; i < NH * 72; i += NTHREADS) {
       const int h = i / 72, c = i % 72;
       uint4 v = make_uint4(0, 0, 0, 0);
       if (h < nheads) {
@@ -211,9 +212,9 @@ __global__ void __maxnreg__(224) sparse_mla_decode_tc_kernel(const SparseMlaArgs
       }
       *reinterpret_cast<uint4*>(sm + SM_Q + (c >> 3) * Q_REGION + sw128_off(h, c & 7)) = v;
     }
-    if (wt < NH) {
-      m_ref[wt] = -1e30f;
-      alpha[wt] = 1.f;
+    if (threadIdx.x < NH) {
+      m_ref[threadIdx.x] = -1e30f;
+      alpha[threadIdx.x] = 1.f;
     }
   }
   fence_proxy_async();
@@ -222,225 +223,241 @@ __global__ void __maxnreg__(224) sparse_mla_decode_tc_kernel(const SparseMlaArgs
   fence_after_sync();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 0) {
-    // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      bool issued = false;
-      for (int t = 0; t < ntiles; ++t) {
-        const uint32_t ph = t & 1;
-        if (!mbar_wait(mb_kv_full, ph, abort_flag, err, kWaitTimeoutNs)) break;
-        fence_after_sync();
+  const int wid = warp;              // producer: rows [16*wid, 16*wid+16) of a tile
+  const int sp = warp & 3;           // TMEM sub-partition: lanes [32*sp, 32*sp+32)
+  const int hh = warp >> 2;          // softmax head half: heads [32*hh, 32*hh+32)
+  const int row_s = 32 * sp + lane;  // the tile row this thread owns in the softmax
+  const uint32_t t_lane = (uint32_t)(32 * sp) << 16;
+  // The running row sums of P live in TMEM columns [L_COL + 32*hh, +32) of
+  // this thread's lane (one latent-row slot x 32 heads), not in registers.
+  Tile T;
+  if (ntiles > 0) load_tile(T, p, b, lo, hi, seq_len, wid, lane);
+  // Control flow is uniform across the block: after a timed-out wait (`ok`
+  // false, abort flag set) every warp still executes the same sequence of
+  // barriers, and every later wait returns at once, so no thread is left
+  // behind on a barrier.
+  bool ok = true;
+  bool issued = false;
+  for (int t = 0; t < ntiles; ++t) {
+    const uint32_t ph = t & 1;
+    // ---- producer: the previous tile's PV has drained the smem tile
+    if (t > 0) ok = ok && mbar_wait(mb_kv_free, ph ^ 1, abort_flag, err, kWaitTimeoutNs);
+    if (ok) store_tile(T, p, sm, valid, wid, lane);
+    fence_proxy_async();
+    __syncthreads();
+    // ---- S^T = KV . Q^T
+    if (issuer && ok) {
+      fence_after_sync();
 #pragma unroll 1
-        for (int kb = 0; kb < 9; ++kb) {
+      for (int kb = 0; kb < 9; ++kb) {
 #pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            const uint64_t a = sw128_desc(base + SM_KV + kb * KV_REGION + 32 * k, 16, 1024);
-            const uint64_t bq = sw128_desc(base + SM_Q + kb * Q_REGION + 32 * k, 16, 1024);
-            mma_f16_ss(tmem + S_COL, a, bq, IDESC_QK, (kb | k) != 0);
-          }
+        for (int k = 0; k < 4; ++k) {
+          const uint64_t a = sw128_desc(base + SM_KV + kb * KV_REGION + 32 * k, 16, 1024);
+          const uint64_t bq = sw128_desc(base + SM_Q + kb * Q_REGION + 32 * k, 16, 1024);
+          mma_f16_ss(tmem + S_COL, a, bq, IDESC_QK, (kb | k) != 0);
         }
-        mma_commit(mb_s_full);
-        issued = true;
-        if (!mbar_wait(mb_p_full, ph, abort_flag, err, kWaitTimeoutNs)) break;
-        fence_after_sync();
-#pragma unroll 1
-        for (int j = 0; j < 4; ++j) {
-#pragma unroll
-          for (int s = 0; s < TM / 16; ++s) {
-            const uint64_t a = sw128_desc(base + SM_KV + 2 * j * KV_REGION + 2048 * s, KV_REGION, 1024);
-            const uint64_t bp = sw128_desc(base + SM_KV + 8 * KV_REGION + 2048 * s, KV_REGION, 1024);
-            mma_f16_ss(tmem + 64 * j, a, bp, IDESC_PV, (t > 0 || s > 0) ? 1u : 0u);
-          }
-        }
-        mma_commit(mb_kv_free);
       }
-      if (issued) {  // every MMA of this CTA has completed before TMEM is released
-        mma_commit(mb_done);
-        mbar_wait(mb_done, 0, abort_flag, err, kWaitTimeoutNs);
-      }
+      mma_commit(mb_s_full);
+      issued = true;
     }
     __syncwarp();
-  } else {
-    // ------------------------------------------------------ producer/softmax
-    const int wid = warp - 1;          // 0..7: rows [16*wid, 16*wid+16) as producer
-    const int sp = warp & 3;           // TMEM sub-partition: rows/lanes [32*sp, 32*sp+32)
-    const int hh = wid >> 2;           // head half: heads [32*hh, 32*hh+32)
-    const int row_s = 32 * sp + lane;  // the tile row this thread owns in the softmax
-    const uint32_t t_lane = (uint32_t)(32 * sp) << 16;
-    float lsum[32];
-#pragma unroll
-    for (int h = 0; h < 32; ++h) lsum[h] = 0.f;
-    Tile T;
-    if (ntiles > 0) load_tile(T, p, b, lo, hi, seq_len, wid, lane);
-    // Control flow is uniform across the 8 worker warps: after a timed-out
-    // wait (`ok` false, abort flag set) every warp still executes the same
-    // sequence of named barriers, and every later wait returns at once, so no
-    // warp can be left behind on a barrier.
-    bool ok = true;
-    for (int t = 0; t < ntiles; ++t) {
-      const uint32_t ph = t & 1;
-      if (t > 0) ok = ok && mbar_wait(mb_kv_free, ph ^ 1, abort_flag, err, kWaitTimeoutNs);
-      if (ok) store_tile(T, sm, valid, wid, lane);
-      fence_proxy_async();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(mb_kv_full);
-      named_bar(3, 32 * NWORK);  // the tile's validity bytes are visible to every worker
-      if (ok && t + 1 < ntiles) load_tile(T, p, b, lo + (t + 1) * TM, hi, seq_len, wid, lane);
+    if (ok && t + 1 < ntiles) load_tile(T, p, b, lo + (t + 1) * TM, hi, seq_len, wid, lane);
 
-      ok = ok && mbar_wait(mb_s_full, ph, abort_flag, err, kWaitTimeoutNs);
-      fence_after_sync();
-      uint32_t sreg[32];
-      if (ok) {
-        tmem_ld32(tmem + t_lane + S_COL + 32 * hh, sreg);
-        tmem_wait_ld();
-      } else {
+    // ---- softmax
+    ok = ok && mbar_wait(mb_s_full, ph, abort_flag, err, kWaitTimeoutNs);
+    fence_after_sync();
+    uint32_t sreg[32];
+    if (ok) {
+      tmem_ld32(tmem + t_lane + S_COL + 32 * hh, sreg);
+      tmem_wait_ld();
+    } else {
 #pragma unroll
-        for (int h = 0; h < 32; ++h) sreg[h] = 0u;
-      }
-      const bool vrow = valid[row_s] != 0;
-      float v[32];
-      uint32_t my_max = 0;
+      for (int h = 0; h < 32; ++h) sreg[h] = 0u;
+    }
+    const bool vrow = valid[row_s] != 0;
+    uint32_t my_max = 0;
 #pragma unroll
-      for (int h = 0; h < 32; ++h) {
-        v[h] = vrow ? __uint_as_float(sreg[h]) * p.scale_log2 : -INFINITY;
-        const uint32_t wm = __reduce_max_sync(0xffffffffu, monotone32(v[h]));
-        if (lane == h) my_max = wm;
-      }
-      tmax[(hh * 4 + sp) * 32 + lane] = unmono(my_max);
-      named_bar(1 + hh, 128);
-      if (sp == 0) {
-        const int head = 32 * hh + lane;
-        float tm = tmax[(hh * 4) * 32 + lane];
+    for (int h = 0; h < 32; ++h) {
+      const float v = vrow ? __uint_as_float(sreg[h]) * p.scale_log2 : -INFINITY;
+      const uint32_t wm = __reduce_max_sync(0xffffffffu, monotone32(v));
+      if (lane == h) my_max = wm;
+    }
+    tmax[(hh * 4 + sp) * 32 + lane] = unmono(my_max);
+    named_bar(1 + hh, 128);
+    if (sp == 0) {
+      const int head = 32 * hh + lane;
+      float tm = tmax[(hh * 4) * 32 + lane];
 #pragma unroll
-        for (int s = 1; s < 4; ++s) tm = fmaxf(tm, tmax[(hh * 4 + s) * 32 + lane]);
-        const float m_old = m_ref[head];
-        float a = 1.f;
-        if (tm > m_old + kRescaleThreshold) {
-          a = exp2f(m_old - tm);
-          m_ref[head] = tm;
-        }
-        alpha[head] = a;
-        const unsigned any = __ballot_sync(0xffffffffu, a != 1.f);
-        if (lane == 0) any_rescale[hh] = any != 0u;
+      for (int s = 1; s < 4; ++s) tm = fmaxf(tm, tmax[(hh * 4 + s) * 32 + lane]);
+      const float m_old = m_ref[head];
+      float a = 1.f;
+      if (tm > m_old + kRescaleThreshold) {
+        a = exp2f(m_old - tm);
+        m_ref[head] = tm;
       }
-      named_bar(1 + hh, 128);
-      if (ok && any_rescale[hh] && t > 0) {  // O^T columns of this head half, rows of this sub-partition
+      alpha[head] = a;
+      const unsigned any = __ballot_sync(0xffffffffu, a != 1.f);
+      if (lane == 0) any_rescale[hh] = any != 0u;
+    }
+    named_bar(1 + hh, 128);
+    if (ok && any_rescale[hh] && t > 0) {  // O^T columns of this head half, lanes of this sub-partition
 #pragma unroll 1
-        for (int j = 0; j < 8; ++j) {  // 4 value tiles x 2 halves of 16 head columns
-          uint32_t o[16];
-          const uint32_t col = 64 * (j >> 1) + 32 * hh + 16 * (j & 1);
-          tmem_ld16(tmem + t_lane + col, o);
-          tmem_wait_ld();
+      for (int j = 0; j < 8; ++j) {  // 4 value tiles x 2 groups of 16 head columns
+        uint32_t o[16];
+        const uint32_t col = 64 * (j >> 1) + 32 * hh + 16 * (j & 1);
+        tmem_ld16(tmem + t_lane + col, o);
+        tmem_wait_ld();
 #pragma unroll
-          for (int h = 0; h < 16; ++h)
-            o[h] = __float_as_uint(__uint_as_float(o[h]) * alpha[32 * hh + 16 * (j & 1) + h]);
-          tmem_st16(tmem + t_lane + col, o);
-        }
-        tmem_wait_st();
+        for (int h = 0; h < 16; ++h)
+          o[h] = __float_as_uint(__uint_as_float(o[h]) * alpha[32 * hh + 16 * (j & 1) + h]);
+        tmem_st16(tmem + t_lane + col, o);
       }
-      uint8_t* preg = sm + SM_KV + 8 * KV_REGION;
+      tmem_wait_st();
+    }
+    // S^T is read from tensor memory a second time, in groups of 16 heads,
+    // instead of being kept in registers across the max reduction; the row
+    // sums are updated in TMEM alongside.
+    uint8_t* preg = sm + SM_KV + 8 * KV_REGION;
+#pragma unroll 1
+    for (int c2 = 0; c2 < 2; ++c2) {
+      const int hb = 32 * hh + 16 * c2;  // first head of this group
+      uint32_t s16[16], l16[16];
+      if (ok) {
+        tmem_ld16(tmem + t_lane + S_COL + hb, s16);
+        if (t > 0) tmem_ld16(tmem + t_lane + L_COL + hb, l16);
+        tmem_wait_ld();
+      }
+      if (!ok || t == 0) {
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {  // 8 heads per 16-byte chunk of the P^T row
+        for (int h = 0; h < 16; ++h) l16[h] = 0u;
+      }
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {  // 8 heads per 16-byte chunk of the P^T row
         uint32_t pk[4];
 #pragma unroll
         for (int e = 0; e < 8; e += 2) {
           const int h = 8 * c + e;
-          const float p0 = exp2f(v[h] - m_ref[32 * hh + h]);
-          const float p1 = exp2f(v[h + 1] - m_ref[32 * hh + h + 1]);
-          lsum[h] = lsum[h] * alpha[32 * hh + h] + p0;
-          lsum[h + 1] = lsum[h + 1] * alpha[32 * hh + h + 1] + p1;
+          const float v0 = vrow ? __uint_as_float(s16[h]) * p.scale_log2 : -INFINITY;
+          const float v1 = vrow ? __uint_as_float(s16[h + 1]) * p.scale_log2 : -INFINITY;
+          const float p0 = exp2f(v0 - m_ref[hb + h]);
+          const float p1 = exp2f(v1 - m_ref[hb + h + 1]);
+          l16[h] = __float_as_uint(__uint_as_float(l16[h]) * alpha[hb + h] + p0);
+          l16[h + 1] = __float_as_uint(__uint_as_float(l16[h + 1]) * alpha[hb + h + 1] + p1);
           pk[e >> 1] = pack_half2(p0, p1);
         }
-        *reinterpret_cast<uint4*>(preg + sw128_off(row_s, 4 * hh + c)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+        *reinterpret_cast<uint4*>(preg + sw128_off(row_s, 4 * hh + 2 * c2 + c)) =
+            make_uint4(pk[0], pk[1], pk[2], pk[3]);
       }
-      fence_proxy_async();
-      fence_before_sync();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(mb_p_full);
+      if (ok) tmem_st16(tmem + t_lane + L_COL + hb, l16);
     }
-    // ---------------------------------------------------------- epilogue
-    if (ok && ntiles > 0) ok = mbar_wait(mb_kv_free, (ntiles - 1) & 1, abort_flag, err, kWaitTimeoutNs);
-    named_bar(3, 32 * NWORK);
-    // A worker whose wait failed set the abort flag before this barrier, so
-    // one reader gives every worker the same decision.
-    if (threadIdx.x == 32) *decision = (*abort_flag == 0) ? 1 : 0;
-    named_bar(3, 32 * NWORK);
-    const bool live = *decision != 0;
-    if (ntiles > 0 && live) {
+    tmem_wait_st();
+    fence_proxy_async();
+    fence_before_sync();
+    __syncthreads();
+    // ---- O^T += V^T . P^T
+    if (issuer && ok) {
       fence_after_sync();
-      float* lbuf = reinterpret_cast<float*>(sm + SM_KV);  // [64 heads][128 rows]; the tile is dead now
-#pragma unroll
-      for (int h = 0; h < 32; ++h) lbuf[(32 * hh + h) * TM + row_s] = lsum[h];
-      named_bar(3, 32 * NWORK);
-      {
-        const int wt = threadIdx.x - 32;
-        const int head = wt >> 2, q4 = wt & 3;
-        float s = 0.f;
-#pragma unroll 8
-        for (int r = 0; r < 32; ++r) s += lbuf[head * TM + 32 * q4 + r];
-        s += __shfl_xor_sync(0xffffffffu, s, 1);
-        s += __shfl_xor_sync(0xffffffffu, s, 2);
-        if (q4 == 0) l_sum[head] = s;
-      }
-      named_bar(3, 32 * NWORK);
 #pragma unroll 1
       for (int j = 0; j < 4; ++j) {
-        uint32_t o[32];
-        tmem_ld32(tmem + t_lane + 64 * j + 32 * hh, o);
-        tmem_wait_ld();
-        const int d = 128 * j + 32 * sp + lane;
+#pragma unroll
+        for (int s = 0; s < TM / 16; ++s) {
+          const uint64_t a = sw128_desc(base + SM_KV + 2 * j * KV_REGION + 2048 * s, KV_REGION, 1024);
+          const uint64_t bp = sw128_desc(base + SM_KV + 8 * KV_REGION + 2048 * s, KV_REGION, 1024);
+          mma_f16_ss(tmem + 64 * j, a, bp, IDESC_PV, (t > 0 || s > 0) ? 1u : 0u);
+        }
+      }
+      mma_commit(mb_kv_free);
+    }
+    __syncwarp();
+  }
+  // -------------------------------------------------------------- epilogue
+  if (ok && ntiles > 0) ok = mbar_wait(mb_kv_free, (ntiles - 1) & 1, abort_flag, err, kWaitTimeoutNs);
+  __syncthreads();
+  // A thread whose wait failed set the abort flag before this barrier, so
+  // every thread reads the same decision.
+  const bool live = *abort_flag == 0;
+  __syncthreads();
+  if (ntiles > 0 && live) {
+    fence_after_sync();
+    float* lbuf = reinterpret_cast<float*>(sm + SM_KV);  // [64 heads][128 rows]; the tile is dead now
+    {
+      uint32_t lr[32];
+      tmem_ld32(tmem + t_lane + L_COL + 32 * hh, lr);
+      tmem_wait_ld();
+#pragma unroll
+      for (int h = 0; h < 32; ++h) lbuf[(32 * hh + h) * TM + row_s] = __uint_as_float(lr[h]);
+    }
+    __syncthreads();
+    {
+      const int head = threadIdx.x >> 2, q4 = threadIdx.x & 3;
+      float s = 0.f;
+#pragma unroll 8
+      for (int r = 0; r < 32; ++r) s += lbuf[head * TM + 32 * q4 + r];
+      s += __shfl_xor_sync(0xffffffffu, s, 1);
+      s += __shfl_xor_sync(0xffffffffu, s, 2);
+      if (q4 == 0) l_sum[head] = s;
+    }
+    __syncthreads();
+#pragma unroll 1
+    for (int j = 0; j < 4; ++j) {
+      uint32_t o[32];
+      tmem_ld32(tmem + t_lane + 64 * j + 32 * hh, o);
+      tmem_wait_ld();
+      const int d = 128 * j + 32 * sp + lane;
 #pragma unroll 4
-        for (int h = 0; h < 32; ++h) {
-          const int hl = 32 * hh + h;
-          const int head = h0 + hl;
-          if (head >= p.n_head) break;
-          const float val = __uint_as_float(o[h]);
-          if (p.n_splits == 1) {
-            const float l = l_sum[hl];
-            const float out = l > 0.f ? val / l : 0.f;
-            const int64_t off = ((int64_t)b * p.n_head + head) * DV + d;
-            if (p.o_bf16)
-              reinterpret_cast<__nv_bfloat16*>(p.o)[off] = __float2bfloat16_rn(out);
-            else
-              reinterpret_cast<__half*>(p.o)[off] = __float2half_rn(out);
-          } else {
-            p.part_o[(((int64_t)b * p.n_head + head) * p.n_splits + split) * DV + d] = val;
-          }
-        }
-      }
-      const int wt = threadIdx.x - 32;
-      if (wt < NH && h0 + wt < p.n_head) {
-        const float l = l_sum[wt], m = m_ref[wt];
-        const int64_t bh = (int64_t)b * p.n_head + h0 + wt;
+      for (int h = 0; h < 32; ++h) {
+        const int hl = 32 * hh + h;
+        const int head = h0 + hl;
+        if (head >= p.n_head) break;
+        const float val = __uint_as_float(o[h]);
         if (p.n_splits == 1) {
-          p.lse[bh] = l > 0.f ? (m + log2f(l)) * kLn2 : -INFINITY;
-        } else {
-          p.part_ml[(bh * p.n_splits + split) * 2] = m;
-          p.part_ml[(bh * p.n_splits + split) * 2 + 1] = l;
-        }
-      }
-    } else if (ntiles == 0) {
-      // empty slice: o = 0 / lse = -inf, or an empty partial state
-      const int wt = threadIdx.x - 32;
-      for (int i = wt; i < NH * DV; i += 32 * NWORK) {
-        const int head = h0 + i / DV, d = i % DV;
-        if (head >= p.n_head) continue;
-        const int64_t bh = (int64_t)b * p.n_head + head;
-        if (p.n_splits == 1) {
+          const float l = l_sum[hl];
+          const float out = l > 0.f ? val / l : 0.f;
+          const int64_t off = ((int64_t)b * p.n_head + head) * DV + d;
           if (p.o_bf16)
-            reinterpret_cast<__nv_bfloat16*>(p.o)[bh * DV + d] = __float2bfloat16_rn(0.f);
+            reinterpret_cast<__nv_bfloat16*>(p.o)[off] = __float2bfloat16_rn(out);
           else
-            reinterpret_cast<__half*>(p.o)[bh * DV + d] = __float2half_rn(0.f);
-          if (d == 0) p.lse[bh] = -INFINITY;
+            reinterpret_cast<__half*>(p.o)[off] = __float2half_rn(out);
         } else {
-          p.part_o[(bh * p.n_splits + split) * DV + d] = 0.f;
-          if (d == 0) {
-            p.part_ml[(bh * p.n_splits + split) * 2] = -1e30f;
-            p.part_ml[(bh * p.n_splits + split) * 2 + 1] = 0.f;
-          }
+          p.part_o[(((int64_t)b * p.n_head + head) * p.n_splits + split) * DV + d] = val;
         }
       }
     }
+    if (threadIdx.x < NH && h0 + (int)threadIdx.x < p.n_head) {
+      const float l = l_sum[threadIdx.x], m = m_ref[threadIdx.x];
+      const int64_t bh = (int64_t)b * p.n_head + h0 + threadIdx.x;
+      if (p.n_splits == 1) {
+        p.lse[bh] = l > 0.f ? (m + log2f(l)) * kLn2 : -INFINITY;
+      } else {
+        p.part_ml[(bh * p.n_splits + split) * 2] = m;
+        p.part_ml[(bh * p.n_splits + split) * 2 + 1] = l;
+      }
+    }
+  } else if (ntiles == 0) {
+    // empty slice: o = 0 / lse = -inf, or an empty partial state
+    for (int i = threadIdx.x; i < NH * DV; i += NTHREADS) {
+      const int head = h0 + i / DV, d = i % DV;
+      if (head >= p.n_head) continue;
+      const int64_t bh = (int64_t)b * p.n_head + head;
+      if (p.n_splits == 1) {
+        if (p.o_bf16)
+          reinterpret_cast<__nv_bfloat16*>(p.o)[bh * DV + d] = __float2bfloat16_rn(0.f);
+        else
+          reinterpret_cast<__half*>(p.o)[bh * DV + d] = __float2half_rn(0.f);
+        if (d == 0) p.lse[bh] = -INFINITY;
+      } else {
+        p.part_o[(bh * p.n_splits + split) * DV + d] = 0.f;
+        if (d == 0) {
+          p.part_ml[(bh * p.n_splits + split) * 2] = -1e30f;
+          p.part_ml[(bh * p.n_splits + split) * 2 + 1] = 0.f;
+        }
+      }
+    }
+  }
+  // every MMA of this CTA has completed before TMEM is released
+  if (issuer && issued && !live) {
+    mma_commit(mb_done);
+    mbar_wait(mb_done, 0, abort_flag, err, kWaitTimeoutNs);
   }
   fence_before_sync();
   __syncthreads();
