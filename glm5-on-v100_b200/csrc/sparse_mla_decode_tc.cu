@@ -67,20 +67,29 @@ __device__ __forceinline__ float unmono(uint32_t k) {
   return __uint_as_float((k & 0x80000000u) ? (k ^ 0x80000000u) : ~k);
 }
 
+// One warp's share of a tile: rows 16*w + (lane >> 3) + 4*rs (rs = 0..3).
+// Lane l holds, for each of its 4 rows, the nope chunk (l & 7) + 8*j of every
+// 128-wide scale group j (one 16-byte chunk = 16 e4m3 per group), the row's
+// four tile scales, and rope chunk (l & 7). Loads of 8 consecutive lanes cover
+// 128 contiguous bytes of a row.
 struct Tile {
-  uint4 nope[16];   // one 16-byte chunk of 16 rows (rotated row order)
-  uint4 rope[4];    // 4 of the warp's 128 rope chunks
-  int64_t my_row;   // lanes 0-15: byte offset of row (16*wid + lane), -1 if none
-  int my_valid;     // lanes 0-15: position valid (counted in the softmax)
+  uint4 nope[4][4];  // [rs][j]
+  float4 sc[4];      // [rs] scales of groups 0..3
+  uint4 rope[4];     // [rs]
+  int my_valid;      // lanes 0-15: row 16*w + lane is a counted position
 };
+
+__device__ __forceinline__ float sc_of(const float4& s, int j) {
+  return j == 0 ? s.x : (j == 1 ? s.y : (j == 2 ? s.z : s.w));
+}
 
 // Resolve + issue the global loads of this warp's 16 rows of a tile.
 __device__ __forceinline__ void load_tile(Tile& T, const SparseMlaArgs& p, int b, int j0, int hi, int seq_len,
-                                          int wid, int lane) {
-  T.my_row = -1;
+                                          int w, int lane) {
+  int64_t my_row = -1;
   T.my_valid = 0;
   if (lane < 16) {
-    const int j = j0 + 16 * wid + lane;
+    const int j = j0 + 16 * w + lane;
     if (j < hi) {
       const int pos = p.idx[(int64_t)b * p.idx_stride + j];
       if (pos >= 0 && pos < seq_len) {
@@ -88,28 +97,27 @@ __device__ __forceinline__ void load_tile(Tile& T, const SparseMlaArgs& p, int b
         const int blk_i = pos / p.page_size;
         if (blk_i < p.max_blocks) {
           const int64_t r = (int64_t)p.bt[(int64_t)b * p.bt_stride + blk_i] * p.page_size + (pos - blk_i * p.page_size);
-          if (r >= 0 && r < p.n_kv_rows) T.my_row = r * ROW_BYTES;
+          if (r >= 0 && r < p.n_kv_rows) my_row = r * ROW_BYTES;
         }
       }
     }
   }
 #pragma unroll
-  for (int r = 0; r < 16; ++r) {
-    const int rr = (r + (lane >> 2)) & 15;
-    const int64_t off = __shfl_sync(0xffffffffu, T.my_row, rr);
+  for (int rs = 0; rs < 4; ++rs) {
+    const int64_t off = __shfl_sync(0xffffffffu, my_row, (lane >> 3) + 4 * rs);
     if (off >= 0) {
-      T.nope[r] = ldg_nc16(p.kv + off + 16 * lane);
-      // the tile scale is read again at store time: bring its line into L1 now
-      asm volatile("prefetch.global.L1 [%0];" ::"l"(p.kv + off + 512));
-    } else {
-      T.nope[r] = make_uint4(0, 0, 0, 0);
-    }
-  }
+      const uint8_t* row = p.kv + off;
 #pragma unroll
-  for (int m = 0; m < 4; ++m) {
-    const int k = lane + 32 * m;  // rope chunk k of 128: row k>>3, chunk k&7
-    const int64_t off = __shfl_sync(0xffffffffu, T.my_row, k >> 3);
-    T.rope[m] = off >= 0 ? ldg_nc16(p.kv + off + 528 + 16 * (k & 7)) : make_uint4(0, 0, 0, 0);
+      for (int j = 0; j < 4; ++j) T.nope[rs][j] = ldg_nc16(row + 16 * ((lane & 7) + 8 * j));
+      const uint4 s = ldg_nc16(row + 512);
+      T.sc[rs] = make_float4(__uint_as_float(s.x), __uint_as_float(s.y), __uint_as_float(s.z), __uint_as_float(s.w));
+      T.rope[rs] = ldg_nc16(row + 528 + 16 * (lane & 7));
+    } else {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) T.nope[rs][j] = make_uint4(0, 0, 0, 0);
+      T.sc[rs] = make_float4(0.f, 0.f, 0.f, 0.f);
+      T.rope[rs] = make_uint4(0, 0, 0, 0);
+    }
   }
 }
 
@@ -139,26 +147,32 @@ __device__ __forceinline__ uint4 dequant8(uint32_t w0, uint32_t w1, float sc) {
   return o;
 }
 
-__device__ __forceinline__ void store_tile(const Tile& T, const SparseMlaArgs& p, uint8_t* sm, uint8_t* valid,
-                                           int wid, int lane) {
+// Store scale group j (K blocks 2j, 2j+1) of this warp's rows.
+__device__ __forceinline__ void store_group(const Tile& T, uint8_t* sm, int j, int w, int lane) {
+  const int c = (lane & 7) + 8 * j;  // nope chunk: e4m3 values [16c, 16c+16)
+  uint8_t* region = sm + SM_KV + (c >> 2) * KV_REGION;
+  const int c0 = 2 * (c & 3);
 #pragma unroll
-  for (int r = 0; r < 16; ++r) {
-    const int rr = (r + (lane >> 2)) & 15;
-    const int i = 16 * wid + rr;
-    const int kb = lane >> 2;
-    const int c0 = 2 * (lane & 3);
-    const int64_t off = __shfl_sync(0xffffffffu, T.my_row, rr);
-    const float sc = off >= 0 ? __ldg(reinterpret_cast<const float*>(p.kv + off + 512) + (lane >> 3)) : 0.f;
-    uint8_t* region = sm + SM_KV + kb * KV_REGION;
-    *reinterpret_cast<uint4*>(region + sw128_off(i, c0)) = dequant8(T.nope[r].x, T.nope[r].y, sc);
-    *reinterpret_cast<uint4*>(region + sw128_off(i, c0 + 1)) = dequant8(T.nope[r].z, T.nope[r].w, sc);
+  for (int rs = 0; rs < 4; ++rs) {
+    const int i = 16 * w + (lane >> 3) + 4 * rs;
+    const float sc = sc_of(T.sc[rs], j);
+    *reinterpret_cast<uint4*>(region + sw128_off(i, c0)) = dequant8(T.nope[rs][j].x, T.nope[rs][j].y, sc);
+    *reinterpret_cast<uint4*>(region + sw128_off(i, c0 + 1)) = dequant8(T.nope[rs][j].z, T.nope[rs][j].w, sc);
   }
+}
+
+__device__ __forceinline__ void store_rope(const Tile& T, uint8_t* sm, uint8_t* valid, int w, int lane) {
 #pragma unroll
-  for (int m = 0; m < 4; ++m) {
-    const int k = lane + 32 * m;
-    *reinterpret_cast<uint4*>(sm + SM_KV + 8 * KV_REGION + sw128_off(16 * wid + (k >> 3), k & 7)) = T.rope[m];
-  }
-  if (lane < 16) valid[16 * wid + lane] = (uint8_t)T.my_valid;
+  for (int rs = 0; rs < 4; ++rs)
+    *reinterpret_cast<uint4*>(sm + SM_KV + 8 * KV_REGION + sw128_off(16 * w + (lane >> 3) + 4 * rs, lane & 7)) =
+        T.rope[rs];
+  if (lane < 16) valid[16 * w + lane] = (uint8_t)T.my_valid;
+}
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
 }
 
 __global__ void __launch_bounds__(NTHREADS, 1) sparse_mla_decode_tc_kernel(const SparseMlaArgs p, int32_t* err) {
@@ -167,17 +181,21 @@ __global__ void __launch_bounds__(NTHREADS, 1) sparse_mla_decode_tc_kernel(const
   const uint32_t base = (raw_base + 1023u) & ~1023u;
   uint8_t* sm = smem_raw + (base - raw_base);
   uint8_t* misc = sm + SM_MISC;
-  uint64_t* mbar = reinterpret_cast<uint64_t*>(misc);  // s_full, kv_free, done
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(misc + 64);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(misc + 68);
-  int* any_rescale = reinterpret_cast<int*>(misc + 72);    // [2]
-  float* m_ref = reinterpret_cast<float*>(misc + 128);     // [64] running max (log2 units)
+  // mbarriers: [0..4] kv_full (groups 0..3, rope), [5..8] kv_free (PV tile j), [9] s_full, [10] done
+  uint64_t* mbar = reinterpret_cast<uint64_t*>(misc);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(misc + 96);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(misc + 100);
+  int* ovf = reinterpret_cast<int*>(misc + 104);           // [2][4] per-warp "score above running max" votes
+  int* any_rescale = reinterpret_cast<int*>(misc + 136);   // [2]
+  float* m_ref = reinterpret_cast<float*>(misc + 256);     // [64] running max (log2 units)
   float* alpha = m_ref + 64;                               // [64] this tile's rescale factors
   float* tmax = alpha + 64;                                // [2][4][32] per-warp tile maxima
   float* l_sum = tmax + 256;                               // [64]
   uint8_t* valid = reinterpret_cast<uint8_t*>(l_sum + 64); // [128]
-
-  const uint32_t mb_s_full = smem_u32(&mbar[0]), mb_kv_free = smem_u32(&mbar[1]), mb_done = smem_u32(&mbar[2]);
+  const uint32_t mb0 = smem_u32(&mbar[0]);
+  auto mb_kv_full = [&](int j) { return mb0 + 8u * (uint32_t)j; };
+  auto mb_kv_free = [&](int j) { return mb0 + 8u * (uint32_t)(5 + j); };
+  const uint32_t mb_s_full = mb0 + 8u * 9, mb_done = mb0 + 8u * 10;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int b = blockIdx.x;
@@ -191,8 +209,9 @@ __global__ void __launch_bounds__(NTHREADS, 1) sparse_mla_decode_tc_kernel(const
 
   if (warp == 0) {
     if (lane == 0) {
+      for (int j = 0; j < 5; ++j) mbar_init(mb_kv_full(j), NWORK);
+      for (int j = 0; j < 4; ++j) mbar_init(mb_kv_free(j), 1);
       mbar_init(mb_s_full, 1);
-      mbar_init(mb_kv_free, 1);
       mbar_init(mb_done, 1);
       mbar_init_fence();
       *abort_flag = 0;
@@ -223,7 +242,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) sparse_mla_decode_tc_kernel(const
   fence_after_sync();
   const uint32_t tmem = *tmem_slot;
 
-  const int wid = warp;              // producer: rows [16*wid, 16*wid+16) of a tile
+  const int w = warp;                // producer: rows 16*w .. 16*w + 15 of a tile
   const int sp = warp & 3;           // TMEM sub-partition: lanes [32*sp, 32*sp+32)
   const int hh = warp >> 2;          // softmax head half: heads [32*hh, 32*hh+32)
   const int row_s = 32 * sp + lane;  // the tile row this thread owns in the softmax
@@ -231,103 +250,141 @@ __global__ void __launch_bounds__(NTHREADS, 1) sparse_mla_decode_tc_kernel(const
   // The running row sums of P live in TMEM columns [L_COL + 32*hh, +32) of
   // this thread's lane (one latent-row slot x 32 heads), not in registers.
   Tile T;
-  if (ntiles > 0) load_tile(T, p, b, lo, hi, seq_len, wid, lane);
+  if (ntiles > 0) load_tile(T, p, b, lo, hi, seq_len, w, lane);
   // Control flow is uniform across the block: after a timed-out wait (`ok`
   // false, abort flag set) every warp still executes the same sequence of
-  // barriers, and every later wait returns at once, so no thread is left
-  // behind on a barrier.
+  // barriers and arrivals, and every later wait returns at once.
   bool ok = true;
   bool issued = false;
   for (int t = 0; t < ntiles; ++t) {
     const uint32_t ph = t & 1;
-    // ---- producer: the previous tile's PV has drained the smem tile
-    if (t > 0) ok = ok && mbar_wait(mb_kv_free, ph ^ 1, abort_flag, err, kWaitTimeoutNs);
-    if (ok) store_tile(T, p, sm, valid, wid, lane);
-    fence_proxy_async();
-    __syncthreads();
-    // ---- S^T = KV . Q^T
-    if (issuer && ok) {
-      fence_after_sync();
-#pragma unroll 1
-      for (int kb = 0; kb < 9; ++kb) {
+    // ---- store tile t group by group as PV(t-1) releases it; QK(t) follows each group
+    // (unrolled: the tile registers are indexed by the group)
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const uint64_t a = sw128_desc(base + SM_KV + kb * KV_REGION + 32 * k, 16, 1024);
-          const uint64_t bq = sw128_desc(base + SM_Q + kb * Q_REGION + 32 * k, 16, 1024);
-          mma_f16_ss(tmem + S_COL, a, bq, IDESC_QK, (kb | k) != 0);
+    for (int j = 0; j < 4; ++j) {
+      if (t > 0) ok = ok && mbar_wait(mb_kv_free(j), ph ^ 1, abort_flag, err, kWaitTimeoutNs);
+      if (ok) store_group(T, sm, j, w, lane);
+      fence_proxy_async();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(mb_kv_full(j));
+      if (issuer) {
+        ok = ok && mbar_wait(mb_kv_full(j), ph, abort_flag, err, kWaitTimeoutNs);
+        if (ok) {
+          fence_after_sync();
+#pragma unroll
+          for (int kb = 2 * j; kb < 2 * j + 2; ++kb)
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const uint64_t a = sw128_desc(base + SM_KV + kb * KV_REGION + 32 * k, 16, 1024);
+              const uint64_t bq = sw128_desc(base + SM_Q + kb * Q_REGION + 32 * k, 16, 1024);
+              mma_f16_ss(tmem + S_COL, a, bq, IDESC_QK, (kb | k) != 0);
+            }
+          issued = true;
         }
       }
-      mma_commit(mb_s_full);
-      issued = true;
+      __syncwarp();
+    }
+    // rope group: its region held P^T(t-1), released when all of PV(t-1) is done (kv_free[3])
+    if (ok) store_rope(T, sm, valid, w, lane);
+    fence_proxy_async();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(mb_kv_full(4));
+    if (issuer) {
+      ok = ok && mbar_wait(mb_kv_full(4), ph, abort_flag, err, kWaitTimeoutNs);
+      if (ok) {
+        fence_after_sync();
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const uint64_t a = sw128_desc(base + SM_KV + 8 * KV_REGION + 32 * k, 16, 1024);
+          const uint64_t bq = sw128_desc(base + SM_Q + 8 * Q_REGION + 32 * k, 16, 1024);
+          mma_f16_ss(tmem + S_COL, a, bq, IDESC_QK, 1u);
+        }
+        mma_commit(mb_s_full);
+      }
     }
     __syncwarp();
-    if (ok && t + 1 < ntiles) load_tile(T, p, b, lo + (t + 1) * TM, hi, seq_len, wid, lane);
+    // ---- next tile's loads stay in flight through softmax(t) and PV(t)
+    if (ok && t + 1 < ntiles) load_tile(T, p, b, lo + (t + 1) * TM, hi, seq_len, w, lane);
 
-    // ---- softmax
+    // ---- softmax(t)
     ok = ok && mbar_wait(mb_s_full, ph, abort_flag, err, kWaitTimeoutNs);
+    __syncthreads();  // validity bytes of tile t (written with the rope group) are visible
     fence_after_sync();
-    uint32_t sreg[32];
-    if (ok) {
-      tmem_ld32(tmem + t_lane + S_COL + 32 * hh, sreg);
-      tmem_wait_ld();
-    } else {
-#pragma unroll
-      for (int h = 0; h < 32; ++h) sreg[h] = 0u;
-    }
-    const bool vrow = valid[row_s] != 0;
-    uint32_t my_max = 0;
-#pragma unroll
-    for (int h = 0; h < 32; ++h) {
-      const float v = vrow ? __uint_as_float(sreg[h]) * p.scale_log2 : -INFINITY;
-      const uint32_t wm = __reduce_max_sync(0xffffffffu, monotone32(v));
-      if (lane == h) my_max = wm;
-    }
-    tmax[(hh * 4 + sp) * 32 + lane] = unmono(my_max);
-    named_bar(1 + hh, 128);
-    if (sp == 0) {
-      const int head = 32 * hh + lane;
-      float tm = tmax[(hh * 4) * 32 + lane];
-#pragma unroll
-      for (int s = 1; s < 4; ++s) tm = fmaxf(tm, tmax[(hh * 4 + s) * 32 + lane]);
-      const float m_old = m_ref[head];
-      float a = 1.f;
-      if (tm > m_old + kRescaleThreshold) {
-        a = exp2f(m_old - tm);
-        m_ref[head] = tm;
-      }
-      alpha[head] = a;
-      const unsigned any = __ballot_sync(0xffffffffu, a != 1.f);
-      if (lane == 0) any_rescale[hh] = any != 0u;
-    }
-    named_bar(1 + hh, 128);
-    if (ok && any_rescale[hh] && t > 0) {  // O^T columns of this head half, lanes of this sub-partition
-#pragma unroll 1
-      for (int j = 0; j < 8; ++j) {  // 4 value tiles x 2 groups of 16 head columns
-        uint32_t o[16];
-        const uint32_t col = 64 * (j >> 1) + 32 * hh + 16 * (j & 1);
-        tmem_ld16(tmem + t_lane + col, o);
+    float v[32];
+    {
+      uint32_t sreg[32];
+      if (ok) {
+        tmem_ld32(tmem + t_lane + S_COL + 32 * hh, sreg);
         tmem_wait_ld();
+      } else {
 #pragma unroll
-        for (int h = 0; h < 16; ++h)
-          o[h] = __float_as_uint(__uint_as_float(o[h]) * alpha[32 * hh + 16 * (j & 1) + h]);
-        tmem_st16(tmem + t_lane + col, o);
+        for (int h = 0; h < 32; ++h) sreg[h] = 0u;
       }
-      tmem_wait_st();
+      const bool vrow = valid[row_s] != 0;
+      bool over = false;
+#pragma unroll
+      for (int h = 0; h < 32; ++h) {
+        v[h] = vrow ? __uint_as_float(sreg[h]) * p.scale_log2 : -INFINITY;
+        over |= v[h] > m_ref[32 * hh + h] + kRescaleThreshold;
+      }
+      const unsigned vote = __ballot_sync(0xffffffffu, over);
+      if (lane == 0) ovf[hh * 4 + sp] = vote != 0u;
     }
-    // S^T is read from tensor memory a second time, in groups of 16 heads,
-    // instead of being kept in registers across the max reduction; the row
-    // sums are updated in TMEM alongside.
-    uint8_t* preg = sm + SM_KV + 8 * KV_REGION;
+    named_bar(1 + hh, 128);
+    const bool slow = ovf[hh * 4] | ovf[hh * 4 + 1] | ovf[hh * 4 + 2] | ovf[hh * 4 + 3];
+    if (slow) {
+      // exact tile maxima of this head half; heads whose max grew by more than
+      // 2^8 move their running max and rescale what was accumulated
+      uint32_t my_max = 0;
+#pragma unroll
+      for (int h = 0; h < 32; ++h) {
+        const uint32_t wm = __reduce_max_sync(0xffffffffu, monotone32(v[h]));
+        if (lane == h) my_max = wm;
+      }
+      tmax[(hh * 4 + sp) * 32 + lane] = unmono(my_max);
+      named_bar(1 + hh, 128);
+      if (sp == 0) {
+        const int head = 32 * hh + lane;
+        float tm = tmax[(hh * 4) * 32 + lane];
+#pragma unroll
+        for (int s = 1; s < 4; ++s) tm = fmaxf(tm, tmax[(hh * 4 + s) * 32 + lane]);
+        const float m_old = m_ref[head];
+        float a = 1.f;
+        if (tm > m_old + kRescaleThreshold) {
+          a = ex2(m_old - tm);
+          m_ref[head] = tm;
+        }
+        alpha[head] = a;
+        const unsigned any = __ballot_sync(0xffffffffu, a != 1.f);
+        if (lane == 0) any_rescale[hh] = any != 0u;
+      }
+      named_bar(1 + hh, 128);
+      if (ok && any_rescale[hh] && t > 0) {  // O^T columns of this head half, lanes of this sub-partition
 #pragma unroll 1
+        for (int jj = 0; jj < 8; ++jj) {  // 4 value tiles x 2 groups of 16 head columns
+          uint32_t o[16];
+          const uint32_t col = 64 * (jj >> 1) + 32 * hh + 16 * (jj & 1);
+          tmem_ld16(tmem + t_lane + col, o);
+          tmem_wait_ld();
+#pragma unroll
+          for (int h = 0; h < 16; ++h)
+            o[h] = __float_as_uint(__uint_as_float(o[h]) * alpha[32 * hh + 16 * (jj & 1) + h]);
+          tmem_st16(tmem + t_lane + col, o);
+        }
+        tmem_wait_st();
+      }
+    }
+    // P = 2^(v - m) in fp16 into the P^T rows (the rope region, consumed by QK(t));
+    // row sums updated in TMEM
+    uint8_t* preg = sm + SM_KV + 8 * KV_REGION;
+#pragma unroll
     for (int c2 = 0; c2 < 2; ++c2) {
       const int hb = 32 * hh + 16 * c2;  // first head of this group
-      uint32_t s16[16], l16[16];
-      if (ok) {
-        tmem_ld16(tmem + t_lane + S_COL + hb, s16);
-        if (t > 0) tmem_ld16(tmem + t_lane + L_COL + hb, l16);
+      uint32_t l16[16];
+      if (ok && t > 0) {
+        tmem_ld16(tmem + t_lane + L_COL + hb, l16);
         tmem_wait_ld();
-      }
-      if (!ok || t == 0) {
+      } else {
 #pragma unroll
         for (int h = 0; h < 16; ++h) l16[h] = 0u;
       }
@@ -336,13 +393,13 @@ __global__ void __launch_bounds__(NTHREADS, 1) sparse_mla_decode_tc_kernel(const
         uint32_t pk[4];
 #pragma unroll
         for (int e = 0; e < 8; e += 2) {
-          const int h = 8 * c + e;
-          const float v0 = vrow ? __uint_as_float(s16[h]) * p.scale_log2 : -INFINITY;
-          const float v1 = vrow ? __uint_as_float(s16[h + 1]) * p.scale_log2 : -INFINITY;
-          const float p0 = exp2f(v0 - m_ref[hb + h]);
-          const float p1 = exp2f(v1 - m_ref[hb + h + 1]);
-          l16[h] = __float_as_uint(__uint_as_float(l16[h]) * alpha[hb + h] + p0);
-          l16[h + 1] = __float_as_uint(__uint_as_float(l16[h + 1]) * alpha[hb + h + 1] + p1);
+          const int h = 16 * c2 + 8 * c + e;  // head index within the half
+          const float p0 = ex2(v[h] - m_ref[32 * hh + h]);
+          const float p1 = ex2(v[h + 1] - m_ref[32 * hh + h + 1]);
+          const int hl = 8 * c + e;
+          const float a0 = slow ? alpha[32 * hh + h] : 1.f, a1 = slow ? alpha[32 * hh + h + 1] : 1.f;
+          l16[hl] = __float_as_uint(__uint_as_float(l16[hl]) * a0 + p0);
+          l16[hl + 1] = __float_as_uint(__uint_as_float(l16[hl + 1]) * a1 + p1);
           pk[e >> 1] = pack_half2(p0, p1);
         }
         *reinterpret_cast<uint4*>(preg + sw128_off(row_s, 4 * hh + 2 * c2 + c)) =
@@ -354,7 +411,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) sparse_mla_decode_tc_kernel(const
     fence_proxy_async();
     fence_before_sync();
     __syncthreads();
-    // ---- O^T += V^T . P^T
+    // ---- O^T += V^T . P^T, one commit per 128-wide value tile
     if (issuer && ok) {
       fence_after_sync();
 #pragma unroll 1
@@ -365,13 +422,13 @@ __global__ void __launch_bounds__(NTHREADS, 1) sparse_mla_decode_tc_kernel(const
           const uint64_t bp = sw128_desc(base + SM_KV + 8 * KV_REGION + 2048 * s, KV_REGION, 1024);
           mma_f16_ss(tmem + 64 * j, a, bp, IDESC_PV, (t > 0 || s > 0) ? 1u : 0u);
         }
+        mma_commit(mb_kv_free(j));
       }
-      mma_commit(mb_kv_free);
     }
     __syncwarp();
   }
   // -------------------------------------------------------------- epilogue
-  if (ok && ntiles > 0) ok = mbar_wait(mb_kv_free, (ntiles - 1) & 1, abort_flag, err, kWaitTimeoutNs);
+  if (ok && ntiles > 0) ok = mbar_wait(mb_kv_free(3), (ntiles - 1) & 1, abort_flag, err, kWaitTimeoutNs);
   __syncthreads();
   // A thread whose wait failed set the abort flag before this barrier, so
   // every thread reads the same decision.

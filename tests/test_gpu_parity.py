@@ -70,15 +70,25 @@ def random_dsmla_cache(nb, page, seed):
     return kv
 
 
-def assert_attn_close(o, lse, o_ref, lse_ref, rtol=ATTN_RTOL):
+def assert_attn_close(o, lse, o_ref, lse_ref, rtol=ATTN_RTOL, out_dtype=None):
+    """Per (row, head): ||o - o_ref|| <= rtol * ||o_ref|| + ||rnd(o_ref) - o_ref||.
+
+    The second term is the error of a perfect kernel whose fp32 result is
+    rounded to the output dtype (for bf16 it alone is ~1.7e-3 relative), so
+    the bound is 2e-3 relative error beyond the output format's own rounding.
+    """
     assert np.isfinite(o).all()
     empty = np.isneginf(lse_ref)
     np.testing.assert_array_equal(np.isneginf(lse), empty)
     assert np.all(o[empty] == 0)
     num = np.linalg.norm(o - o_ref, axis=-1)
-    den = np.linalg.norm(o_ref, axis=-1)
-    rel = np.where(empty, 0.0, num / np.maximum(den, 1e-30))
-    assert rel.max() <= rtol, f"max per-row relative error {rel.max():.3e}"
+    den = np.maximum(np.linalg.norm(o_ref, axis=-1), 1e-30)
+    floor = 0.0
+    if out_dtype is not None:
+        rnd = torch.from_numpy(o_ref.astype(np.float32)).to(out_dtype).float().numpy()
+        floor = np.linalg.norm(rnd - o_ref, axis=-1) / den
+    excess = np.where(empty, 0.0, num / den - floor)
+    assert excess.max() <= rtol, f"max per-row relative error beyond output rounding {excess.max():.3e}"
     np.testing.assert_allclose(lse[~empty], lse_ref[~empty], atol=2e-3, rtol=0)
 
 
@@ -99,7 +109,7 @@ def test_decode_matches_reference_golden(dsa, name):
                                              (torch.bfloat16, torch.float16)])
 def test_decode_formats(dsa, fmt, q_dtype, o_dtype):
     c = cases.decode_case(21, B=4, H=64, page=64, seq_lens=[2048, 5000, 100, 9000], topk=2048, blocks_per_seq=160)
-    assert_attn_close(*run_decode(dsa, c, fmt, q_dtype, o_dtype))
+    assert_attn_close(*run_decode(dsa, c, fmt, q_dtype, o_dtype), out_dtype=o_dtype)
 
 
 @pytest.mark.parametrize("B,H,topk", [(1, 8, 2048), (2, 16, 512), (3, 128, 256), (6, 72, 64), (200, 64, 96),
@@ -108,7 +118,7 @@ def test_decode_shapes_and_splits(dsa, B, H, topk):
     rng = np.random.default_rng(B * 1000 + H)
     seq = rng.integers(1, 6000, size=B)
     c = cases.decode_case(31 + B, B=B, H=H, page=64, seq_lens=seq, topk=topk, blocks_per_seq=94)
-    assert_attn_close(*run_decode(dsa, c, "fp8"))
+    assert_attn_close(*run_decode(dsa, c, "fp8"), out_dtype=torch.bfloat16)
 
 
 @pytest.mark.parametrize("fmt", ["fp8", "f16"])
@@ -122,7 +132,7 @@ def test_decode_growing_scores_rescale_path(dsa, fmt):
     for b in range(3):  # rows of each sequence grow with position
         rows = c["block_table"][b][np.arange(4096) // 64].astype(np.int64) * 64 + np.arange(4096) % 64
         c["kv"][rows] = cases.f16_exact(c["kv"][rows] * grow[:4096])
-    assert_attn_close(*run_decode(dsa, c, fmt, torch.bfloat16, torch.bfloat16, scale=0.5))
+    assert_attn_close(*run_decode(dsa, c, fmt, torch.bfloat16, torch.bfloat16, scale=0.5), out_dtype=torch.bfloat16)
 
 
 def test_decode_invalid_entries_and_empty_rows(dsa):
@@ -136,7 +146,7 @@ def test_decode_invalid_entries_and_empty_rows(dsa):
     c["block_table"][5, 3] = -7            # negative block id: zero row, still counted
     o, lse, o_ref, lse_ref = run_decode(dsa, c, "fp8")
     assert np.isneginf(lse[2]).all() and np.isneginf(lse[4]).all()
-    assert_attn_close(o, lse, o_ref, lse_ref)
+    assert_attn_close(o, lse, o_ref, lse_ref, out_dtype=torch.bfloat16)
 
 
 def test_decode_topk_zero(dsa):
@@ -192,7 +202,8 @@ def test_decode_full_size_sampled_rows(dsa):
                                              np.concatenate([kv_rows, np.zeros((page, 576))]),
                                              np.arange(topk, dtype=np.int32)[None], local_bt,
                                              np.array([topk], np.int32), page, scale)
-        assert_attn_close(o[b:b + 1].float().cpu().numpy(), lse[b:b + 1].cpu().numpy(), o_ref, lse_ref)
+        assert_attn_close(o[b:b + 1].float().cpu().numpy(), lse[b:b + 1].cpu().numpy(), o_ref, lse_ref,
+                          out_dtype=torch.bfloat16)
 
 
 # ---------------------------------------------------------- indexer logits
@@ -320,7 +331,8 @@ def test_decode_topk_with_fused_histogram_end_to_end(dsa):
     np.testing.assert_array_equal(got, O.topk_rows(s, c["seq"], K))
     ref = O.indexer_logits(c["q"], k_ref, c["w"], c["bt"], c["seq"], c["page"], c["max_kv"])
     exp = O.topk_rows(ref.astype(np.float32), c["seq"], K)
-    band = 4 * np.nanmax(np.where(np.isfinite(ref), np.abs(s - ref), 0)) + 1e-6
+    fin = np.isfinite(ref)
+    band = 4 * np.abs(s[fin] - ref[fin]).max() + 1e-6
     for b in range(B):
         diff = set(got[b].tolist()) ^ set(exp[b].tolist())
         if diff:
