@@ -121,28 +121,36 @@ __device__ __forceinline__ void load_tile(Tile& T, const SparseMlaArgs& p, int b
   }
 }
 
+// Two e4m3 bytes (in the low byte of each 16-bit half of x) -> half2 holding
+// value/256 exactly: sign to bit 15, exponent+mantissa shifted into the fp16
+// field (e4m3 bias 7 vs fp16 bias 15 is the 2^8 factor; e4m3 subnormals land
+// on fp16 subnormals). Integer ops only, so the conversion stays off the
+// (narrow) conversion pipe.
+__device__ __forceinline__ uint32_t e4m3x2_div256(uint32_t x) {
+  return ((x << 8) & 0x80008000u) | ((x << 7) & 0x3F803F80u);
+}
+
 // e4m3 x 8 (two words) times scale -> 8 fp16 (uint4).
 __device__ __forceinline__ uint4 dequant8(uint32_t w0, uint32_t w1, float sc) {
-  __half2 a, b, c, d;
-  e4m3x4_to_half2x2(w0, a, b);
-  e4m3x4_to_half2x2(w1, c, d);
+  const uint32_t q[4] = {e4m3x2_div256(__byte_perm(w0, 0, 0x4140)), e4m3x2_div256(__byte_perm(w0, 0, 0x4342)),
+                         e4m3x2_div256(__byte_perm(w1, 0, 0x4140)), e4m3x2_div256(__byte_perm(w1, 0, 0x4342))};
   uint4 o;
-  if (sc >= 6.2e-5f && sc <= 146.0f) {  // scale and every product stay normal in fp16
-    const __half2 s2 = __float2half2_rn(sc);
-    a = __hmul2(a, s2);
-    b = __hmul2(b, s2);
-    c = __hmul2(c, s2);
-    d = __hmul2(d, s2);
-    o.x = *reinterpret_cast<uint32_t*>(&a);
-    o.y = *reinterpret_cast<uint32_t*>(&b);
-    o.z = *reinterpret_cast<uint32_t*>(&c);
-    o.w = *reinterpret_cast<uint32_t*>(&d);
+  const float s256 = sc * 256.0f;
+  if (s256 >= 6.2e-5f && s256 <= 32768.0f) {  // scale*256 and every product stay normal in fp16
+    const __half2 s2 = __float2half2_rn(s256);
+    __half2 r[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) r[e] = __hmul2(*reinterpret_cast<const __half2*>(&q[e]), s2);
+    o = make_uint4(*reinterpret_cast<uint32_t*>(&r[0]), *reinterpret_cast<uint32_t*>(&r[1]),
+                   *reinterpret_cast<uint32_t*>(&r[2]), *reinterpret_cast<uint32_t*>(&r[3]));
   } else {
-    float2 fa = __half22float2(a), fb = __half22float2(b), fc = __half22float2(c), fd = __half22float2(d);
-    o.x = pack_half2(fa.x * sc, fa.y * sc);
-    o.y = pack_half2(fb.x * sc, fb.y * sc);
-    o.z = pack_half2(fc.x * sc, fc.y * sc);
-    o.w = pack_half2(fd.x * sc, fd.y * sc);
+    uint32_t r[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&q[e]));
+      r[e] = pack_half2(f.x * s256, f.y * s256);
+    }
+    o = make_uint4(r[0], r[1], r[2], r[3]);
   }
   return o;
 }
