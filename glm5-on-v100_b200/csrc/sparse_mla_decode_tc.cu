@@ -13,23 +13,29 @@
 //                                                 B = Q, K-major smem)
 //   O^T[512 x 64] += V^T[512 x 128] . P^T        (A = same KV tile read
 //                                                 MN-major; B = P^T, MN-major)
-// S^T and O^T live in tensor memory (64 + 256 columns). The KV tile is stored
-// once as fp16 in 128-byte-swizzled rows that serve both as K-major A of QK
-// and MN-major A of PV; P^T (fp16) overwrites the tile's rope columns after QK
-// has consumed them, which keeps Q (72 KB) + tile (144 KB) within one SM.
+// S^T, O^T and the running row sums live in tensor memory (64 + 256 + 64
+// columns). The KV tile is stored once as fp16 in 128-byte-swizzled rows that
+// serve both as K-major A of QK and MN-major A of PV; P^T (fp16) overwrites
+// the tile's rope columns after QK has consumed them, which keeps Q (72 KB) +
+// tile (144 KB) + the slice's row table (8 KB) within one SM.
 //
-// Block of 8 warps (256 threads, so up to 255 registers per thread). Warp 0
-// allocates TMEM and its lane 0 issues the MMAs between block barriers. As
-// producers, all warps gather the next tile's 656-B rows with coalesced
-// 16-byte loads into registers while the current tile is in the tensor core,
-// then dequantise (e4m3 x per-128 scale -> fp16) into the swizzled tile. As
-// softmax warps, each thread owns one latent row and 32 heads of S^T
-// (tcgen05.ld), computes per-head tile maxima with warp reductions, and keeps
-// a lazily-updated running max: O^T is rescaled in TMEM only when a head's max
-// grows by more than 2^8, which keeps P <= 256 in fp16 while leaving o and lse
-// exact. Row sums accumulate per thread in spare TMEM columns and are reduced
-// once at the end. Every wait on the tensor core is an mbarrier wait bounded
-// by a device-time limit that reports DSA_ERR_TIMEOUT instead of hanging.
+// Block of 16 warps (512 threads). At the start the block resolves the
+// slice's selected positions through the block table into a row table in
+// shared memory, so no dependent index loads sit on the tile pipeline. Each
+// warp produces 8 rows of every tile: the 656-byte rows are read with 16-byte
+// coalesced loads into registers, and as soon as a 128-wide scale group of
+// tile t is stored (dequantised: e4m3 bits expanded to fp16 with integer ops,
+// times the per-group scale) the same registers receive that group of tile
+// t+1, so the next tile's reads stay in flight through softmax and PV. Lane 0
+// of warp 0 issues the QK MMAs group by group as the tile lands and the PV
+// MMAs after the softmax, committing one mbarrier per 128-wide value tile so
+// the next tile's stores start while PV still runs. In the softmax each
+// thread owns one latent row and 16 heads of S^T (tcgen05.ld): probabilities
+// use a lazily-updated running max per head, moved (with an in-TMEM rescale
+// of O^T and the row sums) only when a score exceeds it by more than 2^8, so
+// P <= 256 in fp16 while o and lse stay exact. Every wait on the tensor core
+// is an mbarrier wait bounded by a device-time limit that reports
+// DSA_ERR_TIMEOUT instead of hanging.
 #include "sparse_mla.cuh"
 #include "tc_common.cuh"
 
@@ -38,28 +44,36 @@ namespace {
 
 using namespace tc;
 
-constexpr int TM = kTcTileRows;   // 128 latent rows per tile (MMA M)
-constexpr int NH = 64;            // heads per CTA (MMA N)
-constexpr int NWORK = 8;          // warps; all of them produce tiles and run the softmax
-constexpr int NTHREADS = 32 * NWORK;
+constexpr int TM = kTcTileRows;            // 128 latent rows per tile (MMA M)
+constexpr int NH = 64;                     // heads per CTA (MMA N)
+constexpr int NWARPS = 16;
+constexpr int NTHREADS = 32 * NWARPS;
+constexpr int ROWS_PER_WARP = TM / NWARPS; // 8
 constexpr int DV = 512;
+constexpr int TABLE_ROWS = 2048;           // resolved rows held at a time
 constexpr uint32_t KV_REGION = TM * 128;   // one 64-wide K block of the tile: 16 KB
 constexpr uint32_t Q_REGION = NH * 128;    // one 64-wide K block of Q: 8 KB
 constexpr uint32_t SM_KV = 0;
 constexpr uint32_t SM_Q = 9 * KV_REGION;
-constexpr uint32_t SM_MISC = SM_Q + 9 * Q_REGION;
-constexpr uint32_t MISC_BYTES = 4096;
-constexpr uint32_t SMEM_BYTES = SM_MISC + MISC_BYTES + 1024;  // + alignment slack
+constexpr uint32_t SM_TABLE = SM_Q + 9 * Q_REGION;
+constexpr uint32_t SM_MISC = SM_TABLE + TABLE_ROWS * 4;
+constexpr uint32_t MISC_BYTES = 2048;
+constexpr uint32_t SMEM_BYTES = SM_MISC + MISC_BYTES + 1024;  // + alignment slack = 232,448
 constexpr uint32_t S_COL = 256;            // S^T columns [256, 320); O^T tile j at [64j, 64j+64)
 constexpr uint32_t L_COL = 320;            // running row sums of P: columns [320, 384)
 constexpr uint32_t TMEM_COLS = 512;
 constexpr int ROW_BYTES = 656;
 constexpr float kLn2 = 0.69314718055994530942f;
-constexpr float kRescaleThreshold = 8.0f;  // log2 units
+constexpr float kRescaleThreshold = 8.0f;  // log2 units: P stays <= 256
 constexpr uint64_t kWaitTimeoutNs = 2000000000ull;
+// row table codes
+constexpr int kRowSkip = -1;   // position not selected / out of range: not counted
+constexpr int kRowZero = -2;   // counted position whose row lies outside the cache: zeros
 
 constexpr uint32_t IDESC_QK = idesc_f16(128, NH, false, false);
 constexpr uint32_t IDESC_PV = idesc_f16(128, NH, true, true);
+
+static_assert(SMEM_BYTES <= 232448, "shared memory budget");
 
 __device__ int32_t g_tc_error;  // sticky: DSA_ERR_TIMEOUT when a bounded wait expired
 
@@ -67,114 +81,51 @@ __device__ __forceinline__ float unmono(uint32_t k) {
   return __uint_as_float((k & 0x80000000u) ? (k ^ 0x80000000u) : ~k);
 }
 
-// One warp's share of a tile: rows 16*w + (lane >> 3) + 4*rs (rs = 0..3).
-// Lane l holds, for each of its 4 rows, the nope chunk (l & 7) + 8*j of every
-// 128-wide scale group j (one 16-byte chunk = 16 e4m3 per group), the row's
-// four tile scales, and rope chunk (l & 7). Loads of 8 consecutive lanes cover
-// 128 contiguous bytes of a row.
-struct Tile {
-  uint4 nope[4][4];  // [rs][j]
-  float4 sc[4];      // [rs] scales of groups 0..3
-  uint4 rope[4];     // [rs]
-  int my_valid;      // lanes 0-15: row 16*w + lane is a counted position
-};
-
-__device__ __forceinline__ float sc_of(const float4& s, int j) {
-  return j == 0 ? s.x : (j == 1 ? s.y : (j == 2 ? s.z : s.w));
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t sel) {
+  uint32_t d;
+  asm("prmt.b32 %0, %1, 0, %2;" : "=r"(d) : "r"(a), "r"(sel));
+  return d;
 }
 
-// Resolve + issue the global loads of this warp's 16 rows of a tile.
-__device__ __forceinline__ void load_tile(Tile& T, const SparseMlaArgs& p, int b, int j0, int hi, int seq_len,
-                                          int w, int lane) {
-  int64_t my_row = -1;
-  T.my_valid = 0;
-  if (lane < 16) {
-    const int j = j0 + 16 * w + lane;
-    if (j < hi) {
-      const int pos = p.idx[(int64_t)b * p.idx_stride + j];
-      if (pos >= 0 && pos < seq_len) {
-        T.my_valid = 1;
-        const int blk_i = pos / p.page_size;
-        if (blk_i < p.max_blocks) {
-          const int64_t r = (int64_t)p.bt[(int64_t)b * p.bt_stride + blk_i] * p.page_size + (pos - blk_i * p.page_size);
-          if (r >= 0 && r < p.n_kv_rows) my_row = r * ROW_BYTES;
-        }
-      }
-    }
-  }
-#pragma unroll
-  for (int rs = 0; rs < 4; ++rs) {
-    const int64_t off = __shfl_sync(0xffffffffu, my_row, (lane >> 3) + 4 * rs);
-    if (off >= 0) {
-      const uint8_t* row = p.kv + off;
-#pragma unroll
-      for (int j = 0; j < 4; ++j) T.nope[rs][j] = ldg_nc16(row + 16 * ((lane & 7) + 8 * j));
-      const uint4 s = ldg_nc16(row + 512);
-      T.sc[rs] = make_float4(__uint_as_float(s.x), __uint_as_float(s.y), __uint_as_float(s.z), __uint_as_float(s.w));
-      T.rope[rs] = ldg_nc16(row + 528 + 16 * (lane & 7));
-    } else {
-#pragma unroll
-      for (int j = 0; j < 4; ++j) T.nope[rs][j] = make_uint4(0, 0, 0, 0);
-      T.sc[rs] = make_float4(0.f, 0.f, 0.f, 0.f);
-      T.rope[rs] = make_uint4(0, 0, 0, 0);
-    }
-  }
+// Four e4m3 bytes -> two half2 words holding value/256 each, exactly: each
+// byte is placed in a 16-bit lane with its sign replicated above it (prmt
+// sign-extension selectors), shifted so exponent+mantissa fill fp16 bits
+// 7..13 and the sign lands on bit 15; bit 14 is cleared. e4m3's exponent bias
+// (7) vs fp16's (15) is the 2^-8 factor; e4m3 subnormals become fp16
+// subnormals. Integer ops only (no conversion-pipe instructions).
+__device__ __forceinline__ void e4m3x4_div256(uint32_t w, uint32_t& lo, uint32_t& hi) {
+  lo = (prmt(w, 0x9180u) << 7) & 0xBF80BF80u;
+  hi = (prmt(w, 0xB3A2u) << 7) & 0xBF80BF80u;
 }
 
-// Two e4m3 bytes (in the low byte of each 16-bit half of x) -> half2 holding
-// value/256 exactly: sign to bit 15, exponent+mantissa shifted into the fp16
-// field (e4m3 bias 7 vs fp16 bias 15 is the 2^8 factor; e4m3 subnormals land
-// on fp16 subnormals). Integer ops only, so the conversion stays off the
-// (narrow) conversion pipe.
-__device__ __forceinline__ uint32_t e4m3x2_div256(uint32_t x) {
-  return ((x << 8) & 0x80008000u) | ((x << 7) & 0x3F803F80u);
-}
-
-// e4m3 x 8 (two words) times scale -> 8 fp16 (uint4).
-__device__ __forceinline__ uint4 dequant8(uint32_t w0, uint32_t w1, float sc) {
-  const uint32_t q[4] = {e4m3x2_div256(__byte_perm(w0, 0, 0x4140)), e4m3x2_div256(__byte_perm(w0, 0, 0x4342)),
-                         e4m3x2_div256(__byte_perm(w1, 0, 0x4140)), e4m3x2_div256(__byte_perm(w1, 0, 0x4342))};
-  uint4 o;
+// 16 e4m3 (uint4) times scale -> 16 fp16 (two uint4).
+__device__ __forceinline__ void dequant16(const uint4& r, float sc, uint4& o0, uint4& o1) {
+  uint32_t q[8];
+  e4m3x4_div256(r.x, q[0], q[1]);
+  e4m3x4_div256(r.y, q[2], q[3]);
+  e4m3x4_div256(r.z, q[4], q[5]);
+  e4m3x4_div256(r.w, q[6], q[7]);
   const float s256 = sc * 256.0f;
   if (s256 >= 6.2e-5f && s256 <= 32768.0f) {  // scale*256 and every product stay normal in fp16
     const __half2 s2 = __float2half2_rn(s256);
-    __half2 r[4];
 #pragma unroll
-    for (int e = 0; e < 4; ++e) r[e] = __hmul2(*reinterpret_cast<const __half2*>(&q[e]), s2);
-    o = make_uint4(*reinterpret_cast<uint32_t*>(&r[0]), *reinterpret_cast<uint32_t*>(&r[1]),
-                   *reinterpret_cast<uint32_t*>(&r[2]), *reinterpret_cast<uint32_t*>(&r[3]));
-  } else {
-    uint32_t r[4];
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&q[e]));
-      r[e] = pack_half2(f.x * s256, f.y * s256);
+    for (int e = 0; e < 8; ++e) {
+      const __half2 v = __hmul2(*reinterpret_cast<const __half2*>(&q[e]), s2);
+      q[e] = *reinterpret_cast<const uint32_t*>(&v);
     }
-    o = make_uint4(r[0], r[1], r[2], r[3]);
+  } else {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&q[e]));
+      q[e] = pack_half2(f.x * s256, f.y * s256);
+    }
   }
-  return o;
+  o0 = make_uint4(q[0], q[1], q[2], q[3]);
+  o1 = make_uint4(q[4], q[5], q[6], q[7]);
 }
 
-// Store scale group j (K blocks 2j, 2j+1) of this warp's rows.
-__device__ __forceinline__ void store_group(const Tile& T, uint8_t* sm, int j, int w, int lane) {
-  const int c = (lane & 7) + 8 * j;  // nope chunk: e4m3 values [16c, 16c+16)
-  uint8_t* region = sm + SM_KV + (c >> 2) * KV_REGION;
-  const int c0 = 2 * (c & 3);
-#pragma unroll
-  for (int rs = 0; rs < 4; ++rs) {
-    const int i = 16 * w + (lane >> 3) + 4 * rs;
-    const float sc = sc_of(T.sc[rs], j);
-    *reinterpret_cast<uint4*>(region + sw128_off(i, c0)) = dequant8(T.nope[rs][j].x, T.nope[rs][j].y, sc);
-    *reinterpret_cast<uint4*>(region + sw128_off(i, c0 + 1)) = dequant8(T.nope[rs][j].z, T.nope[rs][j].w, sc);
-  }
-}
-
-__device__ __forceinline__ void store_rope(const Tile& T, uint8_t* sm, uint8_t* valid, int w, int lane) {
-#pragma unroll
-  for (int rs = 0; rs < 4; ++rs)
-    *reinterpret_cast<uint4*>(sm + SM_KV + 8 * KV_REGION + sw128_off(16 * w + (lane >> 3) + 4 * rs, lane & 7)) =
-        T.rope[rs];
-  if (lane < 16) valid[16 * w + lane] = (uint8_t)T.my_valid;
+__device__ __forceinline__ float pick(const float4& s, int j) {
+  return j == 0 ? s.x : (j == 1 ? s.y : (j == 2 ? s.z : s.w));
 }
 
 __device__ __forceinline__ float ex2(float x) {
@@ -183,23 +134,101 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
+// One warp's share of a tile: rows 8*w + (lane >> 3) + 4*rs (rs = 0, 1).
+// Lane l holds, for each of its 2 rows, nope chunk (l & 7) + 8*j of every
+// 128-wide scale group j (16 e4m3 per chunk), the row's four scales, and rope
+// chunk (l & 7); eight consecutive lanes read 128 contiguous bytes of a row.
+struct Tile {
+  uint4 nope[2][4];  // [rs][j]
+  float4 sc[2];
+  uint4 rope[2];
+};
+
+__device__ __forceinline__ int64_t row_offset(const int* table, int i) {
+  const int code = table[i];
+  return code >= 0 ? (int64_t)code * ROW_BYTES : -1;
+}
+
+__device__ __forceinline__ void load_group(Tile& T, const uint8_t* kv, const int* table, int tbase, int j, int w,
+                                           int lane) {
+#pragma unroll
+  for (int rs = 0; rs < 2; ++rs) {
+    const int64_t off = row_offset(table, tbase + ROWS_PER_WARP * w + (lane >> 3) + 4 * rs);
+    T.nope[rs][j] = off >= 0 ? ldg_nc16(kv + off + 16 * ((lane & 7) + 8 * j)) : make_uint4(0, 0, 0, 0);
+  }
+}
+
+__device__ __forceinline__ void load_tail(Tile& T, const uint8_t* kv, const int* table, int tbase, int w, int lane) {
+#pragma unroll
+  for (int rs = 0; rs < 2; ++rs) {
+    const int64_t off = row_offset(table, tbase + ROWS_PER_WARP * w + (lane >> 3) + 4 * rs);
+    if (off >= 0) {
+      const uint4 s = ldg_nc16(kv + off + 512);
+      T.sc[rs] = make_float4(__uint_as_float(s.x), __uint_as_float(s.y), __uint_as_float(s.z), __uint_as_float(s.w));
+      T.rope[rs] = ldg_nc16(kv + off + 528 + 16 * (lane & 7));
+    } else {
+      T.sc[rs] = make_float4(0.f, 0.f, 0.f, 0.f);
+      T.rope[rs] = make_uint4(0, 0, 0, 0);
+    }
+  }
+}
+
+// Store scale group j (K blocks 2j, 2j+1) of this warp's rows.
+__device__ __forceinline__ void store_group(const Tile& T, uint8_t* sm, int j, int w, int lane) {
+  const int c = (lane & 7) + 8 * j;  // nope chunk: e4m3 values [16c, 16c+16)
+  uint8_t* region = sm + SM_KV + (c >> 2) * KV_REGION;
+  const int c0 = 2 * (c & 3);
+#pragma unroll
+  for (int rs = 0; rs < 2; ++rs) {
+    const int i = ROWS_PER_WARP * w + (lane >> 3) + 4 * rs;
+    uint4 o0, o1;
+    dequant16(T.nope[rs][j], pick(T.sc[rs], j), o0, o1);
+    *reinterpret_cast<uint4*>(region + sw128_off(i, c0)) = o0;
+    *reinterpret_cast<uint4*>(region + sw128_off(i, c0 + 1)) = o1;
+  }
+}
+
+__device__ __forceinline__ void store_rope(const Tile& T, uint8_t* sm, int w, int lane) {
+#pragma unroll
+  for (int rs = 0; rs < 2; ++rs)
+    *reinterpret_cast<uint4*>(sm + SM_KV + 8 * KV_REGION +
+                              sw128_off(ROWS_PER_WARP * w + (lane >> 3) + 4 * rs, lane & 7)) = T.rope[rs];
+}
+
+// Row table for slice rows [r0, r0 + n): physical row, kRowZero or kRowSkip.
+__device__ __forceinline__ void resolve_rows(const SparseMlaArgs& p, int b, int seq_len, int r0, int n, int* table) {
+  for (int i = threadIdx.x; i < n; i += NTHREADS) {
+    int code = kRowSkip;
+    const int pos = p.idx[(int64_t)b * p.idx_stride + r0 + i];
+    if (pos >= 0 && pos < seq_len) {
+      code = kRowZero;
+      const int blk_i = pos / p.page_size;
+      if (blk_i < p.max_blocks) {
+        const int64_t r = (int64_t)p.bt[(int64_t)b * p.bt_stride + blk_i] * p.page_size + (pos - blk_i * p.page_size);
+        if (r >= 0 && r < p.n_kv_rows) code = (int)r;
+      }
+    }
+    table[i] = code;
+  }
+}
+
 __global__ void __launch_bounds__(NTHREADS, 1) sparse_mla_decode_tc_kernel(const SparseMlaArgs p, int32_t* err) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_base = smem_u32(smem_raw);
   const uint32_t base = (raw_base + 1023u) & ~1023u;
   uint8_t* sm = smem_raw + (base - raw_base);
+  int* table = reinterpret_cast<int*>(sm + SM_TABLE);
   uint8_t* misc = sm + SM_MISC;
-  // mbarriers: [0..4] kv_full (groups 0..3, rope), [5..8] kv_free (PV tile j), [9] s_full, [10] done
+  // mbarriers: [0..4] kv_full (groups 0..3, rope), [5..8] kv_free (PV value tile j), [9] s_full, [10] done
   uint64_t* mbar = reinterpret_cast<uint64_t*>(misc);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(misc + 96);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(misc + 100);
-  int* ovf = reinterpret_cast<int*>(misc + 104);           // [2][4] per-warp "score above running max" votes
-  int* any_rescale = reinterpret_cast<int*>(misc + 136);   // [2]
-  float* m_ref = reinterpret_cast<float*>(misc + 256);     // [64] running max (log2 units)
-  float* alpha = m_ref + 64;                               // [64] this tile's rescale factors
-  float* tmax = alpha + 64;                                // [2][4][32] per-warp tile maxima
-  float* l_sum = tmax + 256;                               // [64]
-  uint8_t* valid = reinterpret_cast<uint8_t*>(l_sum + 64); // [128]
+  int* ovf = reinterpret_cast<int*>(misc + 128);            // [4 quarters][4 warps] overflow votes
+  int* any_rescale = reinterpret_cast<int*>(misc + 192);    // [4]
+  float* m_ref = reinterpret_cast<float*>(misc + 256);      // [64] running max (log2 units)
+  float* alpha = m_ref + 64;                                // [64] this tile's rescale factors
+  float* tmax = alpha + 64;                                 // [4 quarters][4 warps][16] tile maxima
+  float* l_sum = tmax + 256;                                // [64]
   const uint32_t mb0 = smem_u32(&mbar[0]);
   auto mb_kv_full = [&](int j) { return mb0 + 8u * (uint32_t)j; };
   auto mb_kv_free = [&](int j) { return mb0 + 8u * (uint32_t)(5 + j); };
@@ -212,12 +241,14 @@ __global__ void __launch_bounds__(NTHREADS, 1) sparse_mla_decode_tc_kernel(const
   const int seq_len = p.seq_lens[b];
   const int lo = split * p.span;
   const int hi = min(lo + p.span, p.topk);
-  const int ntiles = hi > lo ? (hi - lo + TM - 1) / TM : 0;
+  const int nrows = max(hi - lo, 0);
+  const int ntiles = (nrows + TM - 1) / TM;
   const bool issuer = threadIdx.x == 0;  // lane 0 of warp 0 issues every MMA
+  constexpr int kTilesPerTable = TABLE_ROWS / TM;
 
   if (warp == 0) {
     if (lane == 0) {
-      for (int j = 0; j < 5; ++j) mbar_init(mb_kv_full(j), NWORK);
+      for (int j = 0; j < 5; ++j) mbar_init(mb_kv_full(j), NWARPS);
       for (int j = 0; j < 4; ++j) mbar_init(mb_kv_free(j), 1);
       mbar_init(mb_s_full, 1);
       mbar_init(mb_done, 1);
@@ -243,6 +274,10 @@ __global__ void __launch_bounds__(NTHREADS, 1) sparse_mla_decode_tc_kernel(const
       m_ref[threadIdx.x] = -1e30f;
       alpha[threadIdx.x] = 1.f;
     }
+    // pad the table so that reads for rows past the slice are "not counted"
+    resolve_rows(p, b, seq_len, lo, min(nrows, TABLE_ROWS), table);
+    for (int i = min(nrows, TABLE_ROWS) + threadIdx.x; i < min(ntiles * TM, TABLE_ROWS); i += NTHREADS)
+      table[i] = kRowSkip;
   }
   fence_proxy_async();
   fence_before_sync();
@@ -250,28 +285,46 @@ __global__ void __launch_bounds__(NTHREADS, 1) sparse_mla_decode_tc_kernel(const
   fence_after_sync();
   const uint32_t tmem = *tmem_slot;
 
-  const int w = warp;                // producer: rows 16*w .. 16*w + 15 of a tile
+  const int w = warp;                // producer: rows 8*w .. 8*w + 7 of a tile
   const int sp = warp & 3;           // TMEM sub-partition: lanes [32*sp, 32*sp+32)
-  const int hh = warp >> 2;          // softmax head half: heads [32*hh, 32*hh+32)
+  const int hq = warp >> 2;          // softmax head quarter: heads [16*hq, 16*hq+16)
   const int row_s = 32 * sp + lane;  // the tile row this thread owns in the softmax
   const uint32_t t_lane = (uint32_t)(32 * sp) << 16;
-  // The running row sums of P live in TMEM columns [L_COL + 32*hh, +32) of
-  // this thread's lane (one latent-row slot x 32 heads), not in registers.
+
   Tile T;
-  if (ntiles > 0) load_tile(T, p, b, lo, hi, seq_len, w, lane);
+  bool ok = true;
+  bool issued = false;
+  bool have_next = false;  // tile t's data was prefetched during iteration t-1
   // Control flow is uniform across the block: after a timed-out wait (`ok`
   // false, abort flag set) every warp still executes the same sequence of
   // barriers and arrivals, and every later wait returns at once.
-  bool ok = true;
-  bool issued = false;
   for (int t = 0; t < ntiles; ++t) {
     const uint32_t ph = t & 1;
+    const int tbase = (t % kTilesPerTable) * TM;  // tile rows in the row table
+    if (!have_next) {
+      if (t > 0) {  // a new table window: resolve it once the previous tile is consumed
+#pragma unroll
+        for (int j = 0; j < 4; ++j) ok = ok && mbar_wait(mb_kv_free(j), ph ^ 1, abort_flag, err, kWaitTimeoutNs);
+        __syncthreads();
+        const int r0 = t * TM;
+        resolve_rows(p, b, seq_len, lo + r0, min(nrows - r0, TABLE_ROWS), table);
+        for (int i = min(nrows - r0, TABLE_ROWS) + threadIdx.x; i < min((ntiles - t) * TM, TABLE_ROWS);
+             i += NTHREADS)
+          table[i] = kRowSkip;
+        __syncthreads();
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) load_group(T, p.kv, table, tbase, j, w, lane);
+      load_tail(T, p.kv, table, tbase, w, lane);
+    }
+    const bool prefetch = (t + 1 < ntiles) && ((t + 1) % kTilesPerTable != 0);
+    const int nbase = ((t + 1) % kTilesPerTable) * TM;
     // ---- store tile t group by group as PV(t-1) releases it; QK(t) follows each group
-    // (unrolled: the tile registers are indexed by the group)
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       if (t > 0) ok = ok && mbar_wait(mb_kv_free(j), ph ^ 1, abort_flag, err, kWaitTimeoutNs);
       if (ok) store_group(T, sm, j, w, lane);
+      if (ok && prefetch) load_group(T, p.kv, table, nbase, j, w, lane);
       fence_proxy_async();
       __syncwarp();
       if (lane == 0) mbar_arrive(mb_kv_full(j));
@@ -292,8 +345,10 @@ __global__ void __launch_bounds__(NTHREADS, 1) sparse_mla_decode_tc_kernel(const
       }
       __syncwarp();
     }
-    // rope group: its region held P^T(t-1), released when all of PV(t-1) is done (kv_free[3])
-    if (ok) store_rope(T, sm, valid, w, lane);
+    // rope group: its region held P^T(t-1), released with the last value tile of PV(t-1)
+    if (ok) store_rope(T, sm, w, lane);
+    if (ok && prefetch) load_tail(T, p.kv, table, nbase, w, lane);
+    have_next = ok && prefetch;
     fence_proxy_async();
     __syncwarp();
     if (lane == 0) mbar_arrive(mb_kv_full(4));
@@ -311,83 +366,87 @@ __global__ void __launch_bounds__(NTHREADS, 1) sparse_mla_decode_tc_kernel(const
       }
     }
     __syncwarp();
-    // ---- next tile's loads stay in flight through softmax(t) and PV(t)
-    if (ok && t + 1 < ntiles) load_tile(T, p, b, lo + (t + 1) * TM, hi, seq_len, w, lane);
 
-    // ---- softmax(t)
+    // ---- softmax(t): this thread = tile row row_s x heads [16*hq, 16*hq+16)
     ok = ok && mbar_wait(mb_s_full, ph, abort_flag, err, kWaitTimeoutNs);
-    __syncthreads();  // validity bytes of tile t (written with the rope group) are visible
     fence_after_sync();
-    float v[32];
-    {
-      uint32_t sreg[32];
-      if (ok) {
-        tmem_ld32(tmem + t_lane + S_COL + 32 * hh, sreg);
-        tmem_wait_ld();
-      } else {
+    const bool vrow = table[tbase + row_s] != kRowSkip;
+    const int hb = 16 * hq;
+    uint32_t s16[16];
+    if (ok) {
+      tmem_ld16(tmem + t_lane + S_COL + hb, s16);
+      tmem_wait_ld();
+    } else {
 #pragma unroll
-        for (int h = 0; h < 32; ++h) sreg[h] = 0u;
-      }
-      const bool vrow = valid[row_s] != 0;
-      bool over = false;
-#pragma unroll
-      for (int h = 0; h < 32; ++h) {
-        v[h] = vrow ? __uint_as_float(sreg[h]) * p.scale_log2 : -INFINITY;
-        over |= v[h] > m_ref[32 * hh + h] + kRescaleThreshold;
-      }
-      const unsigned vote = __ballot_sync(0xffffffffu, over);
-      if (lane == 0) ovf[hh * 4 + sp] = vote != 0u;
+      for (int h = 0; h < 16; ++h) s16[h] = 0u;
     }
-    named_bar(1 + hh, 128);
-    const bool slow = ovf[hh * 4] | ovf[hh * 4 + 1] | ovf[hh * 4 + 2] | ovf[hh * 4 + 3];
+    float pr[16];
+    bool over = false;
+#pragma unroll
+    for (int h4 = 0; h4 < 16; h4 += 4) {
+      const float4 m4 = *reinterpret_cast<const float4*>(m_ref + hb + h4);
+      const float mm[4] = {m4.x, m4.y, m4.z, m4.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float x = (vrow ? __uint_as_float(s16[h4 + e]) * p.scale_log2 : -INFINITY) - mm[e];
+        over |= x > kRescaleThreshold;
+        pr[h4 + e] = ex2(x);
+      }
+    }
+    const unsigned vote = __ballot_sync(0xffffffffu, over);
+    if (lane == 0) ovf[hq * 4 + sp] = vote != 0u;
+    named_bar(1 + hq, 128);
+    const bool slow = (ovf[hq * 4] | ovf[hq * 4 + 1] | ovf[hq * 4 + 2] | ovf[hq * 4 + 3]) != 0;
     if (slow) {
-      // exact tile maxima of this head half; heads whose max grew by more than
-      // 2^8 move their running max and rescale what was accumulated
+      // exact tile maxima of this head quarter; heads whose max grew by more
+      // than 2^8 move their running max and rescale what was accumulated
       uint32_t my_max = 0;
 #pragma unroll
-      for (int h = 0; h < 32; ++h) {
-        const uint32_t wm = __reduce_max_sync(0xffffffffu, monotone32(v[h]));
+      for (int h = 0; h < 16; ++h) {
+        const float v = vrow ? __uint_as_float(s16[h]) * p.scale_log2 : -INFINITY;
+        const uint32_t wm = __reduce_max_sync(0xffffffffu, monotone32(v));
         if (lane == h) my_max = wm;
       }
-      tmax[(hh * 4 + sp) * 32 + lane] = unmono(my_max);
-      named_bar(1 + hh, 128);
+      if (lane < 16) tmax[(hq * 4 + sp) * 16 + lane] = unmono(my_max);
+      named_bar(1 + hq, 128);
       if (sp == 0) {
-        const int head = 32 * hh + lane;
-        float tm = tmax[(hh * 4) * 32 + lane];
-#pragma unroll
-        for (int s = 1; s < 4; ++s) tm = fmaxf(tm, tmax[(hh * 4 + s) * 32 + lane]);
-        const float m_old = m_ref[head];
         float a = 1.f;
-        if (tm > m_old + kRescaleThreshold) {
-          a = ex2(m_old - tm);
-          m_ref[head] = tm;
+        if (lane < 16) {
+          const int head = hb + lane;
+          float tm = tmax[(hq * 4) * 16 + lane];
+#pragma unroll
+          for (int s = 1; s < 4; ++s) tm = fmaxf(tm, tmax[(hq * 4 + s) * 16 + lane]);
+          const float m_old = m_ref[head];
+          if (tm > m_old + kRescaleThreshold) {
+            a = ex2(m_old - tm);
+            m_ref[head] = tm;
+          }
+          alpha[head] = a;
         }
-        alpha[head] = a;
         const unsigned any = __ballot_sync(0xffffffffu, a != 1.f);
-        if (lane == 0) any_rescale[hh] = any != 0u;
+        if (lane == 0) any_rescale[hq] = any != 0u;
       }
-      named_bar(1 + hh, 128);
-      if (ok && any_rescale[hh] && t > 0) {  // O^T columns of this head half, lanes of this sub-partition
+      named_bar(1 + hq, 128);
+      if (ok && any_rescale[hq] && t > 0) {  // O^T columns of this quarter, lanes of this sub-partition
 #pragma unroll 1
-        for (int jj = 0; jj < 8; ++jj) {  // 4 value tiles x 2 groups of 16 head columns
+        for (int j = 0; j < 4; ++j) {
           uint32_t o[16];
-          const uint32_t col = 64 * (jj >> 1) + 32 * hh + 16 * (jj & 1);
-          tmem_ld16(tmem + t_lane + col, o);
+          tmem_ld16(tmem + t_lane + 64 * j + hb, o);
           tmem_wait_ld();
 #pragma unroll
-          for (int h = 0; h < 16; ++h)
-            o[h] = __float_as_uint(__uint_as_float(o[h]) * alpha[32 * hh + 16 * (jj & 1) + h]);
-          tmem_st16(tmem + t_lane + col, o);
+          for (int h = 0; h < 16; ++h) o[h] = __float_as_uint(__uint_as_float(o[h]) * alpha[hb + h]);
+          tmem_st16(tmem + t_lane + 64 * j + hb, o);
         }
         tmem_wait_st();
       }
-    }
-    // P = 2^(v - m) in fp16 into the P^T rows (the rope region, consumed by QK(t));
-    // row sums updated in TMEM
-    uint8_t* preg = sm + SM_KV + 8 * KV_REGION;
 #pragma unroll
-    for (int c2 = 0; c2 < 2; ++c2) {
-      const int hb = 32 * hh + 16 * c2;  // first head of this group
+      for (int h = 0; h < 16; ++h) {
+        const float v = vrow ? __uint_as_float(s16[h]) * p.scale_log2 : -INFINITY;
+        pr[h] = ex2(v - m_ref[hb + h]);
+      }
+    }
+    // row sums (TMEM) and P^T (the rope region, consumed by QK(t))
+    {
       uint32_t l16[16];
       if (ok && t > 0) {
         tmem_ld16(tmem + t_lane + L_COL + hb, l16);
@@ -397,23 +456,17 @@ __global__ void __launch_bounds__(NTHREADS, 1) sparse_mla_decode_tc_kernel(const
         for (int h = 0; h < 16; ++h) l16[h] = 0u;
       }
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {  // 8 heads per 16-byte chunk of the P^T row
-        uint32_t pk[4];
-#pragma unroll
-        for (int e = 0; e < 8; e += 2) {
-          const int h = 16 * c2 + 8 * c + e;  // head index within the half
-          const float p0 = ex2(v[h] - m_ref[32 * hh + h]);
-          const float p1 = ex2(v[h + 1] - m_ref[32 * hh + h + 1]);
-          const int hl = 8 * c + e;
-          const float a0 = slow ? alpha[32 * hh + h] : 1.f, a1 = slow ? alpha[32 * hh + h + 1] : 1.f;
-          l16[hl] = __float_as_uint(__uint_as_float(l16[hl]) * a0 + p0);
-          l16[hl + 1] = __float_as_uint(__uint_as_float(l16[hl + 1]) * a1 + p1);
-          pk[e >> 1] = pack_half2(p0, p1);
-        }
-        *reinterpret_cast<uint4*>(preg + sw128_off(row_s, 4 * hh + 2 * c2 + c)) =
-            make_uint4(pk[0], pk[1], pk[2], pk[3]);
+      for (int h = 0; h < 16; ++h) {
+        const float a = slow ? alpha[hb + h] : 1.f;
+        l16[h] = __float_as_uint(__uint_as_float(l16[h]) * a + pr[h]);
       }
       if (ok) tmem_st16(tmem + t_lane + L_COL + hb, l16);
+      uint8_t* preg = sm + SM_KV + 8 * KV_REGION;
+#pragma unroll
+      for (int c = 0; c < 2; ++c)
+        *reinterpret_cast<uint4*>(preg + sw128_off(row_s, 2 * hq + c)) =
+            make_uint4(pack_half2(pr[8 * c], pr[8 * c + 1]), pack_half2(pr[8 * c + 2], pr[8 * c + 3]),
+                       pack_half2(pr[8 * c + 4], pr[8 * c + 5]), pack_half2(pr[8 * c + 6], pr[8 * c + 7]));
     }
     tmem_wait_st();
     fence_proxy_async();
@@ -442,41 +495,42 @@ __global__ void __launch_bounds__(NTHREADS, 1) sparse_mla_decode_tc_kernel(const
   // every thread reads the same decision.
   const bool live = *abort_flag == 0;
   __syncthreads();
+  const int hb = 16 * hq;
   if (ntiles > 0 && live) {
     fence_after_sync();
     float* lbuf = reinterpret_cast<float*>(sm + SM_KV);  // [64 heads][128 rows]; the tile is dead now
     {
-      uint32_t lr[32];
-      tmem_ld32(tmem + t_lane + L_COL + 32 * hh, lr);
+      uint32_t lr[16];
+      tmem_ld16(tmem + t_lane + L_COL + hb, lr);
       tmem_wait_ld();
 #pragma unroll
-      for (int h = 0; h < 32; ++h) lbuf[(32 * hh + h) * TM + row_s] = __uint_as_float(lr[h]);
+      for (int h = 0; h < 16; ++h) lbuf[(hb + h) * TM + row_s] = __uint_as_float(lr[h]);
     }
     __syncthreads();
     {
-      const int head = threadIdx.x >> 2, q4 = threadIdx.x & 3;
+      const int head = threadIdx.x >> 3, q8 = threadIdx.x & 7;
       float s = 0.f;
-#pragma unroll 8
-      for (int r = 0; r < 32; ++r) s += lbuf[head * TM + 32 * q4 + r];
+#pragma unroll
+      for (int r = 0; r < 16; ++r) s += lbuf[head * TM + 16 * q8 + r];
       s += __shfl_xor_sync(0xffffffffu, s, 1);
       s += __shfl_xor_sync(0xffffffffu, s, 2);
-      if (q4 == 0) l_sum[head] = s;
+      s += __shfl_xor_sync(0xffffffffu, s, 4);
+      if (q8 == 0) l_sum[head] = s;
     }
     __syncthreads();
 #pragma unroll 1
     for (int j = 0; j < 4; ++j) {
-      uint32_t o[32];
-      tmem_ld32(tmem + t_lane + 64 * j + 32 * hh, o);
+      uint32_t o[16];
+      tmem_ld16(tmem + t_lane + 64 * j + hb, o);
       tmem_wait_ld();
       const int d = 128 * j + 32 * sp + lane;
 #pragma unroll 4
-      for (int h = 0; h < 32; ++h) {
-        const int hl = 32 * hh + h;
-        const int head = h0 + hl;
+      for (int h = 0; h < 16; ++h) {
+        const int head = h0 + hb + h;
         if (head >= p.n_head) break;
         const float val = __uint_as_float(o[h]);
         if (p.n_splits == 1) {
-          const float l = l_sum[hl];
+          const float l = l_sum[hb + h];
           const float out = l > 0.f ? val / l : 0.f;
           const int64_t off = ((int64_t)b * p.n_head + head) * DV + d;
           if (p.o_bf16)
