@@ -107,10 +107,14 @@ __device__ __forceinline__ void dequant16(const uint4& r, float sc, uint4& o0, u
   e4m3x4_div256(r.w, q[6], q[7]);
   const float s256 = sc * 256.0f;
   if (s256 >= 6.2e-5f && s256 <= 32768.0f) {  // scale*256 and every product stay normal in fp16
-    const __half2 s2 = __float2half2_rn(s256);
+    // scale = hi + lo in fp16 (hi + lo matches it to ~2^-22), so rounding the
+    // scale leaves no error common to the whole 128-wide group
+    const __half2 s_hi = __float2half2_rn(s256);
+    const __half2 s_lo = __float2half2_rn(s256 - __low2float(s_hi));
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
-      const __half2 v = __hmul2(*reinterpret_cast<const __half2*>(&q[e]), s2);
+      const __half2 x = *reinterpret_cast<const __half2*>(&q[e]);
+      const __half2 v = __hfma2(x, s_lo, __hmul2(x, s_hi));
       q[e] = *reinterpret_cast<const uint32_t*>(&v);
     }
   } else {
@@ -243,7 +247,6 @@ __global__ void __launch_bounds__(NTHREADS, 1) sparse_mla_decode_tc_kernel(const
   const int hi = min(lo + p.span, p.topk);
   const int nrows = max(hi - lo, 0);
   const int ntiles = (nrows + TM - 1) / TM;
-  const bool issuer = threadIdx.x == 0;  // lane 0 of warp 0 issues every MMA
   constexpr int kTilesPerTable = TABLE_ROWS / TM;
 
   if (warp == 0) {
@@ -284,6 +287,11 @@ __global__ void __launch_bounds__(NTHREADS, 1) sparse_mla_decode_tc_kernel(const
   __syncthreads();
   fence_after_sync();
   const uint32_t tmem = *tmem_slot;
+  // Base descriptors; a start-address advance of X bytes adds X >> 4.
+  const uint64_t desc_kv = sw128_desc(base + SM_KV, 16, 1024);                  // KV tile, K-major
+  const uint64_t desc_q = sw128_desc(base + SM_Q, 16, 1024);                    // Q, K-major
+  const uint64_t desc_v = sw128_desc(base + SM_KV, KV_REGION, 1024);            // KV tile, MN-major
+  const uint64_t desc_p = sw128_desc(base + SM_KV + 8 * KV_REGION, KV_REGION, 1024);  // P^T, MN-major
 
   const int w = warp;                // producer: rows 8*w .. 8*w + 7 of a tile
   const int sp = warp & 3;           // TMEM sub-partition: lanes [32*sp, 32*sp+32)
@@ -328,22 +336,23 @@ __global__ void __launch_bounds__(NTHREADS, 1) sparse_mla_decode_tc_kernel(const
       fence_proxy_async();
       __syncwarp();
       if (lane == 0) mbar_arrive(mb_kv_full(j));
-      if (issuer) {
+      if (warp == 0) {  // warp-uniform descriptors; one elected lane issues
         ok = ok && mbar_wait(mb_kv_full(j), ph, abort_flag, err, kWaitTimeoutNs);
+        ok = __all_sync(0xffffffffu, ok);
         if (ok) {
           fence_after_sync();
+          if (elect_one()) {
 #pragma unroll
-          for (int kb = 2 * j; kb < 2 * j + 2; ++kb)
+            for (int kb = 2 * j; kb < 2 * j + 2; ++kb)
 #pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              const uint64_t a = sw128_desc(base + SM_KV + kb * KV_REGION + 32 * k, 16, 1024);
-              const uint64_t bq = sw128_desc(base + SM_Q + kb * Q_REGION + 32 * k, 16, 1024);
-              mma_f16_ss(tmem + S_COL, a, bq, IDESC_QK, (kb | k) != 0);
-            }
+              for (int k = 0; k < 4; ++k)
+                mma_f16_ss(tmem + S_COL, desc_kv + ((kb * KV_REGION + 32 * k) >> 4),
+                           desc_q + ((kb * Q_REGION + 32 * k) >> 4), IDESC_QK, (kb | k) != 0);
+          }
           issued = true;
         }
+        __syncwarp();
       }
-      __syncwarp();
     }
     // rope group: its region held P^T(t-1), released with the last value tile of PV(t-1)
     if (ok) store_rope(T, sm, w, lane);
@@ -352,20 +361,21 @@ __global__ void __launch_bounds__(NTHREADS, 1) sparse_mla_decode_tc_kernel(const
     fence_proxy_async();
     __syncwarp();
     if (lane == 0) mbar_arrive(mb_kv_full(4));
-    if (issuer) {
+    if (warp == 0) {
       ok = ok && mbar_wait(mb_kv_full(4), ph, abort_flag, err, kWaitTimeoutNs);
+      ok = __all_sync(0xffffffffu, ok);
       if (ok) {
         fence_after_sync();
+        if (elect_one()) {
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const uint64_t a = sw128_desc(base + SM_KV + 8 * KV_REGION + 32 * k, 16, 1024);
-          const uint64_t bq = sw128_desc(base + SM_Q + 8 * Q_REGION + 32 * k, 16, 1024);
-          mma_f16_ss(tmem + S_COL, a, bq, IDESC_QK, 1u);
+          for (int k = 0; k < 4; ++k)
+            mma_f16_ss(tmem + S_COL, desc_kv + ((8 * KV_REGION + 32 * k) >> 4),
+                       desc_q + ((8 * Q_REGION + 32 * k) >> 4), IDESC_QK, 1u);
+          mma_commit(mb_s_full);
         }
-        mma_commit(mb_s_full);
       }
+      __syncwarp();
     }
-    __syncwarp();
 
     // ---- softmax(t): this thread = tile row row_s x heads [16*hq, 16*hq+16)
     ok = ok && mbar_wait(mb_s_full, ph, abort_flag, err, kWaitTimeoutNs);
@@ -473,20 +483,23 @@ __global__ void __launch_bounds__(NTHREADS, 1) sparse_mla_decode_tc_kernel(const
     fence_before_sync();
     __syncthreads();
     // ---- O^T += V^T . P^T, one commit per 128-wide value tile
-    if (issuer && ok) {
-      fence_after_sync();
-#pragma unroll 1
-      for (int j = 0; j < 4; ++j) {
+    if (warp == 0) {
+      const bool go = __all_sync(0xffffffffu, ok);
+      if (go) {
+        fence_after_sync();
+        if (elect_one()) {
 #pragma unroll
-        for (int s = 0; s < TM / 16; ++s) {
-          const uint64_t a = sw128_desc(base + SM_KV + 2 * j * KV_REGION + 2048 * s, KV_REGION, 1024);
-          const uint64_t bp = sw128_desc(base + SM_KV + 8 * KV_REGION + 2048 * s, KV_REGION, 1024);
-          mma_f16_ss(tmem + 64 * j, a, bp, IDESC_PV, (t > 0 || s > 0) ? 1u : 0u);
+          for (int j = 0; j < 4; ++j) {
+#pragma unroll
+            for (int s = 0; s < TM / 16; ++s)
+              mma_f16_ss(tmem + 64 * j, desc_v + ((2 * j * KV_REGION + 2048 * s) >> 4), desc_p + ((2048 * s) >> 4),
+                         IDESC_PV, (t > 0 || s > 0) ? 1u : 0u);
+            mma_commit(mb_kv_free(j));
+          }
         }
-        mma_commit(mb_kv_free(j));
       }
+      __syncwarp();
     }
-    __syncwarp();
   }
   // -------------------------------------------------------------- epilogue
   if (ok && ntiles > 0) ok = mbar_wait(mb_kv_free(3), (ntiles - 1) & 1, abort_flag, err, kWaitTimeoutNs);
@@ -573,9 +586,11 @@ __global__ void __launch_bounds__(NTHREADS, 1) sparse_mla_decode_tc_kernel(const
       }
     }
   }
-  // every MMA of this CTA has completed before TMEM is released
-  if (issuer && issued && !live) {
-    mma_commit(mb_done);
+  // every MMA of this CTA has completed before TMEM is released (the elected
+  // lane is the one that issued them: elect.sync is deterministic for a full warp)
+  if (warp == 0 && issued && !live) {
+    if (elect_one()) mma_commit(mb_done);
+    __syncwarp();
     mbar_wait(mb_done, 0, abort_flag, err, kWaitTimeoutNs);
   }
   fence_before_sync();
