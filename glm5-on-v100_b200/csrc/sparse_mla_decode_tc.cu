@@ -332,10 +332,11 @@ __global__ void __launch_bounds__(NTHREADS, 1) sparse_mla_decode_tc_kernel(const
     for (int j = 0; j < 4; ++j) {
       if (t > 0) ok = ok && mbar_wait(mb_kv_free(j), ph ^ 1, abort_flag, err, kWaitTimeoutNs);
       if (ok) store_group(T, sm, j, w, lane);
-      if (ok && prefetch) load_group(T, p.kv, table, nbase, j, w, lane);
       fence_proxy_async();
       __syncwarp();
       if (lane == 0) mbar_arrive(mb_kv_full(j));
+      // next tile's loads go out after the proxy fence so it never waits on them
+      if (ok && prefetch) load_group(T, p.kv, table, nbase, j, w, lane);
       if (warp == 0) {  // warp-uniform descriptors; one elected lane issues
         ok = ok && mbar_wait(mb_kv_full(j), ph, abort_flag, err, kWaitTimeoutNs);
         ok = __all_sync(0xffffffffu, ok);
@@ -356,11 +357,11 @@ __global__ void __launch_bounds__(NTHREADS, 1) sparse_mla_decode_tc_kernel(const
     }
     // rope group: its region held P^T(t-1), released with the last value tile of PV(t-1)
     if (ok) store_rope(T, sm, w, lane);
-    if (ok && prefetch) load_tail(T, p.kv, table, nbase, w, lane);
-    have_next = ok && prefetch;
     fence_proxy_async();
     __syncwarp();
     if (lane == 0) mbar_arrive(mb_kv_full(4));
+    if (ok && prefetch) load_tail(T, p.kv, table, nbase, w, lane);
+    have_next = ok && prefetch;
     if (warp == 0) {
       ok = ok && mbar_wait(mb_kv_full(4), ph, abort_flag, err, kWaitTimeoutNs);
       ok = __all_sync(0xffffffffu, ok);

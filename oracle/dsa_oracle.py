@@ -113,14 +113,22 @@ def dsmla_encode_rows(latent: np.ndarray) -> np.ndarray:
     return out
 
 
-def dsmla_decode_rows(rows: np.ndarray) -> np.ndarray:
-    """[n, 656] uint8 -> [n, 576] float64 dequantised latent (dsa.cu:83-100)."""
+def dsmla_decode_rows(rows: np.ndarray, as_fp16: bool = True) -> np.ndarray:
+    """[n, 656] uint8 -> [n, 576] float64 dequantised latent (dsa.cu:83-100).
+
+    The reference's attention kernels gather each value as e4m3 * scale in
+    f32 and store it as IEEE half before the tensor-core products
+    (dsa.cu:983-1004, :1632-1677), so by default the dequantised values are
+    rounded to fp16 here too; as_fp16=False keeps the f32 products.
+    """
     rows = np.ascontiguousarray(rows, dtype=np.uint8)
     n = rows.shape[0]
     vals = e4m3_decode(rows[:, :512]).reshape(n, 4, 128)
     scale = rows[:, 512:528].copy().view(np.float32).reshape(n, 4).astype(np.float64)
-    # the GPU multiplies in f32: value * scale rounded once to f32
-    nope = (vals * scale[:, :, None]).astype(np.float32).astype(np.float64)
+    nope = (vals * scale[:, :, None]).astype(np.float32)
+    if as_fp16:
+        nope = nope.astype(np.float16)
+    nope = nope.astype(np.float64)
     rope = rows[:, 528:656].copy().view(np.float16).reshape(n, 64).astype(np.float64)
     return np.concatenate([nope.reshape(n, 512), rope], axis=1)
 
