@@ -107,10 +107,12 @@ __device__ __forceinline__ void dequant16(const uint4& r, float sc, uint4& o0, u
   e4m3x4_div256(r.w, q[6], q[7]);
   const float s256 = sc * 256.0f;
   if (s256 >= 6.2e-5f && s256 <= 32768.0f) {  // scale*256 and every product stay normal in fp16
-    // scale = hi + lo in fp16 (hi + lo matches it to ~2^-22), so rounding the
-    // scale leaves no error common to the whole 128-wide group
-    const __half2 s_hi = __float2half2_rn(s256);
-    const __half2 s_lo = __float2half2_rn(s256 - __low2float(s_hi));
+    // scale = hi + lo with hi cut to 7 significant bits: x (an e4m3 value,
+    // 4 significant bits) times hi is exact in fp16, so fma(x, lo, x*hi)
+    // rounds once, like the f32 product rounded to fp16 (up to ~2^-18 ties)
+    const float hi7 = __uint_as_float(__float_as_uint(s256) & 0xFFFF0000u);
+    const __half2 s_hi = __float2half2_rn(hi7);
+    const __half2 s_lo = __float2half2_rn(s256 - hi7);
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
       const __half2 x = *reinterpret_cast<const __half2*>(&q[e]);
