@@ -106,11 +106,12 @@ __device__ __forceinline__ void dequant16(const uint4& r, float sc, uint4& o0, u
   e4m3x4_div256(r.z, q[4], q[5]);
   e4m3x4_div256(r.w, q[6], q[7]);
   const float s256 = sc * 256.0f;
-  if (s256 >= 6.2e-5f && s256 <= 32768.0f) {  // scale*256 and every product stay normal in fp16
+  if (s256 >= 0.0078125f && s256 <= 32768.0f) {  // hi, lo and every product stay normal in fp16
     // scale = hi + lo with hi cut to 7 significant bits: x (an e4m3 value,
-    // 4 significant bits) times hi is exact in fp16, so fma(x, lo, x*hi)
-    // rounds once, like the f32 product rounded to fp16 (up to ~2^-18 ties)
-    const float hi7 = __uint_as_float(__float_as_uint(s256) & 0xFFFF0000u);
+    // 4 significant bits) times hi fits fp16's 11 bits exactly, so
+    // fma(x, lo, x*hi) rounds once, like the f32 product rounded to fp16
+    // (lo carries the rest of the scale to ~2^-18 relative)
+    const float hi7 = __uint_as_float(__float_as_uint(s256) & 0xFFFE0000u);
     const __half2 s_hi = __float2half2_rn(hi7);
     const __half2 s_lo = __float2half2_rn(s256 - hi7);
 #pragma unroll
@@ -339,12 +340,12 @@ __global__ void __launch_bounds__(NTHREADS, 1) sparse_mla_decode_tc_kernel(const
       if (lane == 0) mbar_arrive(mb_kv_full(j));
       // next tile's loads go out after the proxy fence so it never waits on them
       if (ok && prefetch) load_group(T, p.kv, table, nbase, j, w, lane);
-      if (warp == 0) {  // warp-uniform descriptors; one elected lane issues
+      if (warp == 0) {  // warp-uniform descriptors; lane 0 issues
         ok = ok && mbar_wait(mb_kv_full(j), ph, abort_flag, err, kWaitTimeoutNs);
         ok = __all_sync(0xffffffffu, ok);
         if (ok) {
           fence_after_sync();
-          if (elect_one()) {
+          if (lane == 0) {  // the same thread issues and commits every MMA
 #pragma unroll
             for (int kb = 2 * j; kb < 2 * j + 2; ++kb)
 #pragma unroll
@@ -369,7 +370,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) sparse_mla_decode_tc_kernel(const
       ok = __all_sync(0xffffffffu, ok);
       if (ok) {
         fence_after_sync();
-        if (elect_one()) {
+        if (lane == 0) {  // the same thread issues and commits every MMA
 #pragma unroll
           for (int k = 0; k < 4; ++k)
             mma_f16_ss(tmem + S_COL, desc_kv + ((8 * KV_REGION + 32 * k) >> 4),
@@ -490,7 +491,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) sparse_mla_decode_tc_kernel(const
       const bool go = __all_sync(0xffffffffu, ok);
       if (go) {
         fence_after_sync();
-        if (elect_one()) {
+        if (lane == 0) {  // the same thread issues and commits every MMA
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
 #pragma unroll
@@ -589,10 +590,10 @@ __global__ void __launch_bounds__(NTHREADS, 1) sparse_mla_decode_tc_kernel(const
       }
     }
   }
-  // every MMA of this CTA has completed before TMEM is released (the elected
-  // lane is the one that issued them: elect.sync is deterministic for a full warp)
+  // every MMA of this CTA has completed before TMEM is released (a commit
+  // tracks the MMAs of the thread that issues it: lane 0 of warp 0 issued all)
   if (warp == 0 && issued && !live) {
-    if (elect_one()) mma_commit(mb_done);
+    if (lane == 0) mma_commit(mb_done);
     __syncwarp();
     mbar_wait(mb_done, 0, abort_flag, err, kWaitTimeoutNs);
   }

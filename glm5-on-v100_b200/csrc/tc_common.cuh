@@ -143,17 +143,6 @@ __device__ __forceinline__ bool mbar_wait(uint32_t mbar, uint32_t parity, volati
   }
 }
 
-// One lane of a converged warp (the same lane every time for a full warp).
-__device__ __forceinline__ bool elect_one() {
-  uint32_t pred = 0;
-  asm volatile(
-      "{\n\t.reg .pred P1;\n\t"
-      "elect.sync _|P1, 0xffffffff;\n\t"
-      "selp.b32 %0, 1, 0, P1;\n\t}"
-      : "+r"(pred));
-  return pred != 0;
-}
-
 __device__ __forceinline__ void named_bar(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
