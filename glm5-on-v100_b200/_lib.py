@@ -43,6 +43,8 @@ SIGNATURES = {
     "dsa_sparse_mla_decode_workspace_bytes": (_sz, [_i, _i, _i]),
     "dsa_sparse_mla_decode": (_i, [_p, _i, _p, _p, _i, _p, _i, _i64, _i, _p, _i64, _p, _i64, _i, _p,
                                    _i, _i, _i, _d, _p, _sz, _p]),
+    "dsa_sparse_mla_decode_noalloc": (_i, [_p, _i, _p, _p, _i, _p, _i, _i64, _i, _p, _i64, _p, _i64, _i,
+                                           _p, _i, _i, _i, _d, _p]),
     "dsa_indexer_logits": (_i, [_p, _i64, _i, _p, _i, _p, _i, _i64, _i, _p, _i, _p, _i64, _i, _p, _i,
                                 _i, _p, _p]),
     "dsa_indexer_logits_packed": (_i, [_p, _i64, _i, _p, _i, _p, _i, _i64, _i, _p, _i, _p, _i64, _i,

@@ -96,6 +96,28 @@ int dsa_sparse_mla_decode(void* o, int o_dtype, float* lse, const void* q,
                           void* workspace, size_t workspace_bytes,
                           void* stream);
 
+/* dsa_sparse_mla_decode without the workspace: it allocates nothing. It has
+ * no counterpart in the reference. It is for callers that cannot allocate
+ * device memory when they decode, such as an engine whose pool allocator owns
+ * the GPU, or a plugin host that passes only input and output buffers. The
+ * split partial states live in one static 32 MiB array in this library's
+ * device memory, which every GPU that loads the library reserves until the
+ * process exits. A call that needs more than that returns DSA_ERR_WORKSPACE
+ * before it launches anything. All calls share the array. Nothing in it needs
+ * to start at zero, but calls that overlap on the GPU race on it. The first
+ * call on a device looks up the array's address, so make it before any stream
+ * capture begins. Arguments, outputs and status codes are otherwise those of
+ * dsa_sparse_mla_decode. */
+int dsa_sparse_mla_decode_noalloc(void* o, int o_dtype, float* lse,
+                                  const void* q, int q_dtype,
+                                  const void* kv_cache, int kv_format,
+                                  int64_t n_kv_rows, int page_size,
+                                  const int32_t* idx, int64_t idx_stride,
+                                  const int32_t* block_table,
+                                  int64_t bt_stride, int max_blocks,
+                                  const int32_t* seq_lens, int B, int n_head,
+                                  int topk, double scale, void* stream);
+
 /* =====================================================================
  * Lightning-indexer logits.
  * Replaces sm70_indexer_logits (dsa.cu:2626-2764; schema binds
