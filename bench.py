@@ -13,10 +13,20 @@ sets, so consecutive steps read different cache rows: inputs larger than L2).
 `e2e` times the same call through the public op with the step's q and idx
 copied from pinned host memory and o / lse copied back, every step.
 
+Other workloads (BASELINE configs 3 and 4; same JSON contract, value in
+TFLOP/s of the algorithmic FLOPs):
+  indexer_prefill  one causal chunk of 65,536 queries x 65,536 keys, 32
+                   indexer heads x 128, bf16 q and keys, logits then top-2048
+                   per row, in sub-blocks of 4,096 rows.
+  sparse_prefill   16,384 query tokens x 64 heads at the end of a 180,224-token
+                   fp8_ds_mla cache, top-2048 causal positions per token, plus
+                   the indexer-K scatter of the 16,384 new keys.
+
 --impl reference times the reference's own CPU torch path (a port of
-TritonMLAImpl._forward_mqa_torch, oracle/ref_port.py) on the host cores.
-Multi-GPU (torchrun): each rank decodes its own batch of independent rows
-(no data-path collective; weak scaling); timing is the max over ranks.
+TritonMLAImpl._forward_mqa_torch and of the indexer math, oracle/ref_port.py)
+on the host cores. Multi-GPU (torchrun): each rank runs its own copy of the
+workload (independent rows, no data-path collective; weak scaling); timing is
+the max over ranks.
 """
 from __future__ import annotations
 
@@ -29,26 +39,28 @@ import sys
 import threading
 import time
 
-import numpy as np
 import torch
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 ROW_BYTES = 656
-ROOFLINE_NOTE = "of measured"
 
 
 def load_peaks():
+    """(HBM GB/s, bf16 TFLOP/s burst, bf16 TFLOP/s sustained, kind)."""
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
         d = json.load(open(p))
-        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
-    return 6650.0, 1590.0, "fallback"
+        return (float(d["hbm_gbs"]), float(d["bf16_tflops"]),
+                float(d.get("bf16_tflops_sustained", d["bf16_tflops"])), "measured")
+    return 6650.0, 1590.0, 1400.0, "fallback"
 
 
 def profile_traffic(name):
     """Per-launch DRAM bytes recorded in profiles/<name>.md ('traffic_bytes_per_launch: N')."""
+    if name is None:
+        return None
     p = os.path.join(ROOT, "profiles", name + ".md")
     if not os.path.exists(p):
         return None
@@ -150,11 +162,53 @@ def barrier(world):
         dist.barrier()
 
 
+def causal_topk_positions(n_rows, lens, K, dev, g, chunk=512):
+    """[n_rows, K] int32: K distinct uniform-random positions < lens[r], sorted."""
+    out = torch.empty(n_rows, K, dtype=torch.int32, device=dev)
+    S = int(lens.max())
+    pos = torch.arange(S, device=dev)
+    for r0 in range(0, n_rows, chunk):
+        r1 = min(n_rows, r0 + chunk)
+        u = torch.rand(r1 - r0, S, device=dev, generator=g)
+        u.masked_fill_(pos.view(1, S) >= lens[r0:r1].view(-1, 1), -1.0)
+        out[r0:r1] = torch.sort(u.topk(K, dim=1).indices, dim=1).values.to(torch.int32)
+        del u
+    return out
+
+
+def random_dsmla_cache(nb, page, dev, g):
+    kv = torch.randint(0, 256, (nb, page, ROW_BYTES), dtype=torch.uint8, device=dev, generator=g)
+    codes = kv[..., :512]
+    codes[(codes & 0x7F) == 0x7F] = 0x7E
+    sc = (torch.rand(nb, page, 4, device=dev, generator=g) + 0.5) / 448.0
+    kv[..., 512:528] = sc.view(torch.uint8).view(nb, page, 16)
+    kv[..., 528:656] = torch.randn(nb, page, 64, device=dev, generator=g).to(torch.float16).view(
+        torch.uint8).view(nb, page, 128)
+    return kv
+
+
 # --------------------------------------------------------------- workloads
-class DecodeWorkload:
+class Workload:
+    """One benchmark configuration. `units_per_step` is in the numerator of
+    `unit` (rows for tok/s, TFLOP for TFLOP/s)."""
+
+    nsets = 1
+    data = "synthetic (seeded)"
+    traffic_profile = None
+
+    def roofline_part(self):
+        """None, or (graph-capturable callable, its algorithmic amount) for the
+        dominant kernel when the step holds more than that kernel."""
+        return None
+
+
+class DecodeWorkload(Workload):
     metric = "sparse MLA decode tok/s/GPU @128k ctx (HBM % peak)"
     unit = "tok/s"
+    data = "synthetic (seeded random fp8_ds_mla cache, N(0,1) q)"
+    traffic_profile = "sparse_mla_decode_b64_ctx128k"
     B, H, S, PAGE, TOPK, NSETS = 64, 64, 131072, 64, 2048, 8
+    nsets = NSETS
     scale = 1.0 / (192 ** 0.5)
     bytes_per_row = TOPK * ROW_BYTES + TOPK * 4 + H * 576 * 2 + H * 512 * 2 + H * 4  # 1,491,200
 
@@ -167,14 +221,7 @@ class DecodeWorkload:
     def setup(self, dev, seed):
         g = torch.Generator(device=dev).manual_seed(seed)
         nb = self.B * (self.S // self.PAGE)
-        kv = torch.randint(0, 256, (nb, self.PAGE, ROW_BYTES), dtype=torch.uint8, device=dev, generator=g)
-        codes = kv[..., :512]
-        codes[(codes & 0x7F) == 0x7F] = 0x7E
-        sc = (torch.rand(nb, self.PAGE, 4, device=dev, generator=g) + 0.5) / 448.0
-        kv[..., 512:528] = sc.view(torch.uint8).view(nb, self.PAGE, 16)
-        kv[..., 528:656] = torch.randn(nb, self.PAGE, 64, device=dev, generator=g).to(torch.float16).view(
-            torch.uint8).view(nb, self.PAGE, 128)
-        self.kv = kv
+        self.kv = random_dsmla_cache(nb, self.PAGE, dev, g)
         self.bt = torch.randperm(nb, device=dev, generator=g).view(self.B, -1).to(torch.int32)
         self.seq = torch.full((self.B,), self.S, dtype=torch.int32, device=dev)
         self.q = [torch.randn(self.B, self.H, 576, device=dev, generator=g).to(torch.bfloat16)
@@ -197,6 +244,10 @@ class DecodeWorkload:
 
     def algorithmic(self):
         return self.B * self.bytes_per_row, "GB/s", "hbm"
+
+    def roofline_note(self, kind):
+        return (f"peak {kind} HBM copy; achieved = {self.bytes_per_row} B/row x {self.B} rows per launch / "
+                f"CUDA-event time of the op (decode kernel + merge)")
 
     def e2e_setup(self, dev):
         self.h_q = [t.cpu().pin_memory() for t in self.q]
@@ -238,45 +289,292 @@ class DecodeWorkload:
 
         sparse_decode_cpu(self.c_q, self.c_kv, self.c_idx, self.c_bt, self.c_seq, self.PAGE, self.scale)
 
+    def cpu_units(self):
+        return self.cpu_rows
+
+    def cpu_sample(self, steps):
+        return (f"{steps} steps x {self.cpu_rows} rows of the same workload through the reference torch decode path "
+                f"(oracle/ref_port.py, fp8 rows dequantised on the host)")
+
+
+class IndexerPrefillWorkload(Workload):
+    """one causal chunk, logits then top-K per row."""
+
+    metric = "indexer prefill TFLOPS (causal QK FLOPs, logits + top-2048)"
+    unit = "TFLOP/s"
+    data = "synthetic (seeded N(0,1) bf16 q and keys, w ~ N(0, 1/32))"
+    N, HI, HD, PAGE, TOPK, SUB = 65536, 32, 128, 64, 2048, 4096
+
+    def flops(self, rows_lens):
+        return 2.0 * self.HD * self.HI * float(rows_lens)
+
+    def config(self):
+        return {"workload": "indexer_prefill", "queries": self.N, "keys": self.N, "indexer_heads": self.HI,
+                "head_dim": self.HD, "topk": self.TOPK, "page": self.PAGE, "q_dtype": "bf16", "k_cache": "bf16",
+                "w_dtype": "fp16", "sub_block_rows": self.SUB, "causal": True,
+                "flop_convention": "2*128*32*N(N+1)/2 causal pairs (QK only)",
+                "l2": "inputs larger than L2 (q 512 MB, scores 1 GB per sub-block)"}
+
+    def setup(self, dev, seed):
+        g = torch.Generator(device=dev).manual_seed(seed)
+        nb = self.N // self.PAGE
+        self.k_cache = torch.randn(nb, self.PAGE, self.HD, device=dev, generator=g).to(torch.bfloat16)
+        bt_row = torch.randperm(nb, device=dev, generator=g).to(torch.int32)
+        self.bt = bt_row.view(1, nb).expand(self.SUB, nb).contiguous()
+        self.q = torch.randn(self.N, self.HI, self.HD, device=dev, generator=g).to(torch.bfloat16)
+        self.w = (torch.randn(self.N, self.HI, device=dev, generator=g) / (self.HI ** 0.5)).to(torch.float16)
+        self.lens = torch.arange(1, self.N + 1, dtype=torch.int32, device=dev)
+        self.score = torch.empty(self.SUB, self.N, dtype=torch.float32, device=dev)
+        self.idx = torch.empty(self.N, self.TOPK, dtype=torch.int32, device=dev)
+        self.ws = torch.empty(1, dtype=torch.uint8, device=dev)
+        self._bt_row = bt_row
+
+    def _logits(self, dsa, q, w, r0, r1):
+        dsa.sm70_indexer_logits(self.score[: r1 - r0, :r1], q[r0:r1], self.k_cache, w[r0:r1],
+                                self.bt[: r1 - r0], self.lens[r0:r1], None)
+
+    def step_on(self, dsa, q, w, idx):
+        for r0 in range(0, self.N, self.SUB):
+            r1 = min(self.N, r0 + self.SUB)
+            self._logits(dsa, q, w, r0, r1)
+            dsa.persistent_topk(self.score[: r1 - r0, :r1], self.lens[r0:r1], idx[r0:r1], self.ws, self.TOPK, r1)
+
+    def step(self, dsa, i):
+        self.step_on(dsa, self.q, self.w, self.idx)
+
+    def units_per_step(self):
+        return self.flops(self.N * (self.N + 1) // 2) / 1e12
+
+    def launches_per_step(self, dsa):
+        return 2 * ((self.N + self.SUB - 1) // self.SUB)
+
+    def algorithmic(self):
+        return self.flops(self.N * (self.N + 1) // 2), "TFLOP/s", "tensor"
+
+    def roofline_part(self):
+        def logits_only(dsa):
+            for r0 in range(0, self.N, self.SUB):
+                self._logits(dsa, self.q, self.w, r0, min(self.N, r0 + self.SUB))
+
+        return logits_only, self.flops(self.N * (self.N + 1) // 2)
+
+    def roofline_note(self, kind):
+        return (f"peak {kind} bf16 dense (sustained); achieved = causal QK FLOPs / CUDA-event time of the "
+                f"{(self.N + self.SUB - 1) // self.SUB} logits launches alone (top-k excluded)")
+
+    def e2e_setup(self, dev):
+        self.h_q = self.q.cpu().pin_memory()
+        self.h_w = self.w.cpu().pin_memory()
+        self.h_idx = torch.empty(self.idx.shape, dtype=torch.int32).pin_memory()
+        self.d_q = torch.empty_like(self.q)
+        self.d_w = torch.empty_like(self.w)
+        return self.h_q.numel() * 2 + self.h_w.numel() * 2, self.h_idx.numel() * 4
+
+    def e2e_step(self, dsa, i):
+        self.d_q.copy_(self.h_q, non_blocking=True)
+        self.d_w.copy_(self.h_w, non_blocking=True)
+        self.step_on(dsa, self.d_q, self.d_w, self.idx)
+        self.h_idx.copy_(self.idx, non_blocking=True)
+
+    def cpu_setup(self, rows):
+        g = torch.Generator().manual_seed(7)
+        # rows spread over the chunk, so the sample has the chunk's mean causal length
+        self.c_rows = torch.linspace(self.N // (2 * rows), self.N - 1 - self.N // (2 * rows), rows).long()
+        self.c_k = torch.randn(self.N, self.HD, generator=g).to(torch.bfloat16)
+        self.c_q = torch.randn(rows, self.HI, self.HD, generator=g).to(torch.bfloat16)
+        self.c_w = (torch.randn(rows, self.HI, generator=g) / (self.HI ** 0.5)).to(torch.float16)
+        self.c_lens = self.c_rows + 1
+
+    def cpu_step(self):
+        from oracle.ref_port import indexer_prefill_cpu
+
+        indexer_prefill_cpu(self.c_q, self.c_k, self.c_w, self.c_lens, self.TOPK)
+
+    def cpu_units(self):
+        return self.flops(int(self.c_lens.sum())) / 1e12
+
+    def cpu_sample(self, steps):
+        return (f"{steps} steps x {len(self.c_rows)} query rows spread over the chunk (logits over their causal "
+                f"keys + torch.topk, oracle/ref_port.py)")
+
+
+class SparsePrefillWorkload(Workload):
+    """sparse prefill attention + indexer-K scatter."""
+
+    metric = "sparse prefill attention TFLOPS (top-2048, 64 heads)"
+    unit = "TFLOP/s"
+    data = "synthetic (seeded random fp8_ds_mla cache, N(0,1) bf16 q and k)"
+    T, H, S, PAGE, TOPK = 16384, 64, 180224, 64, 2048
+    scale = 1.0 / (192 ** 0.5)
+
+    def flops(self, rows):
+        return 2.0 * rows * self.H * self.TOPK * (576 + 512)
+
+    def config(self):
+        return {"workload": "sparse_prefill", "queries": self.T, "heads": self.H, "ctx": self.S, "topk": self.TOPK,
+                "page": self.PAGE, "kv_cache": "fp8_ds_mla", "q_dtype": "bf16", "o_dtype": "bf16",
+                "k_store": f"{self.T} x 128 bf16 rows into random slots of a bf16 indexer-K cache",
+                "l2": "inputs larger than L2 (q 1.2 GB, o 1 GB); the 118 MB latent cache itself stays L2-resident "
+                      "as in the real layer"}
+
+    def setup(self, dev, seed):
+        g = torch.Generator(device=dev).manual_seed(seed)
+        nb = self.S // self.PAGE
+        self.kv = random_dsmla_cache(nb, self.PAGE, dev, g)
+        bt_row = torch.randperm(nb, device=dev, generator=g).to(torch.int32)
+        self.bt = bt_row.view(1, nb).expand(self.T, nb).contiguous()
+        self.seq = torch.arange(self.S - self.T + 1, self.S + 1, dtype=torch.int32, device=dev)
+        self.idx = causal_topk_positions(self.T, self.seq, self.TOPK, dev, g)
+        self.q = torch.randn(self.T, self.H, 576, device=dev, generator=g).to(torch.bfloat16)
+        self.o = torch.empty(self.T, self.H, 512, dtype=torch.bfloat16, device=dev)
+        self.lse = torch.empty(self.T, self.H, dtype=torch.float32, device=dev)
+        self.k_cache = torch.zeros(nb, self.PAGE, 128, dtype=torch.bfloat16, device=dev)
+        self.k_new = torch.randn(self.T, 128, device=dev, generator=g).to(torch.bfloat16)
+        self.slots = torch.randperm(self.S, device=dev, generator=g)[: self.T].to(torch.int32)
+
+    def _attention(self, dsa, q, idx):
+        dsa.sm70_sparse_mla_decode(self.o, self.lse, q, self.kv, idx, self.bt, self.seq, self.scale)
+
+    def step_on(self, dsa, q, idx, k_new):
+        dsa.sm70_indexer_k_store(self.k_cache, k_new, self.slots)
+        self._attention(dsa, q, idx)
+
+    def step(self, dsa, i):
+        self.step_on(dsa, self.q, self.idx, self.k_new)
+
+    def units_per_step(self):
+        return self.flops(self.T) / 1e12
+
+    def launches_per_step(self, dsa):
+        ws = dsa._lib.lib().dsa_sparse_mla_decode_workspace_bytes(self.T, self.H, self.TOPK)
+        return 2 + (1 if ws else 0)
+
+    def algorithmic(self):
+        return self.flops(self.T), "TFLOP/s", "tensor"
+
+    def roofline_part(self):
+        return (lambda dsa: self._attention(dsa, self.q, self.idx)), self.flops(self.T)
+
+    def roofline_note(self, kind):
+        return (f"peak {kind} bf16 dense (sustained); achieved = 2*T*H*K*(576+512) FLOPs / CUDA-event time of "
+                f"the attention launch alone (K scatter excluded)")
+
+    def e2e_setup(self, dev):
+        self.h_q = self.q.cpu().pin_memory()
+        self.h_idx = self.idx.cpu().pin_memory()
+        self.h_k = self.k_new.cpu().pin_memory()
+        self.h_o = torch.empty(self.o.shape, dtype=self.o.dtype).pin_memory()
+        self.h_lse = torch.empty(self.lse.shape, dtype=self.lse.dtype).pin_memory()
+        self.d_q, self.d_idx, self.d_k = (torch.empty_like(self.q), torch.empty_like(self.idx),
+                                          torch.empty_like(self.k_new))
+        h2d = self.h_q.numel() * 2 + self.h_idx.numel() * 4 + self.h_k.numel() * 2
+        return h2d, self.h_o.numel() * 2 + self.h_lse.numel() * 4
+
+    def e2e_step(self, dsa, i):
+        self.d_q.copy_(self.h_q, non_blocking=True)
+        self.d_idx.copy_(self.h_idx, non_blocking=True)
+        self.d_k.copy_(self.h_k, non_blocking=True)
+        self.step_on(dsa, self.d_q, self.d_idx, self.d_k)
+        self.h_o.copy_(self.o, non_blocking=True)
+        self.h_lse.copy_(self.lse, non_blocking=True)
+
+    def cpu_setup(self, rows):
+        g = torch.Generator().manual_seed(7)
+        self.cpu_rows = rows
+        # the sampled rows read from a cache of their own, the full context long
+        nb = self.S // self.PAGE
+        self.c_kv = torch.randint(0, 256, (nb * self.PAGE, ROW_BYTES), dtype=torch.uint8, generator=g)
+        codes = self.c_kv[:, :512]
+        codes[(codes & 0x7F) == 0x7F] = 0x7E
+        self.c_kv[:, 512:528] = ((torch.rand(nb * self.PAGE, 4, generator=g) + 0.5) / 448.0).view(torch.uint8)
+        self.c_kv[:, 528:656] = torch.randn(nb * self.PAGE, 64, generator=g).to(torch.float16).view(torch.uint8)
+        self.c_bt = torch.randperm(nb, generator=g).to(torch.int32).view(1, nb).expand(rows, nb).contiguous()
+        self.c_seq = torch.arange(self.S - rows + 1, self.S + 1, dtype=torch.int32)
+        self.c_q = torch.randn(rows, self.H, 576, generator=g).to(torch.bfloat16)
+        self.c_idx = torch.sort(torch.rand(rows, self.S - rows, generator=g).topk(self.TOPK, dim=1).indices,
+                                dim=1).values.to(torch.int32)
+
+    def cpu_step(self):
+        from oracle.ref_port import sparse_decode_cpu
+
+        sparse_decode_cpu(self.c_q, self.c_kv, self.c_idx, self.c_bt, self.c_seq, self.PAGE, self.scale)
+
+    def cpu_units(self):
+        return self.flops(self.cpu_rows) / 1e12
+
+    def cpu_sample(self, steps):
+        return (f"{steps} steps x {self.cpu_rows} query rows through the reference torch decode path "
+                f"(oracle/ref_port.py, fp8 rows dequantised on the host; K scatter not included)")
+
+
+WORKLOADS = {"decode": DecodeWorkload, "indexer_prefill": IndexerPrefillWorkload,
+             "sparse_prefill": SparsePrefillWorkload}
+
+
+def capture(fn, stream):
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        fn()
+    return g
+
+
+def time_graphs(graphs, steps, stream):
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        start.record(stream)
+        for i in range(steps):
+            graphs[i % len(graphs)].replay()
+        stop.record(stream)
+        stop.synchronize()
+    return start.elapsed_time(stop)
+
 
 def run_ours(args, world, rank, local):
     dsa = importlib.import_module("glm5-on-v100_b200")
     dev = torch.device("cuda", local)
-    wl = DecodeWorkload()
+    wl = WORKLOADS[args.workload]()
     wl.setup(dev, seed=1234 + rank)
-    hbm_peak, tf_peak, peak_kind = load_peaks()
+    hbm_peak, tf_burst, tf_sustained, peak_kind = load_peaks()
 
     stream = torch.cuda.Stream(dev)
-    graphs = []
     with torch.cuda.stream(stream):
         for i in range(args.warmup):
             wl.step(dsa, i)
         stream.synchronize()
-        for k in range(wl.NSETS):
-            g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g, stream=stream):
-                wl.step(dsa, k)
-            graphs.append(g)
+        graphs = [capture(lambda k=k: wl.step(dsa, k), stream) for k in range(wl.nsets)]
         for i in range(max(3, args.warmup)):
-            graphs[i % wl.NSETS].replay()
+            graphs[i % wl.nsets].replay()
     torch.cuda.synchronize()
 
-    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier(world)
     torch.cuda.synchronize()
     sampler = ClockSampler(torch.cuda.current_device())
-    with sampler, torch.cuda.stream(stream):
-        start.record(stream)
-        for i in range(args.steps):
-            graphs[i % wl.NSETS].replay()
-        stop.record(stream)
-        stop.synchronize()
+    with sampler:
+        ms = time_graphs(graphs, args.steps, stream)
     torch.cuda.synchronize()
     barrier(world)
-    ms = max_over_ranks(start.elapsed_time(stop), world)
+    ms = max_over_ranks(ms, world)
     ms_per_step = ms / args.steps
-    units = wl.units_per_step() * args.steps * world
-    value = units / (ms / 1e3)
+    value = wl.units_per_step() * args.steps * world / (ms / 1e3)
+
+    # the dominant kernel alone, where the step holds more than it
+    part = wl.roofline_part()
+    alg, unit, bound = wl.algorithmic()
+    if part is not None:
+        fn, alg = part
+        with torch.cuda.stream(stream):
+            pg = [capture(lambda: fn(dsa), stream)]
+            pg[0].replay()
+        torch.cuda.synchronize()
+        part_steps = max(3, min(args.steps, 20))
+        part_ms = max_over_ranks(time_graphs(pg, part_steps, stream), world) / part_steps
+        pg.clear()
+    else:
+        part_ms = ms_per_step
+    if unit == "GB/s":
+        achieved, peak = alg / (part_ms / 1e3) / 1e9, hbm_peak
+    else:
+        achieved, peak = alg / (part_ms / 1e3) / 1e12, tf_sustained
 
     # end to end through the public op with host buffers
     e2e = None
@@ -287,30 +585,26 @@ def run_ours(args, world, rank, local):
         torch.cuda.synchronize()
         barrier(world)
         e_start, e_stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e_steps = args.steps if args.workload == "decode" else max(3, min(args.steps, 10))
         e_start.record()
-        for i in range(args.steps):
+        for i in range(e_steps):
             wl.e2e_step(dsa, i)
         e_stop.record()
         e_stop.synchronize()
         barrier(world)
         e_ms = max_over_ranks(e_start.elapsed_time(e_stop), world)
-        e2e = {"value": wl.units_per_step() * args.steps * world / (e_ms / 1e3), "unit": wl.unit,
+        e2e = {"value": wl.units_per_step() * e_steps * world / (e_ms / 1e3), "unit": wl.unit,
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h}
 
-    alg, unit, bound = wl.algorithmic()
-    achieved = alg / (ms_per_step / 1e3) / 1e9
-    traffic = profile_traffic("sparse_mla_decode_b64_ctx128k")
     line = {
         "metric": wl.metric, "value": value, "unit": wl.unit, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded random fp8_ds_mla cache, N(0,1) q)",
-        "config": dict(wl.config(), parallelism=f"dp{world} (independent rows per rank)"),
+        "vs_baseline": None, "dtype": "bf16", "data": wl.data,
+        "config": dict(wl.config(), parallelism=f"dp{world} (independent work per rank)"),
         "e2e": e2e,
         "gpu_launches": args.steps * wl.launches_per_step(dsa),
-        "roofline": {"bound": bound, "achieved": achieved, "peak": hbm_peak, "unit": unit,
-                     "frac": achieved / hbm_peak, "traffic": traffic,
-                     "note": f"peak {peak_kind} HBM copy; achieved = {wl.bytes_per_row} B/row x {wl.B} rows "
-                             f"per launch / CUDA-event time of the op (decode kernel + merge)"},
+        "roofline": {"bound": bound, "achieved": achieved, "peak": peak, "unit": unit, "frac": achieved / peak,
+                     "traffic": profile_traffic(wl.traffic_profile), "note": wl.roofline_note(peak_kind)},
         "clocks": sampler.summary(),
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -331,18 +625,17 @@ def cpu_baseline(wl, args, steps=None, rows=None):
     for _ in range(steps):
         wl.cpu_step()
     dt = time.perf_counter() - t0
-    return {"value": rows * steps / dt, "unit": wl.unit, "cores": torch.get_num_threads(), "kind": "port",
-            "sample": f"{steps} steps x {rows} rows of the same workload through the reference torch decode path "
-                      f"(oracle/ref_port.py, fp8 rows dequantised on the host)"}
+    return {"value": wl.cpu_units() * steps / dt, "unit": wl.unit, "cores": torch.get_num_threads(), "kind": "port",
+            "sample": wl.cpu_sample(steps)}
 
 
 def run_reference(args, world, rank):
     if rank != 0:
         return
-    wl = DecodeWorkload()
+    wl = WORKLOADS[args.workload]()
     steps, rows = args.steps, args.cpu_rows
     cb = cpu_baseline(wl, args, steps=steps, rows=rows)
-    ms_per_step = 1e3 * rows / cb["value"]
+    ms_per_step = 1e3 * wl.cpu_units() / cb["value"]
     line = {
         "metric": wl.metric, "value": cb["value"], "unit": wl.unit, "n_gpus": world, "steps": steps,
         "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
@@ -360,14 +653,17 @@ def main():
     ap.add_argument("--steps", type=int, default=400)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--cpu-rows", type=int, default=8, help="rows per CPU-baseline step")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="decode")
+    ap.add_argument("--cpu-rows", type=int, default=None, help="rows per CPU-baseline step")
     ap.add_argument("--cpu-steps", type=int, default=5)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
     ap.add_argument("--ctx", type=int, default=DecodeWorkload.S,
-                    help="context length (smaller values make the ncu profiling case)")
+                    help="decode context length (smaller values make the ncu profiling case)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    if args.cpu_rows is None:
+        args.cpu_rows = {"decode": 8, "indexer_prefill": 8, "sparse_prefill": 8}[args.workload]
     DecodeWorkload.S = args.ctx
     world, rank, local = dist_setup(args)
     try:

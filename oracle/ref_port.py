@@ -61,3 +61,24 @@ def sparse_decode_cpu(q, kv_u8_flat, idx, block_table, seq_lens, page, scale):
     rows = dequant_dsmla(kv_u8_flat.index_select(0, sel))
     local_bt = torch.arange(sel.numel()).view(B, -1)
     return forward_mqa_torch(q, rows, local_bt, counts, 1, scale)
+
+
+def indexer_prefill_cpu(q, k_rows, w, lens, K):
+    """Indexer prefill on the host: score[i, p] = sum_h w[i,h] * relu(q[i,h,:] . k_p)
+    for p < lens[i] (csrc/attention/sm70_mla_decode.cu:132-149, :332-344),
+    then the per-row top-K positions (torch.topk, the selection the reference's
+    torch shard-merge epilogue uses, reference/sparse_attn_indexer.py:1020).
+
+    q [n, Hi, 128], k_rows [max_len, 128] (the request's keys in position
+    order), w [n, Hi], lens [n]. The reference has no CPU implementation of
+    this step (its logits are SM70 CUDA kernels), so this is a restatement.
+    """
+    out = torch.full((q.shape[0], K), -1, dtype=torch.int32)
+    kf = k_rows.float()
+    for i in range(q.shape[0]):
+        n = int(lens[i])
+        s = torch.relu(q[i].float() @ kf[:n].T)          # [Hi, n]
+        score = (w[i].float().view(-1, 1) * s).sum(0)      # [n]
+        k = min(K, n)
+        out[i, :k] = torch.topk(score, k).indices.sort().values.to(torch.int32)
+    return out
