@@ -21,6 +21,7 @@
 // fp8 key rows (128 e4m3 | f32 scale) are expanded exactly to fp16 and the
 // per-key scale is applied to the dot product (scale > 0 commutes with relu).
 #include "common.cuh"
+#include "indexer_tc.cuh"
 
 namespace dsa {
 namespace {
@@ -453,6 +454,26 @@ int run_logits(LogitsParams p, int k_format, int page_size, bool use_rows, cudaS
     else
       launch_rows<K_F16, false>(p, mt, s);
     return check_launch("indexer_rows_kernel");
+  }
+  if (!p.packed && indexer_tc_eligible(k_format, p.q_bf16, page_size, p.n_ihead, p.n_kv_rows, p.B, p.max_kv)) {
+    IndexerTcArgs t{};
+    t.score = p.score;
+    t.score_stride = p.score_stride;
+    t.max_kv = p.max_kv;
+    t.q = p.q;
+    t.q_bf16 = p.q_bf16;
+    t.n_ihead = p.n_ihead;
+    t.B = p.B;
+    t.k = p.k;
+    t.n_kv_rows = p.n_kv_rows;
+    t.page_size = page_size;
+    t.w = p.w;
+    t.w_dtype = p.w_dtype;
+    t.bt = p.bt;
+    t.bt_stride = p.bt_stride;
+    t.max_blocks = p.max_blocks;
+    t.seq_lens = p.seq_lens;
+    return launch_indexer_logits_tc(t, s);
   }
   if (k_format == DSA_FP8_IDXK)
     launch_tiles<K_FP8, false>(p, s);

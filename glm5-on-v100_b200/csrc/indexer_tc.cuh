@@ -1,0 +1,33 @@
+// Internal interface of the tensor-core (tcgen05) indexer-logits kernel.
+#pragma once
+
+#include "common.cuh"
+
+namespace dsa {
+
+struct IndexerTcArgs {
+  float* score;
+  int64_t score_stride;
+  int max_kv;
+  const void* q;       // [B, n_ihead, 128], same 16-bit type as the cache
+  int q_bf16;
+  int n_ihead;
+  int B;
+  const void* k;       // [n_kv_rows / page, page, 128] f16 / bf16
+  int64_t n_kv_rows;
+  int page_size;
+  const void* w;       // [B, n_ihead]
+  int w_dtype;
+  const int32_t* bt;   // the first row of each 128-row tile serves the tile
+  int64_t bt_stride;
+  int max_blocks;
+  const int32_t* seq_lens;
+};
+
+// True when the tcgen05 kernel serves this call (16-bit cache of q's type,
+// page >= 8, unpacked q); the caller keeps the mma.sync kernel otherwise.
+bool indexer_tc_eligible(int k_format, int q_bf16, int page_size, int n_ihead, int64_t n_kv_rows, int B,
+                         int max_kv);
+int launch_indexer_logits_tc(const IndexerTcArgs& a, cudaStream_t s);
+
+}  // namespace dsa

@@ -33,5 +33,8 @@ int tc_choose_splits(int B, int head_tiles, int topk, int nsm);
 int launch_sparse_mla_tc(const SparseMlaArgs& a, cudaStream_t s);
 // Merge per-slice partial states into o / lse (defined with the v1 kernel).
 int launch_sparse_mla_merge(const SparseMlaArgs& a, cudaStream_t s);
+// Device address of the sticky status word that every tensor-core kernel of
+// this library sets on a timed-out wait (read by dsa_device_error).
+int tc_error_word(int dev, int32_t** out);
 
 }  // namespace dsa

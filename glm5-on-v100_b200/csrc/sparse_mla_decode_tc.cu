@@ -660,6 +660,13 @@ int launch_sparse_mla_tc(const SparseMlaArgs& a, cudaStream_t s) {
   return check_launch("sparse_mla_decode_tc_kernel");
 }
 
+int tc_error_word(int dev, int32_t** out) {
+  const int st = ensure_setup(dev);
+  if (st != DSA_OK) return st;
+  *out = g_err_ptr[dev];
+  return DSA_OK;
+}
+
 }  // namespace dsa
 
 extern "C" int dsa_device_error(int reset) {

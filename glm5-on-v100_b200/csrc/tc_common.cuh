@@ -143,6 +143,39 @@ __device__ __forceinline__ bool mbar_wait(uint32_t mbar, uint32_t parity, volati
   }
 }
 
+// Wait with a device-time limit only (ignores the abort flag): used to drain
+// this CTA's own copies and MMAs after an abort, before TMEM is freed.
+__device__ __forceinline__ bool mbar_wait_drain(uint32_t mbar, uint32_t parity, uint64_t timeout_ns) {
+  if (mbar_try_wait(mbar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t it = 1;; ++it) {
+    if (mbar_try_wait(mbar, parity)) return true;
+    if ((it & 255u) == 0 && globaltimer_ns() - t0 > timeout_ns) return false;
+  }
+}
+
+// ------------------------------------------------------------------ TMA
+// One arrival on `mbar` that also expects `bytes` of asynchronous copies.
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t mbar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(mbar), "r"(bytes) : "memory");
+}
+// Tiled tensor loads (no multicast) completing on `mbar`. `tmap` is the
+// generic address of a __grid_constant__ CUtensorMap kernel parameter.
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, uint64_t tmap, int x, int y, uint32_t mbar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+      "[%4];" ::"r"(dst),
+      "l"(tmap), "r"(x), "r"(y), "r"(mbar)
+      : "memory");
+}
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, uint64_t tmap, int x, int y, int z, uint32_t mbar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+      "[%5];" ::"r"(dst),
+      "l"(tmap), "r"(x), "r"(y), "r"(z), "r"(mbar)
+      : "memory");
+}
+
 __device__ __forceinline__ void named_bar(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }

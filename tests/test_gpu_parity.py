@@ -287,12 +287,82 @@ def test_indexer_tiles_kernel_causal(dsa, fmt):
     assert_scores_close(s, ref)
 
 
+@pytest.mark.parametrize("fmt,Hi,page,B,S,pad,holes", [
+    ("bf16", 32, 64, 300, 5000, 0, False),
+    ("f16", 64, 8, 130, 777, 3, True),
+    ("bf16", 1, 512, 129, 1300, 1, True),
+    ("f16", 17, 16, 67, 2100, 0, False),
+])
+def test_indexer_tc_kernel_edges(dsa, fmt, Hi, page, B, S, pad, holes):
+    """The tcgen05 prefill kernel (16-bit cache of q's type, rows sharing one
+    block table): partial query and key tiles, pages shorter and longer than
+    its 256-key tile, missing blocks (negative and past the cache), an
+    unaligned score row stride, a row of length 0 and a row longer than
+    max_kv. Nothing is written past max_kv."""
+    c = logits_case(500 + B, B=B, Hi=Hi, S=S, page=page, shared_bt=True)
+    if holes:
+        nb = c["k"].shape[0] // page
+        bt = c["bt"].copy()
+        bt[:, 1] = -1
+        bt[:, 3 % bt.shape[1]] = nb + 5
+        c["bt"] = bt
+    c["seq"][0] = 0
+    c["seq"][1] = c["max_kv"] + 100
+    kc, k_ref = idx_cache(c["k"], page, fmt)
+    q = to_dev(c["q"], torch.bfloat16 if fmt == "bf16" else torch.float16)
+    w = to_dev(c["w"], torch.float32)
+    buf = torch.full((B, c["max_kv"] + pad), float("nan"), device=DEV)
+    score = buf[:, : c["max_kv"]]
+    dsa.sm70_indexer_logits(score, q, kc, w, to_dev(c["bt"]), to_dev(c["seq"]), None)
+    torch.cuda.synchronize()
+    ref = O.indexer_logits(q.float().cpu().numpy(), k_ref, c["w"], c["bt"], c["seq"], page, c["max_kv"])
+    assert_scores_close(score.cpu().numpy(), ref)
+    if pad:
+        assert torch.isnan(buf[:, c["max_kv"]:]).all()
+
+
 def test_indexer_packed_equals_unpacked(dsa):
+    # the fp8 cache runs the same mma.sync kernel for both q layouts: bit-identical
     c = logits_case(300, B=70, Hi=32, S=1500, page=64, shared_bt=True, causal=True)
-    s1, ref, _ = run_logits(dsa, c, "f16")
-    s2, _, _ = run_logits(dsa, c, "f16", packed=True)
+    s1, ref, _ = run_logits(dsa, c, "fp8")
+    s2, _, _ = run_logits(dsa, c, "fp8", packed=True)
     np.testing.assert_array_equal(s1, s2)
     assert_scores_close(s2, ref)
+    # with a 16-bit cache the unpacked layout runs the tcgen05 kernel
+    s3, ref3, _ = run_logits(dsa, c, "f16")
+    s4, _, _ = run_logits(dsa, c, "f16", packed=True)
+    assert_scores_close(s3, ref3)
+    assert_scores_close(s4, ref3)
+
+
+def test_indexer_prefill_full_size_sampled_rows(dsa):
+    """BASELINE config 3 shapes (65,536 keys, 32 heads, bf16): the last
+    4,096-row sub-block of the causal chunk through logits + top-2048; sampled
+    rows against the oracle, and every row's selection exact on the kernel's
+    own scores for 64 rows spread over the sub-block."""
+    N, Hi, page, K, R = 65536, 32, 64, 2048, 4096
+    g = torch.Generator(device=DEV).manual_seed(77)
+    nb = N // page
+    kc = torch.randn(nb, page, 128, device=DEV, generator=g).to(torch.bfloat16)
+    bt_row = torch.randperm(nb, device=DEV, generator=g).to(torch.int32)
+    bt = bt_row.view(1, nb).expand(R, nb).contiguous()
+    q = torch.randn(R, Hi, 128, device=DEV, generator=g).to(torch.bfloat16)
+    w = (torch.randn(R, Hi, device=DEV, generator=g) / Hi ** 0.5).to(torch.float16)
+    lens = torch.arange(N - R + 1, N + 1, dtype=torch.int32, device=DEV)
+    score = torch.empty(R, N, device=DEV)
+    idx = torch.empty(R, K, dtype=torch.int32, device=DEV)
+    dsa.sm70_indexer_logits(score, q, kc, w, bt, lens, None)
+    dsa.persistent_topk(score, lens, idx, torch.empty(0, device=DEV), K, N)
+    torch.cuda.synchronize()
+    k_ref = kc.float().cpu().numpy().reshape(-1, 128).astype(np.float64)
+    rows = [0, 1, 2047, R - 1]
+    s_rows = score[rows].cpu().numpy()
+    ref = O.indexer_logits(q[rows].float().cpu().numpy(), k_ref, w[rows].float().cpu().numpy(),
+                           bt[rows].cpu().numpy(), lens[rows].cpu().numpy(), page, N)
+    assert_scores_close(s_rows, ref)
+    sample = torch.arange(0, R, R // 64, device=DEV)
+    np.testing.assert_array_equal(idx[sample].cpu().numpy(),
+                                  O.topk_rows(score[sample].cpu().numpy(), lens[sample].cpu().numpy(), K))
 
 
 def test_indexer_q_bf16_with_fp16_cache(dsa):
