@@ -5,23 +5,34 @@
 // calls for prefill (reference/sparse_attn_indexer.py:632-639, :841-848,
 // :873-880).
 //
-// One CTA of 1024 threads owns one row, so no cross-CTA arrival counters or
+// One CTA of 512 threads owns one row, so no cross-CTA arrival counters or
 // spin-waits are needed (the reference's decode kernel spins on co-resident
-// CTAs, dsa.cu:1372-1375). Selection is an exact MSB-first radix select on
-// the 32-bit monotone image of each score: 12 bits (4096 bins, or the
-// level-1 histogram the logits kernel already built), then 12 bits, then 8
-// bits; the K-th key is exact, so the selected set is exact. Keys equal to
-// the K-th key are taken lowest position first. The final compaction walks
-// positions in order with block-wide prefix sums, so the output is in
-// ascending position order (coalesced gathers downstream), -1 padded.
+// CTAs, dsa.cu:1372-1375). Keys are the 32-bit monotone images of the
+// scores; the K-th largest key is found exactly, keys equal to it are taken
+// lowest position first, and the output lists positions in ascending order
+// (coalesced gathers downstream), -1 padded.
+//
+//   1. Level-1 histogram of the top 12 key bits (or the one the logits kernel
+//      built) gives the bin T1 holding the K-th key.
+//   2. One ordered sweep (each warp owns a contiguous run of positions, read
+//      with 16-byte coalesced loads) writes every position of a bin above T1
+//      to a "sure" list and every key of bin T1 with its position to a
+//      candidate list, both in position order, in shared memory.
+//   3. The remaining 20 bits are resolved among the candidates in shared
+//      memory (12 + 8 bit radix levels), the selected candidates compacted in
+//      order, and the two ascending lists merged into the output.
+// When bin T1 holds more keys than the candidate buffer, the row is resolved
+// by radix levels over global memory and an ordered block-wide compaction.
 #include "common.cuh"
 
 namespace dsa {
 namespace {
 
-constexpr int NT = 1024;
+constexpr int NT = 512;
 constexpr int NWARP = NT / 32;
 constexpr int NBIN1 = 4096;
+constexpr int CAP = 8192;  // candidates of the threshold bin kept in shared memory
+constexpr int KMAX = 4096;
 
 struct TopkParams {
   int32_t* idx;
@@ -34,12 +45,24 @@ struct TopkParams {
   int K;
 };
 
+struct TopkSmem {
+  uint32_t hist[NBIN1];
+  uint32_t cand_key[CAP];
+  int32_t cand_pos[CAP];
+  int32_t sure[KMAX];
+  int32_t sel[KMAX];
+  uint32_t warp[64];
+  uint32_t warp_off[NWARP];
+  int T;
+  uint32_t above, total;
+};
+
 // Block-wide: find the largest bin T with count(bins >= T) >= need, scanning
-// `nbins` (<= 4 * NT) bins. Writes T and count(bins > T) to shared memory.
-__device__ void find_threshold(const uint32_t* hist, int nbins, uint32_t need, uint32_t* s_warp,
-                               int* s_T, uint32_t* s_above) {
+// `nbins` bins (contiguous runs per thread). Writes T and count(bins > T).
+__device__ void find_threshold(const uint32_t* hist, int nbins, uint32_t need, uint32_t* s_warp, int* s_T,
+                               uint32_t* s_above) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int per = (nbins + NT - 1) / NT;  // bins per thread (contiguous)
+  const int per = (nbins + NT - 1) / NT;
   if (tid == 0) {  // defined result even for an inconsistent caller histogram
     *s_T = 0;
     *s_above = 0;
@@ -49,28 +72,27 @@ __device__ void find_threshold(const uint32_t* hist, int nbins, uint32_t need, u
     const int bin = tid * per + i;
     if (bin < nbins) cs += hist[bin];
   }
-  // inclusive suffix scan: sum over threads >= tid
-  uint32_t suf = cs;
+  uint32_t suf = cs;  // inclusive suffix sum within the warp
 #pragma unroll
   for (int off = 1; off < 32; off <<= 1) {
     const uint32_t v = __shfl_down_sync(0xffffffffu, suf, off);
     if (lane + off < 32) suf += v;
   }
-  if (lane == 0) s_warp[warp] = suf;  // warp total
+  if (lane == 0) s_warp[warp] = suf;
   __syncthreads();
   if (warp == 0) {
-    uint32_t wt = s_warp[lane];
+    const uint32_t wt = lane < NWARP ? s_warp[lane] : 0u;
     uint32_t ws = wt;
 #pragma unroll
     for (int off = 1; off < 32; off <<= 1) {
       const uint32_t v = __shfl_down_sync(0xffffffffu, ws, off);
       if (lane + off < 32) ws += v;
     }
-    s_warp[32 + lane] = ws - wt;  // total of warps strictly after this one
+    s_warp[32 + lane] = ws - wt;  // total of the warps after this one
   }
   __syncthreads();
   suf += s_warp[32 + warp];
-  const uint32_t above_chunk = suf - cs;  // count in bins of later threads
+  const uint32_t above_chunk = suf - cs;
   if (above_chunk < need && suf >= need) {
     uint32_t above = above_chunk;
     for (int i = per - 1; i >= 0; --i) {
@@ -88,39 +110,107 @@ __device__ void find_threshold(const uint32_t* hist, int nbins, uint32_t need, u
   __syncthreads();
 }
 
-// Block-wide exclusive prefix of a 0/1 flag in thread order; returns the
-// prefix and writes the block total to *s_total.
-__device__ __forceinline__ uint32_t block_prefix(bool flag, uint32_t* s_warp, uint32_t* s_total) {
+// Block-wide exclusive prefix of v in thread order; *s_total gets the sum.
+__device__ __forceinline__ uint32_t block_exclusive(uint32_t v, uint32_t* s_warp, uint32_t* s_total) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const uint32_t bal = __ballot_sync(0xffffffffu, flag);
-  const uint32_t in_warp = __popc(bal & ((1u << lane) - 1u));
-  if (lane == 0) s_warp[warp] = __popc(bal);
+  uint32_t inc = v;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const uint32_t u = __shfl_up_sync(0xffffffffu, inc, off);
+    if (lane >= off) inc += u;
+  }
+  if (lane == 31) s_warp[warp] = inc;
   __syncthreads();
   if (warp == 0) {
-    const uint32_t v = s_warp[lane];
-    uint32_t inc = v;
+    const uint32_t wv = lane < NWARP ? s_warp[lane] : 0u;
+    uint32_t wi = wv;
 #pragma unroll
     for (int off = 1; off < 32; off <<= 1) {
-      const uint32_t u = __shfl_up_sync(0xffffffffu, inc, off);
-      if (lane >= off) inc += u;
+      const uint32_t u = __shfl_up_sync(0xffffffffu, wi, off);
+      if (lane >= off) wi += u;
     }
-    s_warp[32 + lane] = inc - v;
-    if (lane == 31) *s_total = inc;
+    s_warp[32 + lane] = wi - wv;
+    if (lane == 31) *s_total = wi;
   }
   __syncthreads();
-  const uint32_t r = s_warp[32 + warp] + in_warp;
+  const uint32_t r = s_warp[32 + warp] + inc - v;
   __syncthreads();
   return r;
 }
 
-__global__ void __launch_bounds__(NT) topk_rows_kernel(const TopkParams p) {
-  __shared__ uint32_t s_hist[NBIN1];
-  __shared__ uint32_t s_warp[64];
-  __shared__ int s_T;
-  __shared__ uint32_t s_above, s_total;
+// Four consecutive keys at positions i..i+3 (missing ones, past n, as 0).
+__device__ __forceinline__ void load4(const float* row, int i, int n, bool vec, uint32_t (&k)[4]) {
+  if (vec && i + 4 <= n) {
+    const float4 v = __ldg(reinterpret_cast<const float4*>(row + i));
+    k[0] = monotone32(v.x);
+    k[1] = monotone32(v.y);
+    k[2] = monotone32(v.z);
+    k[3] = monotone32(v.w);
+  } else {
+#pragma unroll
+    for (int e = 0; e < 4; ++e) k[e] = i + e < n ? monotone32(__ldg(row + i + e)) : 0u;
+  }
+}
 
-  const int b = blockIdx.x;
+// Lower bound: number of entries of the ascending list a[0..m) below x.
+__device__ __forceinline__ int count_below(const int32_t* a, int m, int32_t x) {
+  int lo = 0, hi = m;
+  while (lo < hi) {
+    const int mid = (lo + hi) >> 1;
+    if (a[mid] < x)
+      lo = mid + 1;
+    else
+      hi = mid;
+  }
+  return lo;
+}
+
+// Rows whose threshold bin overflows the candidate buffer: two more radix
+// levels and an ordered compaction, all over global memory.
+__device__ void select_global(const float* row, int n, int K, uint32_t T1, uint32_t need2, int32_t* out,
+                              TopkSmem& s) {
   const int tid = threadIdx.x;
+  for (int i = tid; i < NBIN1; i += NT) s.hist[i] = 0;
+  __syncthreads();
+  for (int i = tid; i < n; i += NT) {
+    const uint32_t key = monotone32(__ldg(row + i));
+    if ((key >> 20) == T1) atomicAdd(&s.hist[(key >> 8) & 0xFFFu], 1u);
+  }
+  __syncthreads();
+  find_threshold(s.hist, NBIN1, need2, s.warp, &s.T, &s.above);
+  const uint32_t pre2 = (T1 << 12) | (uint32_t)s.T;
+  const uint32_t need3 = need2 - s.above;
+  for (int i = tid; i < 256; i += NT) s.hist[i] = 0;
+  __syncthreads();
+  for (int i = tid; i < n; i += NT) {
+    const uint32_t key = monotone32(__ldg(row + i));
+    if ((key >> 8) == pre2) atomicAdd(&s.hist[key & 0xFFu], 1u);
+  }
+  __syncthreads();
+  find_threshold(s.hist, 256, need3, s.warp, &s.T, &s.above);
+  const uint32_t kth = (pre2 << 8) | (uint32_t)s.T;
+  const uint32_t n_ties = need3 - s.above;
+  uint32_t out_base = 0, tie_base = 0;
+  for (int base = 0; base < n; base += NT) {
+    const int i = base + tid;
+    const bool in = i < n;
+    const uint32_t key = in ? monotone32(__ldg(row + i)) : 0u;
+    const bool eq = in && key == kth;
+    const uint32_t tie_rank = tie_base + block_exclusive(eq ? 1u : 0u, s.warp, &s.total);
+    const uint32_t n_eq = s.total;
+    const bool sel = in && (key > kth || (eq && tie_rank < n_ties));
+    const uint32_t pos = out_base + block_exclusive(sel ? 1u : 0u, s.warp, &s.total);
+    if (sel && pos < (uint32_t)K) out[pos] = i;
+    out_base += s.total;
+    tie_base += n_eq;
+  }
+}
+
+__global__ void __launch_bounds__(NT, 2) topk_rows_kernel(const TopkParams p) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  TopkSmem& s = *reinterpret_cast<TopkSmem*>(smem_raw);
+  const int b = blockIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int K = p.K;
   int32_t* out = p.idx + (int64_t)b * p.idx_stride;
   const float* row = p.score + (int64_t)b * p.score_stride;
@@ -130,67 +220,201 @@ __global__ void __launch_bounds__(NT) topk_rows_kernel(const TopkParams p) {
     for (int i = tid; i < K; i += NT) out[i] = i < n ? i : -1;
     return;
   }
-  // ---- level 1: bits 31..20
-  if (p.hist) {
-    for (int i = tid; i < NBIN1; i += NT) s_hist[i] = (uint32_t)p.hist[(int64_t)b * NBIN1 + i];
-  } else {
-    for (int i = tid; i < NBIN1; i += NT) s_hist[i] = 0;
-    __syncthreads();
-    for (int i = tid; i < n; i += NT) atomicAdd(&s_hist[monotone32(__ldg(row + i)) >> 20], 1u);
-  }
-  __syncthreads();
-  find_threshold(s_hist, NBIN1, (uint32_t)K, s_warp, &s_T, &s_above);
-  const uint32_t T1 = (uint32_t)s_T;
-  const uint32_t need2 = (uint32_t)K - s_above;
-  // ---- level 2: bits 19..8 among keys with the level-1 prefix
-  for (int i = tid; i < NBIN1; i += NT) s_hist[i] = 0;
-  __syncthreads();
-  for (int i = tid; i < n; i += NT) {
-    const uint32_t key = monotone32(__ldg(row + i));
-    if ((key >> 20) == T1) atomicAdd(&s_hist[(key >> 8) & 0xFFFu], 1u);
-  }
-  __syncthreads();
-  find_threshold(s_hist, NBIN1, need2, s_warp, &s_T, &s_above);
-  const uint32_t pre2 = (T1 << 12) | (uint32_t)s_T;
-  const uint32_t need3 = need2 - s_above;
-  // ---- level 3: bits 7..0
-  for (int i = tid; i < 256; i += NT) s_hist[i] = 0;
-  __syncthreads();
-  for (int i = tid; i < n; i += NT) {
-    const uint32_t key = monotone32(__ldg(row + i));
-    if ((key >> 8) == pre2) atomicAdd(&s_hist[key & 0xFFu], 1u);
-  }
-  __syncthreads();
-  find_threshold(s_hist, 256, need3, s_warp, &s_T, &s_above);
-  const uint32_t kth = (pre2 << 8) | (uint32_t)s_T;
-  const uint32_t n_ties = need3 - s_above;  // keys == kth to take, lowest positions first
+  const bool vec = (reinterpret_cast<uintptr_t>(row) & 15) == 0;
+  // each warp owns a contiguous run of positions, 128 per step (16-byte loads)
+  const int run = ((n + NWARP * 128 - 1) / (NWARP * 128)) * 128;
+  const int w0 = warp * run, w1 = min(n, w0 + run);
 
-  // ---- ordered compaction
-  uint32_t out_base = 0, tie_base = 0;
-  for (int base = 0; base < n; base += NT) {
-    const int i = base + tid;
-    uint32_t key = 0;
-    bool in = i < n;
-    if (in) key = monotone32(__ldg(row + i));
-    const bool eq = in && key == kth;
-    const uint32_t tie_rank = tie_base + block_prefix(eq, s_warp, &s_total);
-    const uint32_t n_eq = s_total;
-    const bool sel = in && (key > kth || (eq && tie_rank < n_ties));
-    const uint32_t pos = out_base + block_prefix(sel, s_warp, &s_total);
-    if (sel) out[pos] = i;
-    out_base += s_total;
-    tie_base += n_eq;
+  // ---- 1. level-1 histogram: bits 31..20
+  if (p.hist) {
+    for (int i = tid; i < NBIN1; i += NT) s.hist[i] = (uint32_t)p.hist[(int64_t)b * NBIN1 + i];
+  } else {
+    for (int i = tid; i < NBIN1; i += NT) s.hist[i] = 0;
+    __syncthreads();
+    for (int i0 = w0; i0 < w1; i0 += 128) {
+      const int i = i0 + 4 * lane;
+      uint32_t k[4];
+      load4(row, i, w1, vec, k);
+#pragma unroll
+      for (int e = 0; e < 4; ++e)
+        if (i + e < w1) atomicAdd(&s.hist[k[e] >> 20], 1u);
+    }
   }
+  __syncthreads();
+  find_threshold(s.hist, NBIN1, (uint32_t)K, s.warp, &s.T, &s.above);
+  const uint32_t T1 = (uint32_t)s.T;
+  const uint32_t n_above1 = s.above;
+  const uint32_t need2 = (uint32_t)K - n_above1;
+  const uint32_t cnt1 = s.hist[T1];
+  __syncthreads();
+  if (cnt1 > (uint32_t)CAP || n_above1 > (uint32_t)KMAX) {
+    select_global(row, n, K, T1, need2, out, s);
+    return;
+  }
+
+  // ---- 2. ordered sweep: sure positions (bin > T1) and candidates (bin == T1)
+  uint32_t ns = 0, nc = 0;
+  for (int i0 = w0; i0 < w1; i0 += 128) {
+    const int i = i0 + 4 * lane;
+    uint32_t k[4];
+    load4(row, i, w1, vec, k);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      if (i + e >= w1) continue;
+      const uint32_t bin = k[e] >> 20;
+      ns += bin > T1;
+      nc += bin == T1;
+    }
+  }
+  // per-warp totals -> warp offsets (sure in the low half, candidates high)
+  uint32_t packed = ns | (nc << 16);
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) packed += __shfl_xor_sync(0xffffffffu, packed, off);
+  if (lane == 0) s.warp_off[warp] = packed;
+  __syncthreads();
+  if (warp == 0) {
+    const uint32_t v = lane < NWARP ? s.warp_off[lane] : 0u;
+    uint32_t inc_s = v & 0xFFFFu, inc_c = v >> 16;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const uint32_t us = __shfl_up_sync(0xffffffffu, inc_s, off);
+      const uint32_t uc = __shfl_up_sync(0xffffffffu, inc_c, off);
+      if (lane >= off) {
+        inc_s += us;
+        inc_c += uc;
+      }
+    }
+    if (lane < NWARP) s.warp[lane] = (inc_s - (v & 0xFFFFu)) | ((inc_c - (v >> 16)) << 16);
+    if (lane == NWARP - 1) s.total = inc_s | (inc_c << 16);
+  }
+  __syncthreads();
+  uint32_t off_s = s.warp[warp] & 0xFFFFu, off_c = s.warp[warp] >> 16;
+  const uint32_t n_sure = min(s.total & 0xFFFFu, (uint32_t)KMAX);
+  const uint32_t n_cand = min(s.total >> 16, (uint32_t)CAP);
+  // every lane takes the same number of steps (the shuffles below need the
+  // whole warp); positions past w1 count as absent
+  for (int i0 = w0; i0 < w1; i0 += 128) {
+    const int i = i0 + 4 * lane;
+    uint32_t k[4];
+    load4(row, i, w1, vec, k);
+    uint32_t cs = 0, cc = 0;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      if (i + e >= w1) continue;
+      cs += (k[e] >> 20) > T1;
+      cc += (k[e] >> 20) == T1;
+    }
+    uint32_t inc = cs | (cc << 16);
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const uint32_t u = __shfl_up_sync(0xffffffffu, inc, off);
+      if (lane >= off) inc += u;
+    }
+    const uint32_t tot = __shfl_sync(0xffffffffu, inc, 31);
+    const uint32_t ex = inc - (cs | (cc << 16));
+    uint32_t ps = off_s + (ex & 0xFFFFu), pc = off_c + (ex >> 16);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      if (i + e >= w1) continue;
+      const uint32_t bin = k[e] >> 20;
+      if (bin > T1) {
+        if (ps < (uint32_t)KMAX) s.sure[ps] = i + e;
+        ++ps;
+      } else if (bin == T1) {
+        if (pc < (uint32_t)CAP) {
+          s.cand_key[pc] = k[e];
+          s.cand_pos[pc] = i + e;
+        }
+        ++pc;
+      }
+    }
+    off_s += tot & 0xFFFFu;
+    off_c += tot >> 16;
+  }
+  __syncthreads();
+
+  // ---- 3. resolve the low 20 bits among the candidates
+  for (int i = tid; i < NBIN1; i += NT) s.hist[i] = 0;
+  __syncthreads();
+  for (int i = tid; i < (int)n_cand; i += NT) atomicAdd(&s.hist[(s.cand_key[i] >> 8) & 0xFFFu], 1u);
+  __syncthreads();
+  find_threshold(s.hist, NBIN1, need2, s.warp, &s.T, &s.above);
+  const uint32_t T2 = (uint32_t)s.T;
+  const uint32_t need3 = need2 - s.above;
+  __syncthreads();
+  for (int i = tid; i < 256; i += NT) s.hist[i] = 0;
+  __syncthreads();
+  for (int i = tid; i < (int)n_cand; i += NT) {
+    const uint32_t key = s.cand_key[i];
+    if (((key >> 8) & 0xFFFu) == T2) atomicAdd(&s.hist[key & 0xFFu], 1u);
+  }
+  __syncthreads();
+  find_threshold(s.hist, 256, need3, s.warp, &s.T, &s.above);
+  const uint32_t kth = (T1 << 20) | (T2 << 8) | (uint32_t)s.T;
+  const uint32_t n_ties = need3 - s.above;
+  __syncthreads();
+
+  // selected candidates, in position order: key > kth, or key == kth among
+  // the first n_ties such keys
+  const int per = (int)((n_cand + NT - 1) / NT);
+  const int c0 = min((int)n_cand, tid * per), c1 = min((int)n_cand, c0 + per);
+  uint32_t my_eq = 0;
+  for (int i = c0; i < c1; ++i) my_eq += s.cand_key[i] == kth;
+  uint32_t tie = block_exclusive(my_eq, s.warp, &s.total);
+  uint32_t my_sel = 0;
+  for (int i = c0; i < c1; ++i) {
+    const uint32_t key = s.cand_key[i];
+    if (key > kth || (key == kth && tie < n_ties)) ++my_sel;
+    tie += key == kth;
+  }
+  uint32_t sp = block_exclusive(my_sel, s.warp, &s.total);
+  const uint32_t n_sel = min(s.total, (uint32_t)KMAX);
+  tie -= my_eq;
+  for (int i = c0; i < c1; ++i) {
+    const uint32_t key = s.cand_key[i];
+    if (key > kth || (key == kth && tie < n_ties)) {
+      if (sp < (uint32_t)KMAX) s.sel[sp] = s.cand_pos[i];
+      ++sp;
+    }
+    tie += key == kth;
+  }
+  __syncthreads();
+
+  // ---- merge the two ascending lists
+  for (int i = tid; i < (int)n_sure; i += NT) {
+    const int32_t P = s.sure[i];
+    const int o = i + count_below(s.sel, (int)n_sel, P);
+    if (o < K) out[o] = P;
+  }
+  for (int i = tid; i < (int)n_sel; i += NT) {
+    const int32_t P = s.sel[i];
+    const int o = i + count_below(s.sure, (int)n_sure, P);
+    if (o < K) out[o] = P;
+  }
+  for (int i = (int)(n_sure + n_sel) + tid; i < K; i += NT) out[i] = -1;  // only for an inconsistent histogram
 }
+
+std::once_flag g_once[kMaxDevices];
+int g_status[kMaxDevices];
 
 int run_topk(const TopkParams& p, int B, cudaStream_t s) {
   DSA_REQUIRE(B >= 0 && p.max_kv >= 0, DSA_ERR_INVALID, "topk: negative size");
-  DSA_REQUIRE(p.K >= 1 && p.K <= 4096, DSA_ERR_UNSUPPORTED, "topk: K must be in [1, 4096] (got %d)", p.K);
+  DSA_REQUIRE(p.K >= 1 && p.K <= KMAX, DSA_ERR_UNSUPPORTED, "topk: K must be in [1, %d] (got %d)", KMAX, p.K);
   if (B == 0) return DSA_OK;
   DSA_REQUIRE(p.idx && p.lens && (p.score || p.max_kv == 0), DSA_ERR_INVALID, "topk: null pointer");
   DSA_REQUIRE(p.idx_stride >= p.K && p.score_stride >= p.max_kv, DSA_ERR_INVALID,
               "topk: row stride smaller than the row");
-  topk_rows_kernel<<<B, NT, 0, s>>>(p);
+  const int dev = current_device();
+  DSA_REQUIRE(dev >= 0 && dev < kMaxDevices, DSA_ERR_UNSUPPORTED, "topk: device %d out of range", dev);
+  std::call_once(g_once[dev], [dev] {
+    g_status[dev] = (int)cudaFuncSetAttribute(topk_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                              (int)sizeof(TopkSmem));
+  });
+  if (g_status[dev] != 0) {
+    set_error("cudaFuncSetAttribute(topk): %s", cudaGetErrorString((cudaError_t)g_status[dev]));
+    return DSA_ERR_CUDA;
+  }
+  topk_rows_kernel<<<B, NT, sizeof(TopkSmem), s>>>(p);
   return check_launch("topk_rows_kernel");
 }
 

@@ -372,7 +372,7 @@ def test_indexer_q_bf16_with_fp16_cache(dsa):
 
 
 # ------------------------------------------------------------------- top-k
-@pytest.mark.parametrize("K", [1, 7, 512, 2048])
+@pytest.mark.parametrize("K", [1, 7, 512, 2048, 4096])
 def test_topk_rows_exact_with_ties(dsa, K):
     rng = np.random.default_rng(K)
     B, S = 9, 9000
