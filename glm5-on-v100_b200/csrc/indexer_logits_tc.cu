@@ -175,11 +175,14 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         tma_load_2d(sbase + OFF_K + rg * (KTILE_BYTES / 2) + j * k_box_rows * 128, tmk, 64 * rg, row, mb_k);
     }
     for (; q_issued < min(QSTAGES, H); ++q_issued) load_q(q_issued);
-    ok = mbar_wait(mb_k, 0, abort_flag, err, kWaitTimeoutNs) &&
-         mbar_wait(mb_q_full(0), 0, abort_flag, err, kWaitTimeoutNs);
-    if (ok) {
-      fence_after_sync();
-      issue_head(0);
+    // two heads in flight from the start: S buffers 0 and 1 are both free
+    ok = mbar_wait(mb_k, 0, abort_flag, err, kWaitTimeoutNs);
+    for (int h = 0; h < 2 && h < H && ok; ++h) {
+      ok = mbar_wait(mb_q_full(h), 0, abort_flag, err, kWaitTimeoutNs);
+      if (ok) {
+        fence_after_sync();
+        issue_head(h);
+      }
     }
   }
   __syncwarp();
@@ -195,42 +198,51 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   for (int h = 0; h < H; ++h) {
     const int b = h & 1;
     ok = ok && mbar_wait(mb_s_full(b), (uint32_t)((h >> 1) & 1), abort_flag, err, kWaitTimeoutNs);
+    ok = __all_sync(0xffffffffu, ok);
     fence_after_sync();
-    if (tid == 0 && ok) {
-      // MMA h has completed, so its Q stage is free: request head h + QSTAGES
-      if (q_issued < H) {
-        load_q(q_issued);
-        ++q_issued;
-      }
-      if (h + 1 < H) {
-        bool ok2 = true;
-        if (h >= 1) ok2 = mbar_wait(mb_s_free(b ^ 1), (uint32_t)(((h - 1) >> 1) & 1), abort_flag, err, kWaitTimeoutNs);
-        ok2 = ok2 && mbar_wait(mb_q_full((h + 1) % QSTAGES), (uint32_t)(((h + 1) / QSTAGES) & 1), abort_flag, err,
-                               kWaitTimeoutNs);
-        if (ok2) {
-          fence_after_sync();
-          issue_head(h + 1);
-        }
-      }
+    if (tid == 0 && ok && q_issued < H) {  // MMA h completed: its Q stage takes head h + QSTAGES
+      load_q(q_issued);
+      ++q_issued;
     }
     __syncwarp();
-    ok = __all_sync(0xffffffffu, ok);
     const float wv = s_w[h * QM + row];
-    uint32_t v[32];
+    // 64 columns in 4 chunks of 16: the next chunk's TMEM load is in flight
+    // while the current one is accumulated
+    uint32_t va[16], vb[16];
     if (ok) {
-      tmem_ld32(t_lane + 256u * (uint32_t)b, v);
+      const uint32_t ta = t_lane + 256u * (uint32_t)b;
+      tmem_ld16(ta, va);
       tmem_wait_ld();
+      tmem_ld16(ta + 16u, vb);
 #pragma unroll
-      for (int j = 0; j < 32; ++j) acc[j] = fmaf(wv, fmaxf(__uint_as_float(v[j]), 0.f), acc[j]);
-      tmem_ld32(t_lane + 256u * (uint32_t)b + 32u, v);
+      for (int j = 0; j < 16; ++j) acc[j] = fmaf(wv, fmaxf(__uint_as_float(va[j]), 0.f), acc[j]);
+      tmem_wait_ld();
+      tmem_ld16(ta + 32u, va);
+#pragma unroll
+      for (int j = 0; j < 16; ++j) acc[16 + j] = fmaf(wv, fmaxf(__uint_as_float(vb[j]), 0.f), acc[16 + j]);
+      tmem_wait_ld();
+      tmem_ld16(ta + 48u, vb);
+#pragma unroll
+      for (int j = 0; j < 16; ++j) acc[32 + j] = fmaf(wv, fmaxf(__uint_as_float(va[j]), 0.f), acc[32 + j]);
       tmem_wait_ld();
     }
     fence_before_sync();
     __syncwarp();
     if (lane == 0) mbar_arrive(mb_s_free(b));
+    // every warp has read S_h: its buffer takes head h + 2
+    if (tid == 0 && ok && h + 2 < H) {
+      bool ok2 = mbar_wait(mb_s_free(b), (uint32_t)((h >> 1) & 1), abort_flag, err, kWaitTimeoutNs);
+      ok2 = ok2 && mbar_wait(mb_q_full((h + 2) % QSTAGES), (uint32_t)(((h + 2) / QSTAGES) & 1), abort_flag, err,
+                             kWaitTimeoutNs);
+      if (ok2) {
+        fence_after_sync();
+        issue_head(h + 2);
+      }
+    }
+    __syncwarp();
     if (ok) {
 #pragma unroll
-      for (int j = 0; j < 32; ++j) acc[32 + j] = fmaf(wv, fmaxf(__uint_as_float(v[j]), 0.f), acc[32 + j]);
+      for (int j = 0; j < 16; ++j) acc[48 + j] = fmaf(wv, fmaxf(__uint_as_float(vb[j]), 0.f), acc[48 + j]);
     }
   }
 

@@ -386,6 +386,26 @@ def test_topk_rows_exact_with_ties(dsa, K):
     np.testing.assert_array_equal(out.cpu().numpy(), O.topk_rows(score, lens, K))
 
 
+def test_topk_adversarial_rows_and_boundaries(dsa):
+    """persistent_topk on rows that defeat shortcuts: large scores only at
+    512 evenly spaced runs of 8 positions (what a strided sample would see),
+    rows of 8192 and 8193 keys (power-of-two edges), and heavy ties from
+    quarter-step rounding; every row exact against the oracle."""
+    rng = np.random.default_rng(5)
+    K, S = 2048, 60000
+    score = rng.standard_normal((4, S)).astype(np.float32)
+    n = S
+    starts = (np.arange(512, dtype=np.int64) * (n - 8) // 511) & ~3
+    sampled = (starts[:, None] + np.arange(8)).reshape(-1)
+    score[0, sampled] = 1000.0 + rng.random(sampled.size).astype(np.float32)
+    score[2, :] = np.round(score[2, :] * 4) / 4
+    lens = np.array([S, 8192, 8193, S], np.int32)
+    out = torch.full((4, K), -7, dtype=torch.int32, device=DEV)
+    dsa.persistent_topk(to_dev(score), to_dev(lens.reshape(-1, 1)), out, torch.empty(0, device=DEV), K, S)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(out.cpu().numpy(), O.topk_rows(score, lens, K))
+
+
 def test_decode_topk_with_fused_histogram_end_to_end(dsa):
     """indexer logits (+hist) -> decode top-k: exact on the kernel's own scores;
     against fp64 logits the sets differ only inside the rounding tie band."""
