@@ -1,0 +1,276 @@
+"""Host logic of the indexer orchestration and the MLA glue, on CPU (no GPU):
+shard spans, sub-blocks, payload packing, merge destinations, the torch merge
+epilogue, spec-row expansion, per-token prefill metadata, the P2P exchange's
+slot and flag protocol against a fake IPC backend (two ranks as threads), and
+the key-sharded merge across two gloo ranks (separate processes).
+
+Mirrors the reference's orchestration (reference/sparse_attn_indexer.py:
+44-106, :726-1030; reference/triton_mla.py:261-279, :414-466).
+"""
+import importlib
+import os
+import socket
+import threading
+import time
+
+import numpy as np
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+from oracle import dsa_oracle as O
+
+sai = importlib.import_module("glm5-on-v100_b200.sparse_attn_indexer")
+mla = importlib.import_module("glm5-on-v100_b200.mla_sparse")
+
+
+# ------------------------------------------------------------ pure helpers
+@pytest.mark.parametrize("max_kv,tp,page", [(65536, 4, 64), (180224, 8, 64), (1000, 3, 16), (64, 8, 64)])
+def test_shard_span_covers_keys_contiguously(max_kv, tp, page):
+    spans = [sai.shard_span(max_kv, tp, r, page) for r in range(tp)]
+    assert spans == [O.shard_span(max_kv, tp, r, page) for r in range(tp)]
+    per = spans[0][1]
+    assert per % max(64, page) == 0
+    covered = 0
+    for r, (off, span) in enumerate(spans):
+        assert off == r * per and span >= page
+        if off < max_kv:
+            assert off == covered
+            covered = min(max_kv, off + span)
+    assert covered == max_kv
+
+
+def test_sub_blocks_tile_the_segment():
+    for lo, hi, kv in [(0, 65536, 65536), (5, 7000, 180224), (0, 100, 64)]:
+        blocks = list(sai.sub_blocks(lo, hi, kv))
+        assert blocks[0][0] == lo and blocks[-1][1] == hi
+        assert all(a2 == b1 for (_, b1), (a2, _) in zip(blocks, blocks[1:]))
+        rows = blocks[0][1] - blocks[0][0]
+        assert rows >= min(128, hi - lo)
+        assert rows * kv * 4 <= max(sai.SCORE_BUDGET_BYTES, 128 * kv * 4)
+
+
+def test_request_bounds():
+    c1 = sai.PrefillChunk(0, torch.zeros(5), torch.zeros(5), torch.zeros(1, 4), 1)
+    assert sai.request_bounds(c1, 5) == [0, 5]
+    c2 = sai.PrefillChunk(0, torch.zeros(9), torch.zeros(9), torch.zeros(2, 4), 2, query_start_loc_cpu=[0, 4, 9])
+    assert sai.request_bounds(c2, 9) == [0, 4, 9]
+    c3 = sai.PrefillChunk(0, torch.zeros(9), torch.zeros(9), torch.zeros(2, 4), 2)
+    with pytest.raises(RuntimeError):
+        sai.request_bounds(c3, 9)
+
+
+def test_pack_payload_and_destination():
+    K = 4
+    pend = [(10, 2, torch.arange(8, dtype=torch.float32).view(2, 4), torch.arange(100, 108, dtype=torch.int32).view(2, 4)),
+            (12, 1, torch.full((1, 4), 5.0), torch.full((1, 4), 7, dtype=torch.int32))]
+    f = sai.pack_payload(pend, K, "cpu")
+    assert f.shape == (3, 8)
+    assert torch.equal(f[:2, :4], pend[0][2])
+    assert torch.equal(f[:2, 4:].contiguous().view(torch.int32), pend[0][3])
+    dst, base = sai.destination(pend, "cpu")
+    assert dst.numel() == 0 and base == 10
+    pend2 = [pend[0], (20, 1, pend[1][2], pend[1][3])]
+    dst, base = sai.destination(pend2, "cpu")
+    assert base == -1 and dst.tolist() == [10, 11, 20]
+
+
+def test_torch_merge_epilogue_matches_reference_restatement():
+    rng = np.random.default_rng(3)
+    tp, R, K = 3, 5, 16
+    vals = rng.standard_normal((tp, R, K)).astype(np.float32)
+    vals[1, 2, :5] = -np.inf
+    pos = np.stack([rng.permutation(1000)[:K] + 1000 * s for s in range(tp) for _ in range(R)]).reshape(tp, R, K)
+    allf = np.concatenate([vals, pos.astype(np.int32).view(np.float32)], axis=2)
+    got = sai.torch_merge_epilogue(torch.from_numpy(allf), K).numpy()
+    np.testing.assert_array_equal(np.sort(got, axis=1), O.shard_merge_torch_epilogue(allf, K))
+    np.testing.assert_array_equal(np.sort(got, axis=1), O.shard_merge(allf, K))
+
+
+def test_expand_spec_rows():
+    seq = torch.tensor([10, 20], dtype=torch.int32)
+    bt = torch.tensor([[1, 2], [3, 4]], dtype=torch.int32)
+    s, b = mla.expand_spec_rows(seq, bt, 2)
+    assert torch.equal(s, seq) and torch.equal(b, bt)
+    s, b = mla.expand_spec_rows(seq, bt, 6)  # next_n = 3 verify tokens per request
+    assert s.tolist() == [8, 9, 10, 18, 19, 20]
+    assert b.tolist() == [[1, 2]] * 3 + [[3, 4]] * 3
+    with pytest.raises(RuntimeError):
+        mla.expand_spec_rows(seq, bt, 5)
+
+
+def test_per_token_metadata():
+    qsl = torch.tensor([0, 3, 7], dtype=torch.int32)
+    bt = torch.tensor([[5, 6], [7, 8]], dtype=torch.int32)
+    chunks = [(2, 4, torch.tensor([1, 2, 3, 1])), (6, 3, torch.tensor([2, 3, 4]))]
+    seq, rows = mla.per_token_metadata(chunks, 2, 7, qsl, bt)
+    assert seq.tolist() == [1, 2, 3, 1, 2, 3, 4]
+    assert rows.tolist() == [[5, 6]] * 3 + [[7, 8]] * 4
+    with pytest.raises(RuntimeError):
+        mla.per_token_metadata(chunks, 2, 8, qsl, bt)  # chunks do not tile [2, 10)
+    with pytest.raises(RuntimeError):
+        mla.per_token_metadata(None, 0, 1, qsl, bt)
+
+
+# ------------------------------------------- P2P exchange, fake IPC backend
+class FakeIPC:
+    """CPU stand-in for the IPC ops of ops.py: buffers in a shared registry,
+    device waits as bounded host polls, the merge by the oracle."""
+
+    registry: dict = {}
+    lock = threading.Lock()
+
+    def __init__(self, rank, timeout_s=5.0):
+        self.rank, self.n_alloc, self.timeout_s = rank, 0, timeout_s
+
+    @staticmethod
+    def key(rank, i):
+        return 1000 * (rank + 1) + i
+
+    def sm70_ipc_alloc(self, nbytes):
+        k = self.key(self.rank, self.n_alloc)
+        self.n_alloc += 1
+        buf = torch.zeros(nbytes, dtype=torch.uint8)
+        with self.lock:
+            self.registry[k] = buf
+            self.registry[buf.data_ptr()] = buf
+        return buf, torch.tensor(list(k.to_bytes(64, "little")), dtype=torch.uint8)
+
+    def sm70_ipc_open(self, handle):
+        return int.from_bytes(bytes(handle.numpy().tolist()), "little")
+
+    def _buf(self, ptr):
+        return self.registry[int(ptr)]
+
+    def _flags(self, ptr):
+        return self._buf(ptr).view(torch.int32)
+
+    def _poll(self, cond, what):
+        t0 = time.monotonic()
+        while not cond():
+            if time.monotonic() - t0 > self.timeout_s:
+                raise RuntimeError(f"fake IPC wait timed out: {what}")
+            time.sleep(0.001)
+
+    def sm70_ipc_flag_set(self, flag_ptr, which, seq):
+        self._flags(flag_ptr)[which] = seq
+
+    def sm70_ipc_slot_wait(self, flag_ptrs, tp, min_seq):
+        self._poll(lambda: all(int(self._flags(p)[1]) >= min_seq for p in flag_ptrs[:tp].tolist()), "slot")
+
+    def sm70_indexer_shard_merge_p2p(self, out, data_ptrs, flag_ptrs, dst_rows, dst_base, topk, tp, R, seq, slot_off):
+        self._poll(lambda: all(int(self._flags(p)[0]) >= seq for p in flag_ptrs[:tp].tolist()), "staged")
+        allf = np.stack([self._buf(p)[slot_off:slot_off + R * 2 * topk * 4].view(torch.float32).view(R, 2 * topk)
+                         .numpy() for p in data_ptrs[:tp].tolist()])
+        merged = torch.from_numpy(O.shard_merge(allf, topk))
+        rows = dst_rows.tolist() if dst_base < 0 else list(range(dst_base, dst_base + R))
+        for i, r in enumerate(rows):
+            out[r, :topk] = merged[i]
+
+
+def _payloads(seed, tp, R, K, rounds):
+    rng = np.random.default_rng(seed)
+    out = []
+    for _ in range(rounds):
+        vals = rng.standard_normal((tp, R, K)).astype(np.float32)
+        pos = (rng.permutation(50000)[:tp * R * K].reshape(tp, R, K)).astype(np.int32)
+        out.append((vals, pos))
+    return out
+
+
+def test_p2p_exchange_protocol_two_ranks():
+    """Two ranks (threads) merge three times: the slots alternate (seq & 1)
+    and the third merge waits until every rank merged the first."""
+    tp, R, K, rounds = 2, 6, 8, 3
+    FakeIPC.registry.clear()
+    handles = [[FakeIPC.key(r, 0).to_bytes(64, "little"), FakeIPC.key(r, 1).to_bytes(64, "little")] for r in range(tp)]
+
+    def gather(objs, payload):
+        objs[:] = [tuple(h) for h in handles]
+
+    ex = [sai.P2PExchange("cpu", tp, r, K, rows_cap=16, all_gather_object=gather, backend=FakeIPC(r))
+          for r in range(tp)]
+    data = _payloads(11, tp, R, K, rounds)
+    outs = [[torch.full((R, K), -9, dtype=torch.int32) for _ in range(rounds)] for _ in range(tp)]
+    errors = []
+
+    def run(r):
+        try:
+            for i, (vals, pos) in enumerate(data):
+                pend = [(0, R, torch.from_numpy(vals[r]), torch.from_numpy(pos[r]))]
+                ex[r].merge(pend, outs[r][i])
+        except Exception as e:  # surfaced below
+            errors.append(e)
+
+    threads = [threading.Thread(target=run, args=(r,)) for r in range(tp)]
+    for t in threads:
+        t.start()
+    for t in threads:
+        t.join(30)
+    assert not errors, errors
+    for i, (vals, pos) in enumerate(data):
+        allf = np.concatenate([vals, pos.view(np.float32)], axis=2)
+        exp = O.shard_merge(allf, K)
+        for r in range(tp):
+            np.testing.assert_array_equal(outs[r][i].numpy(), exp)
+    assert [e.seq for e in ex] == [rounds, rounds]
+
+
+def test_p2p_exchange_times_out_when_a_peer_never_stages():
+    tp, R, K = 2, 2, 4
+    FakeIPC.registry.clear()
+    handles = [[FakeIPC.key(r, 0).to_bytes(64, "little"), FakeIPC.key(r, 1).to_bytes(64, "little")] for r in range(tp)]
+    ex = [sai.P2PExchange("cpu", tp, r, K, rows_cap=4, all_gather_object=lambda o, p: o.__setitem__(
+        slice(None), [tuple(h) for h in handles]), backend=FakeIPC(r, timeout_s=0.2)) for r in range(tp)]
+    vals = torch.zeros(R, K)
+    pos = torch.zeros(R, K, dtype=torch.int32)
+    with pytest.raises(RuntimeError, match="timed out"):
+        ex[0].merge([(0, R, vals, pos)], torch.empty(R, K, dtype=torch.int32))
+
+
+# ------------------------------------------------ key-sharded merge, gloo
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _sharded_worker(rank, world, port, seed, result_q):
+    import torch.distributed as dist
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        sai_w = importlib.import_module("glm5-on-v100_b200.sparse_attn_indexer")
+        rng = np.random.default_rng(seed)
+        R, max_kv, K, page = 7, 3000, 64, 64
+        score = rng.standard_normal((R, max_kv)).astype(np.float32)  # distinct with probability 1
+        lens = np.array([3000, 2999, 1500, 900, 100, 64, 2048], np.int32)
+        off, span = sai_w.shard_span(max_kv, world, rank, page)
+        vals, gidx = O.sharded_local_candidates(score, lens, K, off, span, rank)
+        buf = torch.full((R, K), -9, dtype=torch.int32)
+        shard = sai_w.ShardConfig(tp=world, rank=rank, merge="torch")
+        sai_w.merge_shards([(0, R, torch.from_numpy(vals), torch.from_numpy(gidx))], buf, K, shard)
+        result_q.put((rank, buf.numpy(), O.topk_rows(score, lens, K)))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_key_sharded_merge_two_gloo_ranks():
+    """Each rank selects local top-K on its key span, then the all-gather +
+    torch epilogue path of merge_shards yields the exact global top-K on every
+    rank (the reference's global-subset-of-shard-union property)."""
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_sharded_worker, args=(r, world, port, 21, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=120) for _ in range(world)]
+    for p in procs:
+        p.join(60)
+        assert p.exitcode == 0
+    for rank, got, exp in res:
+        np.testing.assert_array_equal(np.sort(got, axis=1), np.sort(exp, axis=1))
