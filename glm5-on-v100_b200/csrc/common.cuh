@@ -146,6 +146,12 @@ __device__ __forceinline__ uint4 ldg_nc16(const void* p) {
   return v;
 }
 
+// Bulk prefetch of [p, p + bytes) into L2 (p and bytes multiples of 16);
+// no registers or scoreboards are held while it is in flight.
+__device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
 __device__ __forceinline__ uint64_t globaltimer_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));

@@ -27,7 +27,7 @@ struct SparseMlaArgs {
 
 // Tensor-core (tcgen05) kernel for the fp8_ds_mla cache: rows per tile and
 // the slice count it would use for a problem.
-constexpr int kTcTileRows = 128;
+constexpr int kTcTileRows = 64;
 int tc_choose_splits(int B, int head_tiles, int topk, int nsm);
 // Launch the tcgen05 kernel; args.n_splits / args.span already chosen.
 int launch_sparse_mla_tc(const SparseMlaArgs& a, cudaStream_t s);

@@ -6,36 +6,41 @@
 // (:1563-2051); see sparse_mla_decode.cu for the semantics.
 //
 // One CTA = one query row x 64 heads x one slice of the top-k axis, processed
-// in tiles of 128 selected latent rows. The MMAs are "transposed" so that the
-// 128 latent rows are the M side (full-rate M = 128 tcgen05 tiles) and the 64
+// in tiles of 64 selected latent rows that alternate between two shared-memory
+// buffers, so that one tile is loaded while the previous one is in softmax and
+// PV. The MMAs are "transposed" so that latent rows are the M side and the 64
 // heads are N:
-//   S^T[128 x 64]  = KV[128 x 576] . Q^T        (A = KV tile, K-major smem;
-//                                                 B = Q, K-major smem)
-//   O^T[512 x 64] += V^T[512 x 128] . P^T        (A = same KV tile read
+//   S^T[64 x 64]   = KV[64 x 576] . Q^T          (M = 64; A = KV tile,
+//                                                 K-major; B = Q, K-major)
+//   O^T[512 x 64] += V^T[512 x 64] . P^T         (M = 128 per value tile;
+//                                                 A = same KV tile read
 //                                                 MN-major; B = P^T, MN-major)
-// S^T, O^T and the running row sums live in tensor memory (64 + 256 + 64
-// columns). The KV tile is stored once as fp16 in 128-byte-swizzled rows that
-// serve both as K-major A of QK and MN-major A of PV; P^T (fp16) overwrites
-// the tile's rope columns after QK has consumed them, which keeps Q (72 KB) +
-// tile (144 KB) + the slice's row table (8 KB) within one SM.
+// O^T (256 columns) and one S^T per buffer (64 columns each) live in tensor
+// memory. A KV tile is stored once as fp16 in 128-byte-swizzled rows that serve
+// both as K-major A of QK and MN-major A of PV; P^T (fp16) overwrites the
+// tile's rope columns after QK has consumed them. Q (72 KB) + two tiles
+// (2 x 72 KB) + the slice's row table (8 KB) fill one SM's shared memory.
 //
-// Block of 16 warps (512 threads). At the start the block resolves the
-// slice's selected positions through the block table into a row table in
-// shared memory, so no dependent index loads sit on the tile pipeline. Each
-// warp produces 8 rows of every tile: the 656-byte rows are read with 16-byte
-// coalesced loads into registers, and as soon as a 128-wide scale group of
-// tile t is stored (dequantised: e4m3 bits expanded to fp16 with integer ops,
-// times the per-group scale) the same registers receive that group of tile
-// t+1, so the next tile's reads stay in flight through softmax and PV. Lane 0
-// of warp 0 issues the QK MMAs group by group as the tile lands and the PV
-// MMAs after the softmax, committing one mbarrier per 128-wide value tile so
-// the next tile's stores start while PV still runs. In the softmax each
-// thread owns one latent row and 16 heads of S^T (tcgen05.ld): probabilities
-// use a lazily-updated running max per head, moved (with an in-TMEM rescale
-// of O^T and the row sums) only when a score exceeds it by more than 2^8, so
-// P <= 256 in fp16 while o and lse stay exact. Every wait on the tensor core
-// is an mbarrier wait bounded by a device-time limit that reports
-// DSA_ERR_TIMEOUT instead of hanging.
+// Warp roles (16 warps):
+//   * warps 0-7, producers: 8 rows of every tile each; the 656-byte rows are
+//     read with 16-byte coalesced loads into registers, and as soon as a
+//     128-wide scale group of tile t is stored (dequantised: e4m3 bits
+//     expanded to fp16 with integer ops, times the per-group scale, rounded
+//     once) the same registers receive that group of tile t+1, so the next
+//     tile's reads stay in flight while this one is stored.
+//   * warp 12, lane 0: issues QK(t) when tile t is stored and PV(t-1) when its
+//     P^T is written, committing mbarriers that release S, the tile buffer
+//     and (for the softmax) the accumulated O^T.
+//   * warps 8-11, softmax: each thread owns one tile row and 32 heads of S^T
+//     (tcgen05.ld 16x64b). Probabilities use a lazily updated running max per
+//     head, moved (with an in-TMEM rescale of O^T after PV(t-1) completes) only
+//     when a score exceeds it by more than 2^8, so P <= 256 in fp16 while o and
+//     lse stay exact; row sums accumulate in registers.
+// At the start the block resolves the slice's selected positions through the
+// block table into a row table in shared memory, so no dependent index loads
+// sit on the tile pipeline. Every wait on another role or the tensor core is an
+// mbarrier wait bounded by a device-time limit that reports DSA_ERR_TIMEOUT
+// instead of hanging.
 #include "sparse_mla.cuh"
 #include "tc_common.cuh"
 
@@ -44,35 +49,40 @@ namespace {
 
 using namespace tc;
 
-constexpr int TM = kTcTileRows;            // 128 latent rows per tile (MMA M)
-constexpr int NH = 64;                     // heads per CTA (MMA N)
+constexpr int TM = kTcTileRows;             // 64 latent rows per tile
+constexpr int NH = 64;                      // heads per CTA (MMA N)
 constexpr int NWARPS = 16;
 constexpr int NTHREADS = 32 * NWARPS;
-constexpr int ROWS_PER_WARP = TM / NWARPS; // 8
+constexpr int PRODUCERS = 8;                // warps 0-7
+constexpr int SOFTMAX0 = 8;                 // warps 8-11
+constexpr int SOFTMAX_WARPS = 4;
+constexpr int MMA_WARP = 12;
+constexpr int ROWS_PER_WARP = TM / PRODUCERS;  // 8
 constexpr int DV = 512;
-constexpr int TABLE_ROWS = 2048;           // resolved rows held at a time
-constexpr uint32_t KV_REGION = TM * 128;   // one 64-wide K block of the tile: 16 KB
-constexpr uint32_t Q_REGION = NH * 128;    // one 64-wide K block of Q: 8 KB
-constexpr uint32_t SM_KV = 0;
-constexpr uint32_t SM_Q = 9 * KV_REGION;
+constexpr int TABLE_ROWS = 2048;            // resolved rows held at a time
+constexpr uint32_t KV_REGION = TM * 128;    // one 64-wide K block of a tile: 8 KB
+constexpr uint32_t KV_BUF = 9 * KV_REGION;  // one tile: 72 KB
+constexpr uint32_t Q_REGION = NH * 128;     // one 64-wide K block of Q: 8 KB
+constexpr uint32_t SM_KV = 0;               // two tile buffers
+constexpr uint32_t SM_Q = 2 * KV_BUF;
 constexpr uint32_t SM_TABLE = SM_Q + 9 * Q_REGION;
 constexpr uint32_t SM_MISC = SM_TABLE + TABLE_ROWS * 4;
 constexpr uint32_t MISC_BYTES = 2048;
 constexpr uint32_t SMEM_BYTES = SM_MISC + MISC_BYTES + 1024;  // + alignment slack = 232,448
-constexpr uint32_t S_COL = 256;            // S^T columns [256, 320); O^T tile j at [64j, 64j+64)
-constexpr uint32_t L_COL = 320;            // running row sums of P: columns [320, 384)
+constexpr uint32_t S_COL = 256;             // S^T of buffer x at [256 + 64x, +64); O^T tile j at [64j, 64j+64)
 constexpr uint32_t TMEM_COLS = 512;
 constexpr int ROW_BYTES = 656;
 constexpr float kLn2 = 0.69314718055994530942f;
-constexpr float kRescaleThreshold = 8.0f;  // log2 units: P stays <= 256
+constexpr float kRescaleThreshold = 8.0f;   // log2 units: P stays <= 256
 constexpr uint64_t kWaitTimeoutNs = 2000000000ull;
 // row table codes
 constexpr int kRowSkip = -1;   // position not selected / out of range: not counted
 constexpr int kRowZero = -2;   // counted position whose row lies outside the cache: zeros
 
-constexpr uint32_t IDESC_QK = idesc_f16(128, NH, false, false);
+constexpr uint32_t IDESC_QK = idesc_f16(TM, NH, false, false);
 constexpr uint32_t IDESC_PV = idesc_f16(128, NH, true, true);
 
+static_assert(TM == 64, "M = 64 QK tiles");
 static_assert(SMEM_BYTES <= 232448, "shared memory budget");
 
 __device__ int32_t g_tc_error;  // sticky: DSA_ERR_TIMEOUT when a bounded wait expired
@@ -141,8 +151,8 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
-// One warp's share of a tile: rows 8*w + (lane >> 3) + 4*rs (rs = 0, 1).
-// Lane l holds, for each of its 2 rows, nope chunk (l & 7) + 8*j of every
+// One producer warp's share of a tile: rows 8*w + (lane >> 3) + 4*rs (rs = 0,
+// 1). Lane l holds, for each of its 2 rows, nope chunk (l & 7) + 8*j of every
 // 128-wide scale group j (16 e4m3 per chunk), the row's four scales, and rope
 // chunk (l & 7); eight consecutive lanes read 128 contiguous bytes of a row.
 struct Tile {
@@ -180,10 +190,10 @@ __device__ __forceinline__ void load_tail(Tile& T, const uint8_t* kv, const int*
   }
 }
 
-// Store scale group j (K blocks 2j, 2j+1) of this warp's rows.
-__device__ __forceinline__ void store_group(const Tile& T, uint8_t* sm, int j, int w, int lane) {
+// Store scale group j (K blocks 2j, 2j+1) of this warp's rows into tile buffer `buf`.
+__device__ __forceinline__ void store_group(const Tile& T, uint8_t* buf, int j, int w, int lane) {
   const int c = (lane & 7) + 8 * j;  // nope chunk: e4m3 values [16c, 16c+16)
-  uint8_t* region = sm + SM_KV + (c >> 2) * KV_REGION;
+  uint8_t* region = buf + (c >> 2) * KV_REGION;
   const int c0 = 2 * (c & 3);
 #pragma unroll
   for (int rs = 0; rs < 2; ++rs) {
@@ -195,16 +205,18 @@ __device__ __forceinline__ void store_group(const Tile& T, uint8_t* sm, int j, i
   }
 }
 
-__device__ __forceinline__ void store_rope(const Tile& T, uint8_t* sm, int w, int lane) {
+__device__ __forceinline__ void store_rope(const Tile& T, uint8_t* buf, int w, int lane) {
 #pragma unroll
   for (int rs = 0; rs < 2; ++rs)
-    *reinterpret_cast<uint4*>(sm + SM_KV + 8 * KV_REGION +
+    *reinterpret_cast<uint4*>(buf + 8 * KV_REGION +
                               sw128_off(ROWS_PER_WARP * w + (lane >> 3) + 4 * rs, lane & 7)) = T.rope[rs];
 }
 
-// Row table for slice rows [r0, r0 + n): physical row, kRowZero or kRowSkip.
-__device__ __forceinline__ void resolve_rows(const SparseMlaArgs& p, int b, int seq_len, int r0, int n, int* table) {
-  for (int i = threadIdx.x; i < n; i += NTHREADS) {
+// Row table for slice rows [r0, r0 + n): physical row, kRowZero or kRowSkip;
+// written by threads [0, nthreads) of the block.
+__device__ __forceinline__ void resolve_rows(const SparseMlaArgs& p, int b, int seq_len, int r0, int n, int* table,
+                                             int nthreads) {
+  for (int i = threadIdx.x; i < n; i += nthreads) {
     int code = kRowSkip;
     const int pos = p.idx[(int64_t)b * p.idx_stride + r0 + i];
     if (pos >= 0 && pos < seq_len) {
@@ -226,20 +238,24 @@ __global__ void __launch_bounds__(NTHREADS, 1) sparse_mla_decode_tc_kernel(const
   uint8_t* sm = smem_raw + (base - raw_base);
   int* table = reinterpret_cast<int*>(sm + SM_TABLE);
   uint8_t* misc = sm + SM_MISC;
-  // mbarriers: [0..4] kv_full (groups 0..3, rope), [5..8] kv_free (PV value tile j), [9] s_full, [10] done
+  // misc: [0, 72) 9 mbarriers | 80 TMEM base | 84 abort | 88 any_rescale |
+  // [96, 128) ovf | [128, 256) s_valid | [256, 2048) per-head floats
   uint64_t* mbar = reinterpret_cast<uint64_t*>(misc);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(misc + 96);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(misc + 100);
-  int* ovf = reinterpret_cast<int*>(misc + 128);            // [4 quarters][4 warps] overflow votes
-  int* any_rescale = reinterpret_cast<int*>(misc + 192);    // [4]
-  float* m_ref = reinterpret_cast<float*>(misc + 256);      // [64] running max (log2 units)
-  float* alpha = m_ref + 64;                                // [64] this tile's rescale factors
-  float* tmax = alpha + 64;                                 // [4 quarters][4 warps][16] tile maxima
-  float* l_sum = tmax + 256;                                // [64]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(misc + 80);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(misc + 84);
+  int* any_rescale = reinterpret_cast<int*>(misc + 88);
+  int* ovf = reinterpret_cast<int*>(misc + 96);           // [2 parities][4 softmax warps] overflow votes
+  uint8_t* s_valid = misc + 128;                          // [2 buffers][64 rows] row counted
+  float* m_ref = reinterpret_cast<float*>(misc + 256);    // [64] running max (log2 units)
+  float* alpha = m_ref + 64;                              // [64] this tile's rescale factors
+  float* tmax = alpha + 64;                               // [4][64] tile maxima; then row-sum partials
+  float* l_sum = tmax + 256;                              // [64]
   const uint32_t mb0 = smem_u32(&mbar[0]);
-  auto mb_kv_full = [&](int j) { return mb0 + 8u * (uint32_t)j; };
-  auto mb_kv_free = [&](int j) { return mb0 + 8u * (uint32_t)(5 + j); };
-  const uint32_t mb_s_full = mb0 + 8u * 9, mb_done = mb0 + 8u * 10;
+  auto mb_kv_full = [&](int x) { return mb0 + 8u * (uint32_t)x; };         // producers: tile stored
+  auto mb_s_full = [&](int x) { return mb0 + 16u + 8u * (uint32_t)x; };    // QK done
+  auto mb_p_full = [&](int x) { return mb0 + 32u + 8u * (uint32_t)x; };    // softmax: P^T written
+  auto mb_kv_free = [&](int x) { return mb0 + 48u + 8u * (uint32_t)x; };   // PV done: buffer and O^T released
+  const uint32_t mb_done = mb0 + 64u;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int b = blockIdx.x;
@@ -254,12 +270,16 @@ __global__ void __launch_bounds__(NTHREADS, 1) sparse_mla_decode_tc_kernel(const
 
   if (warp == 0) {
     if (lane == 0) {
-      for (int j = 0; j < 5; ++j) mbar_init(mb_kv_full(j), NWARPS);
-      for (int j = 0; j < 4; ++j) mbar_init(mb_kv_free(j), 1);
-      mbar_init(mb_s_full, 1);
+      for (int x = 0; x < 2; ++x) {
+        mbar_init(mb_kv_full(x), PRODUCERS);
+        mbar_init(mb_s_full(x), 1);
+        mbar_init(mb_p_full(x), SOFTMAX_WARPS);
+        mbar_init(mb_kv_free(x), 1);
+      }
       mbar_init(mb_done, 1);
       mbar_init_fence();
       *abort_flag = 0;
+      *any_rescale = 0;
     }
     __syncwarp();
     tmem_alloc(smem_u32(tmem_slot), TMEM_COLS);
@@ -281,7 +301,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) sparse_mla_decode_tc_kernel(const
       alpha[threadIdx.x] = 1.f;
     }
     // pad the table so that reads for rows past the slice are "not counted"
-    resolve_rows(p, b, seq_len, lo, min(nrows, TABLE_ROWS), table);
+    resolve_rows(p, b, seq_len, lo, min(nrows, TABLE_ROWS), table, NTHREADS);
     for (int i = min(nrows, TABLE_ROWS) + threadIdx.x; i < min(ntiles * TM, TABLE_ROWS); i += NTHREADS)
       table[i] = kRowSkip;
   }
@@ -291,249 +311,298 @@ __global__ void __launch_bounds__(NTHREADS, 1) sparse_mla_decode_tc_kernel(const
   fence_after_sync();
   const uint32_t tmem = *tmem_slot;
   // Base descriptors; a start-address advance of X bytes adds X >> 4.
-  const uint64_t desc_kv = sw128_desc(base + SM_KV, 16, 1024);                  // KV tile, K-major
-  const uint64_t desc_q = sw128_desc(base + SM_Q, 16, 1024);                    // Q, K-major
-  const uint64_t desc_v = sw128_desc(base + SM_KV, KV_REGION, 1024);            // KV tile, MN-major
-  const uint64_t desc_p = sw128_desc(base + SM_KV + 8 * KV_REGION, KV_REGION, 1024);  // P^T, MN-major
+  const uint64_t desc_kv = sw128_desc(base + SM_KV, 16, 1024);                       // tile buffer 0, K-major
+  const uint64_t desc_q = sw128_desc(base + SM_Q, 16, 1024);                         // Q, K-major
+  const uint64_t desc_v = sw128_desc(base + SM_KV, KV_REGION, 1024);                 // tile buffer 0, MN-major
+  const uint64_t desc_p = sw128_desc(base + SM_KV + 8 * KV_REGION, KV_REGION, 1024);  // P^T of buffer 0, MN-major
+  constexpr uint64_t kBufStep = KV_BUF >> 4;                                         // descriptor step per buffer
 
-  const int w = warp;                // producer: rows 8*w .. 8*w + 7 of a tile
-  const int sp = warp & 3;           // TMEM sub-partition: lanes [32*sp, 32*sp+32)
-  const int hq = warp >> 2;          // softmax head quarter: heads [16*hq, 16*hq+16)
-  const int row_s = 32 * sp + lane;  // the tile row this thread owns in the softmax
-  const uint32_t t_lane = (uint32_t)(32 * sp) << 16;
-
-  Tile T;
   bool ok = true;
-  bool issued = false;
-  bool have_next = false;  // tile t's data was prefetched during iteration t-1
-  // Control flow is uniform across the block: after a timed-out wait (`ok`
-  // false, abort flag set) every warp still executes the same sequence of
-  // barriers and arrivals, and every later wait returns at once.
-  for (int t = 0; t < ntiles; ++t) {
-    const uint32_t ph = t & 1;
-    const int tbase = (t % kTilesPerTable) * TM;  // tile rows in the row table
-    if (!have_next) {
-      if (t > 0) {  // a new table window: resolve it once the previous tile is consumed
+  bool issued = false;  // the MMA thread issued at least one MMA
+  // Control flow is uniform within each role: after a timed-out wait (`ok`
+  // false, abort flag set) every thread still executes its role's barriers
+  // and arrivals, and every later wait returns at once.
+  if (warp < PRODUCERS) {
+    // ------------------------------------------------------------- producers
+    const int w = warp;
+    Tile T;
+    bool have_next = false;  // tile t's data was prefetched during iteration t-1
+    for (int t = 0; t < ntiles; ++t) {
+      const int x = t & 1;
+      const uint32_t ph = (t >> 1) & 1;
+      const int tbase = (t % kTilesPerTable) * TM;  // tile rows in the row table
+      if (!have_next) {
+        if (t > 0) {  // a new table window: every producer has read its last entries
+          named_bar(2, PRODUCERS * 32);
+          const int r0 = t * TM;
+          resolve_rows(p, b, seq_len, lo + r0, min(nrows - r0, TABLE_ROWS), table, PRODUCERS * 32);
+          for (int i = min(nrows - r0, TABLE_ROWS) + threadIdx.x; i < min((ntiles - t) * TM, TABLE_ROWS);
+               i += PRODUCERS * 32)
+            table[i] = kRowSkip;
+          named_bar(2, PRODUCERS * 32);
+        }
+        if (ok) {
 #pragma unroll
-        for (int j = 0; j < 4; ++j) ok = ok && mbar_wait(mb_kv_free(j), ph ^ 1, abort_flag, err, kWaitTimeoutNs);
-        __syncthreads();
-        const int r0 = t * TM;
-        resolve_rows(p, b, seq_len, lo + r0, min(nrows - r0, TABLE_ROWS), table);
-        for (int i = min(nrows - r0, TABLE_ROWS) + threadIdx.x; i < min((ntiles - t) * TM, TABLE_ROWS);
-             i += NTHREADS)
-          table[i] = kRowSkip;
-        __syncthreads();
+          for (int j = 0; j < 4; ++j) load_group(T, p.kv, table, tbase, j, w, lane);
+          load_tail(T, p.kv, table, tbase, w, lane);
+        }
       }
+      // buffer x is free once PV(t-2) has completed
+      if (t >= 2) ok = ok && mbar_wait(mb_kv_free(x), ph ^ 1, abort_flag, err, kWaitTimeoutNs);
+      const bool prefetch = (t + 1 < ntiles) && ((t + 1) % kTilesPerTable != 0);
+      const int nbase = ((t + 1) % kTilesPerTable) * TM;
+      uint8_t* buf = sm + SM_KV + x * KV_BUF;
 #pragma unroll
-      for (int j = 0; j < 4; ++j) load_group(T, p.kv, table, tbase, j, w, lane);
-      load_tail(T, p.kv, table, tbase, w, lane);
-    }
-    const bool prefetch = (t + 1 < ntiles) && ((t + 1) % kTilesPerTable != 0);
-    const int nbase = ((t + 1) % kTilesPerTable) * TM;
-    // ---- store tile t group by group as PV(t-1) releases it; QK(t) follows each group
+      for (int j = 0; j < 4; ++j) {
+        if (ok) store_group(T, buf, j, w, lane);
+        if (ok && prefetch) load_group(T, p.kv, table, nbase, j, w, lane);
+      }
+      if (ok) store_rope(T, buf, w, lane);
+      if (ok && prefetch) load_tail(T, p.kv, table, nbase, w, lane);
+      // tile t+2's rows into L2 (bulk prefetch: no registers held), so that
+      // next iteration's register loads of them return quickly
+      if (ok && t + 2 < ntiles && (t + 2) / kTilesPerTable == t / kTilesPerTable && (lane & 7) == 0) {
+        const int pb = ((t + 2) % kTilesPerTable) * TM;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      if (t > 0) ok = ok && mbar_wait(mb_kv_free(j), ph ^ 1, abort_flag, err, kWaitTimeoutNs);
-      if (ok) store_group(T, sm, j, w, lane);
+        for (int rs = 0; rs < 2; ++rs) {
+          const int code = table[pb + ROWS_PER_WARP * w + (lane >> 3) + 4 * rs];
+          if (code >= 0) prefetch_l2(p.kv + (int64_t)code * ROW_BYTES, ROW_BYTES);
+        }
+      }
+      if ((lane & 7) == 0) {  // which of this warp's rows count, for the softmax
+#pragma unroll
+        for (int rs = 0; rs < 2; ++rs) {
+          const int row = ROWS_PER_WARP * w + (lane >> 3) + 4 * rs;
+          s_valid[x * TM + row] = table[tbase + row] != kRowSkip ? 1 : 0;
+        }
+      }
       fence_proxy_async();
       __syncwarp();
-      if (lane == 0) mbar_arrive(mb_kv_full(j));
-      // next tile's loads go out after the proxy fence so it never waits on them
-      if (ok && prefetch) load_group(T, p.kv, table, nbase, j, w, lane);
-      if (warp == 0) {  // warp-uniform descriptors; lane 0 issues
-        ok = ok && mbar_wait(mb_kv_full(j), ph, abort_flag, err, kWaitTimeoutNs);
-        ok = __all_sync(0xffffffffu, ok);
-        if (ok) {
+      if (lane == 0) mbar_arrive(mb_kv_full(x));
+      have_next = prefetch;
+    }
+  } else if (warp == MMA_WARP) {
+    // --------------------------------------------------------- MMA issue
+    // Lane 0 issues QK(t) as soon as tile t is stored and PV(u) as soon as
+    // P^T(u) is written, whichever comes first (the two touch different
+    // buffers), so PV(t-1), which frees the buffer of tile t+1, never waits
+    // for tile t. Polling is bounded: no progress for kWaitTimeoutNs aborts.
+    if (lane == 0 && ntiles > 0) {
+      int tq = 0, tp = 0;  // next tile to issue QK / PV for
+      uint64_t t_idle = globaltimer_ns();
+      uint32_t spins = 0;
+      while (tp < ntiles) {
+        bool progress = false;
+        if (tq < ntiles && mbar_test(mb_kv_full(tq & 1), (tq >> 1) & 1)) {  // S^T(x) = KV(tq) . Q^T
+          const int x = tq & 1;
           fence_after_sync();
-          if (lane == 0) {  // the same thread issues and commits every MMA
+          const uint64_t dk = desc_kv + x * kBufStep;
 #pragma unroll
-            for (int kb = 2 * j; kb < 2 * j + 2; ++kb)
+          for (int kb = 0; kb < 9; ++kb)
 #pragma unroll
-              for (int k = 0; k < 4; ++k)
-                mma_f16_ss(tmem + S_COL, desc_kv + ((kb * KV_REGION + 32 * k) >> 4),
-                           desc_q + ((kb * Q_REGION + 32 * k) >> 4), IDESC_QK, (kb | k) != 0);
-          }
+            for (int k = 0; k < 4; ++k)
+              mma_f16_ss(tmem + S_COL + 64 * x, dk + ((kb * KV_REGION + 32 * k) >> 4),
+                         desc_q + ((kb * Q_REGION + 32 * k) >> 4), IDESC_QK, (kb | k) != 0);
+          mma_commit(mb_s_full(x));
           issued = true;
+          ++tq;
+          progress = true;
         }
-        __syncwarp();
-      }
-    }
-    // rope group: its region held P^T(t-1), released with the last value tile of PV(t-1)
-    if (ok) store_rope(T, sm, w, lane);
-    fence_proxy_async();
-    __syncwarp();
-    if (lane == 0) mbar_arrive(mb_kv_full(4));
-    if (ok && prefetch) load_tail(T, p.kv, table, nbase, w, lane);
-    have_next = ok && prefetch;
-    if (warp == 0) {
-      ok = ok && mbar_wait(mb_kv_full(4), ph, abort_flag, err, kWaitTimeoutNs);
-      ok = __all_sync(0xffffffffu, ok);
-      if (ok) {
-        fence_after_sync();
-        if (lane == 0) {  // the same thread issues and commits every MMA
+        if (tp < tq && mbar_test(mb_p_full(tp & 1), (tp >> 1) & 1)) {  // O^T += V^T(tp) . P^T(tp)
+          const int y = tp & 1;
+          fence_after_sync();
+          const uint64_t dv = desc_v + y * kBufStep, dp = desc_p + y * kBufStep;
 #pragma unroll
-          for (int k = 0; k < 4; ++k)
-            mma_f16_ss(tmem + S_COL, desc_kv + ((8 * KV_REGION + 32 * k) >> 4),
-                       desc_q + ((8 * Q_REGION + 32 * k) >> 4), IDESC_QK, 1u);
-          mma_commit(mb_s_full);
+          for (int j = 0; j < 4; ++j)
+#pragma unroll
+            for (int s = 0; s < TM / 16; ++s)
+              mma_f16_ss(tmem + 64 * j, dv + ((2 * j * KV_REGION + 2048 * s) >> 4), dp + ((2048 * s) >> 4), IDESC_PV,
+                         (tp > 0 || s > 0) ? 1u : 0u);
+          mma_commit(mb_kv_free(y));
+          ++tp;
+          progress = true;
         }
-      }
-      __syncwarp();
-    }
-
-    // ---- softmax(t): this thread = tile row row_s x heads [16*hq, 16*hq+16)
-    ok = ok && mbar_wait(mb_s_full, ph, abort_flag, err, kWaitTimeoutNs);
-    fence_after_sync();
-    const bool vrow = table[tbase + row_s] != kRowSkip;
-    const int hb = 16 * hq;
-    uint32_t s16[16];
-    if (ok) {
-      tmem_ld16(tmem + t_lane + S_COL + hb, s16);
-      tmem_wait_ld();
-    } else {
-#pragma unroll
-      for (int h = 0; h < 16; ++h) s16[h] = 0u;
-    }
-    float pr[16];
-    bool over = false;
-#pragma unroll
-    for (int h4 = 0; h4 < 16; h4 += 4) {
-      const float4 m4 = *reinterpret_cast<const float4*>(m_ref + hb + h4);
-      const float mm[4] = {m4.x, m4.y, m4.z, m4.w};
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float x = (vrow ? __uint_as_float(s16[h4 + e]) * p.scale_log2 : -INFINITY) - mm[e];
-        over |= x > kRescaleThreshold;
-        pr[h4 + e] = ex2(x);
-      }
-    }
-    const unsigned vote = __ballot_sync(0xffffffffu, over);
-    if (lane == 0) ovf[hq * 4 + sp] = vote != 0u;
-    named_bar(1 + hq, 128);
-    const bool slow = (ovf[hq * 4] | ovf[hq * 4 + 1] | ovf[hq * 4 + 2] | ovf[hq * 4 + 3]) != 0;
-    if (slow) {
-      // exact tile maxima of this head quarter; heads whose max grew by more
-      // than 2^8 move their running max and rescale what was accumulated
-      uint32_t my_max = 0;
-#pragma unroll
-      for (int h = 0; h < 16; ++h) {
-        const float v = vrow ? __uint_as_float(s16[h]) * p.scale_log2 : -INFINITY;
-        const uint32_t wm = __reduce_max_sync(0xffffffffu, monotone32(v));
-        if (lane == h) my_max = wm;
-      }
-      if (lane < 16) tmax[(hq * 4 + sp) * 16 + lane] = unmono(my_max);
-      named_bar(1 + hq, 128);
-      if (sp == 0) {
-        float a = 1.f;
-        if (lane < 16) {
-          const int head = hb + lane;
-          float tm = tmax[(hq * 4) * 16 + lane];
-#pragma unroll
-          for (int s = 1; s < 4; ++s) tm = fmaxf(tm, tmax[(hq * 4 + s) * 16 + lane]);
-          const float m_old = m_ref[head];
-          if (tm > m_old + kRescaleThreshold) {
-            a = ex2(m_old - tm);
-            m_ref[head] = tm;
+        if (progress) {
+          t_idle = globaltimer_ns();
+          spins = 0;
+        } else if ((++spins & 255u) == 0) {
+          if (*abort_flag) {
+            ok = false;
+            break;
           }
-          alpha[head] = a;
+          if (globaltimer_ns() - t_idle > kWaitTimeoutNs) {
+            *abort_flag = 1;
+            if (err) atomicExch(err, (int32_t)DSA_ERR_TIMEOUT);
+            ok = false;
+            break;
+          }
         }
-        const unsigned any = __ballot_sync(0xffffffffu, a != 1.f);
-        if (lane == 0) any_rescale[hq] = any != 0u;
-      }
-      named_bar(1 + hq, 128);
-      if (ok && any_rescale[hq] && t > 0) {  // O^T columns of this quarter, lanes of this sub-partition
-#pragma unroll 1
-        for (int j = 0; j < 4; ++j) {
-          uint32_t o[16];
-          tmem_ld16(tmem + t_lane + 64 * j + hb, o);
-          tmem_wait_ld();
-#pragma unroll
-          for (int h = 0; h < 16; ++h) o[h] = __float_as_uint(__uint_as_float(o[h]) * alpha[hb + h]);
-          tmem_st16(tmem + t_lane + 64 * j + hb, o);
-        }
-        tmem_wait_st();
-      }
-#pragma unroll
-      for (int h = 0; h < 16; ++h) {
-        const float v = vrow ? __uint_as_float(s16[h]) * p.scale_log2 : -INFINITY;
-        pr[h] = ex2(v - m_ref[hb + h]);
       }
     }
-    // row sums (TMEM) and P^T (the rope region, consumed by QK(t))
-    {
-      uint32_t l16[16];
-      if (ok && t > 0) {
-        tmem_ld16(tmem + t_lane + L_COL + hb, l16);
+    __syncwarp();
+    ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+    issued = __shfl_sync(0xffffffffu, issued ? 1 : 0, 0) != 0;
+  } else if (warp >= SOFTMAX0 && warp < SOFTMAX0 + SOFTMAX_WARPS) {
+    // ---------------------------------------------------------- softmax
+    const int sp = warp - SOFTMAX0;                    // TMEM sub-partition: lanes [32sp, 32sp + 16)
+    const int row = 16 * sp + (lane >> 2) + 8 * (lane & 1);  // tile row of this thread (16x64b layout)
+    const int par = (lane >> 1) & 1;                   // this thread's heads: 2i + par
+    const bool head_row = ((lane >> 2) + 8 * (lane & 1)) == 0;  // lanes 0 and 2: first row of the group
+    const uint32_t t_sp = tmem + ((uint32_t)(32 * sp) << 16);
+    float L[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) L[i] = 0.f;
+    for (int t = 0; t < ntiles; ++t) {
+      const int x = t & 1;
+      const uint32_t ph = (t >> 1) & 1;
+      ok = ok && mbar_wait(mb_s_full(x), ph, abort_flag, err, kWaitTimeoutNs) &&
+           mbar_wait(mb_kv_full(x), ph, abort_flag, err, kWaitTimeoutNs);
+      ok = __all_sync(0xffffffffu, ok);
+      fence_after_sync();
+      uint32_t s[32];
+      if (ok) {
+        tmem_ld16x64(t_sp + S_COL + 64 * x, s);
         tmem_wait_ld();
       } else {
 #pragma unroll
-        for (int h = 0; h < 16; ++h) l16[h] = 0u;
+        for (int i = 0; i < 32; ++i) s[i] = 0u;
       }
+      const bool vrow = s_valid[x * TM + row] != 0;
+      // in place: score (log2 units) - running max
+      bool over = false;
 #pragma unroll
-      for (int h = 0; h < 16; ++h) {
-        const float a = slow ? alpha[hb + h] : 1.f;
-        l16[h] = __float_as_uint(__uint_as_float(l16[h]) * a + pr[h]);
+      for (int i = 0; i < 32; ++i) {
+        const float v = (vrow ? __uint_as_float(s[i]) * p.scale_log2 : -INFINITY) - m_ref[2 * i + par];
+        s[i] = __float_as_uint(v);
+        over |= v > kRescaleThreshold;
       }
-      if (ok) tmem_st16(tmem + t_lane + L_COL + hb, l16);
-      uint8_t* preg = sm + SM_KV + 8 * KV_REGION;
+      const unsigned vote = __ballot_sync(0xffffffffu, over);
+      if (lane == 0) ovf[x * 4 + sp] = vote != 0u;
+      named_bar(1, SOFTMAX_WARPS * 32);
+      const bool slow = (ovf[x * 4] | ovf[x * 4 + 1] | ovf[x * 4 + 2] | ovf[x * 4 + 3]) != 0;
+      if (slow) {
+        // exact tile maxima per head (S^T read again); heads whose max grew by
+        // more than 2^8 move their running max and rescale what was accumulated
+        if (ok) {
+          tmem_ld16x64(t_sp + S_COL + 64 * x, s);
+          tmem_wait_ld();
+        }
 #pragma unroll
-      for (int c = 0; c < 2; ++c)
-        *reinterpret_cast<uint4*>(preg + sw128_off(row_s, 2 * hq + c)) =
-            make_uint4(pack_half2(pr[8 * c], pr[8 * c + 1]), pack_half2(pr[8 * c + 2], pr[8 * c + 3]),
-                       pack_half2(pr[8 * c + 4], pr[8 * c + 5]), pack_half2(pr[8 * c + 6], pr[8 * c + 7]));
-    }
-    tmem_wait_st();
-    fence_proxy_async();
-    fence_before_sync();
-    __syncthreads();
-    // ---- O^T += V^T . P^T, one commit per 128-wide value tile
-    if (warp == 0) {
-      const bool go = __all_sync(0xffffffffu, ok);
-      if (go) {
-        fence_after_sync();
-        if (lane == 0) {  // the same thread issues and commits every MMA
+        for (int i = 0; i < 32; ++i) {
+          const float v = vrow ? __uint_as_float(s[i]) * p.scale_log2 : -INFINITY;
+          s[i] = __float_as_uint(v);
+          uint32_t m = monotone32(v);
+          m = max(m, __shfl_xor_sync(0xffffffffu, m, 1));
+          m = max(m, __shfl_xor_sync(0xffffffffu, m, 4));
+          m = max(m, __shfl_xor_sync(0xffffffffu, m, 8));
+          m = max(m, __shfl_xor_sync(0xffffffffu, m, 16));
+          if (head_row) tmax[sp * 64 + 2 * i + par] = unmono(m);
+        }
+        named_bar(1, SOFTMAX_WARPS * 32);
+        if (sp == 0) {
+          bool moved = false;
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
+          for (int k = 0; k < 2; ++k) {
+            const int head = lane + 32 * k;
+            const float tm = fmaxf(fmaxf(tmax[head], tmax[64 + head]), fmaxf(tmax[128 + head], tmax[192 + head]));
+            const float m_old = m_ref[head];
+            float a = 1.f;
+            if (tm > m_old + kRescaleThreshold) {
+              a = ex2(m_old - tm);
+              m_ref[head] = tm;
+              moved = true;
+            }
+            alpha[head] = a;
+          }
+          const unsigned any = __ballot_sync(0xffffffffu, moved);
+          if (lane == 0) *any_rescale = any != 0u;
+        }
+        named_bar(1, SOFTMAX_WARPS * 32);
+        if (*any_rescale && t > 0) {
+          // O^T holds PV(0..t-1): rescale after PV(t-1) has completed
+          const int u = t - 1;
+          ok = ok && mbar_wait(mb_kv_free(u & 1), (u >> 1) & 1, abort_flag, err, kWaitTimeoutNs);
+          ok = __all_sync(0xffffffffu, ok);
+          if (ok) {
+            fence_after_sync();
+#pragma unroll 1
+            for (int c = 0; c < 16; ++c) {  // columns [16c, 16c+16): heads (16c % 64) ..
+              uint32_t o[16];
+              tmem_ld16(t_sp + 16 * c, o);
+              tmem_wait_ld();
 #pragma unroll
-            for (int s = 0; s < TM / 16; ++s)
-              mma_f16_ss(tmem + 64 * j, desc_v + ((2 * j * KV_REGION + 2048 * s) >> 4), desc_p + ((2048 * s) >> 4),
-                         IDESC_PV, (t > 0 || s > 0) ? 1u : 0u);
-            mma_commit(mb_kv_free(j));
+              for (int h = 0; h < 16; ++h) o[h] = __float_as_uint(__uint_as_float(o[h]) * alpha[(16 * c + h) & 63]);
+              tmem_st16(t_sp + 16 * c, o);
+            }
+            tmem_wait_st();
           }
         }
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          s[i] = __float_as_uint(__uint_as_float(s[i]) - m_ref[2 * i + par]);
+          L[i] *= alpha[2 * i + par];
+        }
       }
+      // probabilities and row sums
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const float pe = ex2(__uint_as_float(s[i]));
+        s[i] = __float_as_uint(pe);
+        L[i] += pe;
+      }
+      // P^T row `row`: heads 0..31 from the even-parity thread, 32..63 from
+      // its partner (lane ^ 2), each pairing its values with the partner's;
+      // one 16-byte chunk (8 heads) at a time
+      uint8_t* preg = sm + SM_KV + x * KV_BUF + 8 * KV_REGION;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t pk[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int j = 4 * c + e;
+          const float lo_v = __uint_as_float(s[j]), hi_v = __uint_as_float(s[j + 16]);
+          const float recv = __shfl_xor_sync(0xffffffffu, par ? lo_v : hi_v, 2);
+          pk[e] = par ? pack_half2(recv, hi_v) : pack_half2(lo_v, recv);
+        }
+        if (ok) *reinterpret_cast<uint4*>(preg + sw128_off(row, 4 * par + c)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+      }
+      fence_proxy_async();
+      fence_before_sync();
       __syncwarp();
+      if (lane == 0) mbar_arrive(mb_p_full(x));
+    }
+    // per-head sums over this sub-partition's rows (threads of one parity)
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      float v = L[i];
+      v += __shfl_xor_sync(0xffffffffu, v, 1);
+      v += __shfl_xor_sync(0xffffffffu, v, 4);
+      v += __shfl_xor_sync(0xffffffffu, v, 8);
+      v += __shfl_xor_sync(0xffffffffu, v, 16);
+      L[i] = v;
+    }
+    named_bar(1, SOFTMAX_WARPS * 32);  // every warp is past its last use of tmax as tile maxima
+    if (head_row) {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) tmax[sp * 64 + 2 * i + par] = L[i];
     }
   }
   // -------------------------------------------------------------- epilogue
-  if (ok && ntiles > 0) ok = mbar_wait(mb_kv_free(3), (ntiles - 1) & 1, abort_flag, err, kWaitTimeoutNs);
+  __syncthreads();
+  if (ok && ntiles > 0)  // the last PV has completed
+    ok = mbar_wait(mb_kv_free((ntiles - 1) & 1), ((ntiles - 1) >> 1) & 1, abort_flag, err, kWaitTimeoutNs);
   __syncthreads();
   // A thread whose wait failed set the abort flag before this barrier, so
   // every thread reads the same decision.
   const bool live = *abort_flag == 0;
   __syncthreads();
-  const int hb = 16 * hq;
+  const int sp = warp & 3;           // TMEM sub-partition: lanes [32*sp, 32*sp+32)
+  const int hb = 16 * (warp >> 2);   // heads [hb, hb + 16)
+  const uint32_t t_lane = (uint32_t)(32 * sp) << 16;
   if (ntiles > 0 && live) {
     fence_after_sync();
-    float* lbuf = reinterpret_cast<float*>(sm + SM_KV);  // [64 heads][128 rows]; the tile is dead now
-    {
-      uint32_t lr[16];
-      tmem_ld16(tmem + t_lane + L_COL + hb, lr);
-      tmem_wait_ld();
-#pragma unroll
-      for (int h = 0; h < 16; ++h) lbuf[(hb + h) * TM + row_s] = __uint_as_float(lr[h]);
-    }
-    __syncthreads();
-    {
-      const int head = threadIdx.x >> 3, q8 = threadIdx.x & 7;
-      float s = 0.f;
-#pragma unroll
-      for (int r = 0; r < 16; ++r) s += lbuf[head * TM + 16 * q8 + r];
-      s += __shfl_xor_sync(0xffffffffu, s, 1);
-      s += __shfl_xor_sync(0xffffffffu, s, 2);
-      s += __shfl_xor_sync(0xffffffffu, s, 4);
-      if (q8 == 0) l_sum[head] = s;
-    }
+    if (threadIdx.x < NH)
+      l_sum[threadIdx.x] = (tmax[threadIdx.x] + tmax[64 + threadIdx.x]) + (tmax[128 + threadIdx.x] + tmax[192 + threadIdx.x]);
     __syncthreads();
 #pragma unroll 1
     for (int j = 0; j < 4; ++j) {
@@ -591,11 +660,12 @@ __global__ void __launch_bounds__(NTHREADS, 1) sparse_mla_decode_tc_kernel(const
     }
   }
   // every MMA of this CTA has completed before TMEM is released (a commit
-  // tracks the MMAs of the thread that issues it: lane 0 of warp 0 issued all)
-  if (warp == 0 && issued && !live) {
+  // tracks the MMAs of the thread that issues it: lane 0 of the MMA warp
+  // issued all)
+  if (warp == MMA_WARP && issued && !live) {
     if (lane == 0) mma_commit(mb_done);
     __syncwarp();
-    mbar_wait(mb_done, 0, abort_flag, err, kWaitTimeoutNs);
+    mbar_wait_drain(mb_done, 0, kWaitTimeoutNs);
   }
   fence_before_sync();
   __syncthreads();
@@ -641,7 +711,8 @@ int tc_choose_splits(int B, int head_tiles, int topk, int nsm) {
     const int per = (ntiles + s - 1) / s;
     if ((ntiles + per - 1) / per != s) continue;
     const double waves = std::ceil(units * s / nsm);
-    // one tile of 128 fp8 rows moves 84 KB; a slice's partial state 2 x 128 KB
+    // cost in tile times: a tile of TM fp8 rows moves TM x 656 B; a slice's
+    // partial state is written and merged (2 x 128 KB)
     double cost = waves * per + (s > 1 ? units * s * 2.0 * NH * DV * 4.0 / ((double)nsm * TM * ROW_BYTES) : 0.0);
     if (cost < best_cost - 1e-9) {
       best_cost = cost;
