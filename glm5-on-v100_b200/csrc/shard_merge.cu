@@ -12,7 +12,7 @@
 // only visits candidates still matching the prefix. The selected positions
 // (-1 for -inf values) are sorted ascending with a bitonic network in shared
 // memory. The P2P variant reads each shard straight from the peer's buffer
-// with plain loads (no TMA, no multicast) after a bounded acquire-wait on the
+// with plain loads (no TMA) after a bounded acquire-wait on the
 // peer's staged flag.
 #include <climits>
 

@@ -184,7 +184,7 @@ __device__ __forceinline__ bool mbar_wait_drain(uint32_t mbar, uint32_t parity, 
 __device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t mbar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(mbar), "r"(bytes) : "memory");
 }
-// Tiled tensor loads (no multicast) completing on `mbar`. `tmap` is the
+// Tiled tensor loads into this CTA only, completing on `mbar`. `tmap` is the
 // generic address of a __grid_constant__ CUtensorMap kernel parameter.
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, uint64_t tmap, int x, int y, uint32_t mbar) {
   asm volatile(
