@@ -51,13 +51,14 @@ using namespace tc;
 
 constexpr int TM = kTcTileRows;             // 64 latent rows per tile
 constexpr int NH = 64;                      // heads per CTA (MMA N)
-constexpr int NWARPS = 16;
+constexpr int NWARPS = 32;
 constexpr int NTHREADS = 32 * NWARPS;
-constexpr int PRODUCERS = 8;                // warps 0-7
-constexpr int SOFTMAX0 = 8;                 // warps 8-11
-constexpr int SOFTMAX_WARPS = 4;
-constexpr int MMA_WARP = 12;
-constexpr int ROWS_PER_WARP = TM / PRODUCERS;  // 8
+constexpr int PRODUCERS = 16;               // warps 0-15
+constexpr int SOFTMAX0 = 16;                // warps 16-23: two per TMEM sub-partition
+constexpr int SOFTMAX_WARPS = 8;
+constexpr int MMA_WARP = 24;                // warps 25-31 only join the block barriers
+constexpr int ROWS_PER_WARP = TM / PRODUCERS;  // 4
+constexpr int RS = ROWS_PER_WARP / 4;          // rows per group of 8 lanes
 constexpr int DV = 512;
 constexpr int TABLE_ROWS = 2048;            // resolved rows held at a time
 constexpr uint32_t KV_REGION = TM * 128;    // one 64-wide K block of a tile: 8 KB
@@ -156,9 +157,9 @@ __device__ __forceinline__ float ex2(float x) {
 // 128-wide scale group j (16 e4m3 per chunk), the row's four scales, and rope
 // chunk (l & 7); eight consecutive lanes read 128 contiguous bytes of a row.
 struct Tile {
-  uint4 nope[2][4];  // [rs][j]
-  float4 sc[2];
-  uint4 rope[2];
+  uint4 nope[RS][4];  // [rs][j]
+  float4 sc[RS];
+  uint4 rope[RS];
 };
 
 __device__ __forceinline__ int64_t row_offset(const int* table, int i) {
@@ -169,7 +170,7 @@ __device__ __forceinline__ int64_t row_offset(const int* table, int i) {
 __device__ __forceinline__ void load_group(Tile& T, const uint8_t* kv, const int* table, int tbase, int j, int w,
                                            int lane) {
 #pragma unroll
-  for (int rs = 0; rs < 2; ++rs) {
+  for (int rs = 0; rs < RS; ++rs) {
     const int64_t off = row_offset(table, tbase + ROWS_PER_WARP * w + (lane >> 3) + 4 * rs);
     T.nope[rs][j] = off >= 0 ? ldg_nc16(kv + off + 16 * ((lane & 7) + 8 * j)) : make_uint4(0, 0, 0, 0);
   }
@@ -177,7 +178,7 @@ __device__ __forceinline__ void load_group(Tile& T, const uint8_t* kv, const int
 
 __device__ __forceinline__ void load_tail(Tile& T, const uint8_t* kv, const int* table, int tbase, int w, int lane) {
 #pragma unroll
-  for (int rs = 0; rs < 2; ++rs) {
+  for (int rs = 0; rs < RS; ++rs) {
     const int64_t off = row_offset(table, tbase + ROWS_PER_WARP * w + (lane >> 3) + 4 * rs);
     if (off >= 0) {
       const uint4 s = ldg_nc16(kv + off + 512);
@@ -196,7 +197,7 @@ __device__ __forceinline__ void store_group(const Tile& T, uint8_t* buf, int j, 
   uint8_t* region = buf + (c >> 2) * KV_REGION;
   const int c0 = 2 * (c & 3);
 #pragma unroll
-  for (int rs = 0; rs < 2; ++rs) {
+  for (int rs = 0; rs < RS; ++rs) {
     const int i = ROWS_PER_WARP * w + (lane >> 3) + 4 * rs;
     uint4 o0, o1;
     dequant16(T.nope[rs][j], pick(T.sc[rs], j), o0, o1);
@@ -207,7 +208,7 @@ __device__ __forceinline__ void store_group(const Tile& T, uint8_t* buf, int j, 
 
 __device__ __forceinline__ void store_rope(const Tile& T, uint8_t* buf, int w, int lane) {
 #pragma unroll
-  for (int rs = 0; rs < 2; ++rs)
+  for (int rs = 0; rs < RS; ++rs)
     *reinterpret_cast<uint4*>(buf + 8 * KV_REGION +
                               sw128_off(ROWS_PER_WARP * w + (lane >> 3) + 4 * rs, lane & 7)) = T.rope[rs];
 }
@@ -239,17 +240,17 @@ __global__ void __launch_bounds__(NTHREADS, 1) sparse_mla_decode_tc_kernel(const
   int* table = reinterpret_cast<int*>(sm + SM_TABLE);
   uint8_t* misc = sm + SM_MISC;
   // misc: [0, 72) 9 mbarriers | 80 TMEM base | 84 abort | 88 any_rescale |
-  // [96, 128) ovf | [128, 256) s_valid | [256, 2048) per-head floats
+  // [96, 160) ovf | [160, 288) s_valid | [288, 1824) per-head floats
   uint64_t* mbar = reinterpret_cast<uint64_t*>(misc);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(misc + 80);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(misc + 84);
   int* any_rescale = reinterpret_cast<int*>(misc + 88);
-  int* ovf = reinterpret_cast<int*>(misc + 96);           // [2 parities][4 softmax warps] overflow votes
-  uint8_t* s_valid = misc + 128;                          // [2 buffers][64 rows] row counted
-  float* m_ref = reinterpret_cast<float*>(misc + 256);    // [64] running max (log2 units)
+  int* ovf = reinterpret_cast<int*>(misc + 96);           // [2 parities][8 softmax warps] overflow votes
+  uint8_t* s_valid = misc + 160;                          // [2 buffers][64 rows] row counted
+  float* m_ref = reinterpret_cast<float*>(misc + 288);    // [64] running max (log2 units)
   float* alpha = m_ref + 64;                              // [64] this tile's rescale factors
   float* tmax = alpha + 64;                               // [4][64] tile maxima; then row-sum partials
-  float* l_sum = tmax + 256;                              // [64]
+  float* l_sum = alpha;                                   // [64] in the epilogue (alpha is dead)
   const uint32_t mb0 = smem_u32(&mbar[0]);
   auto mb_kv_full = [&](int x) { return mb0 + 8u * (uint32_t)x; };         // producers: tile stored
   auto mb_s_full = [&](int x) { return mb0 + 16u + 8u * (uint32_t)x; };    // QK done
@@ -364,14 +365,14 @@ __global__ void __launch_bounds__(NTHREADS, 1) sparse_mla_decode_tc_kernel(const
       if (ok && t + 2 < ntiles && (t + 2) / kTilesPerTable == t / kTilesPerTable && (lane & 7) == 0) {
         const int pb = ((t + 2) % kTilesPerTable) * TM;
 #pragma unroll
-        for (int rs = 0; rs < 2; ++rs) {
+        for (int rs = 0; rs < RS; ++rs) {
           const int code = table[pb + ROWS_PER_WARP * w + (lane >> 3) + 4 * rs];
           if (code >= 0) prefetch_l2(p.kv + (int64_t)code * ROW_BYTES, ROW_BYTES);
         }
       }
       if ((lane & 7) == 0) {  // which of this warp's rows count, for the softmax
 #pragma unroll
-        for (int rs = 0; rs < 2; ++rs) {
+        for (int rs = 0; rs < RS; ++rs) {
           const int row = ROWS_PER_WARP * w + (lane >> 3) + 4 * rs;
           s_valid[x * TM + row] = table[tbase + row] != kRowSkip ? 1 : 0;
         }
@@ -444,14 +445,17 @@ __global__ void __launch_bounds__(NTHREADS, 1) sparse_mla_decode_tc_kernel(const
     issued = __shfl_sync(0xffffffffu, issued ? 1 : 0, 0) != 0;
   } else if (warp >= SOFTMAX0 && warp < SOFTMAX0 + SOFTMAX_WARPS) {
     // ---------------------------------------------------------- softmax
-    const int sp = warp - SOFTMAX0;                    // TMEM sub-partition: lanes [32sp, 32sp + 16)
+    const int s8 = warp - SOFTMAX0;                    // softmax warp 0..7
+    const int sp = warp & 3;                           // TMEM sub-partition: lanes [32sp, 32sp + 16)
+    const int hh = s8 >> 2;                            // heads [32hh, 32hh + 32)
     const int row = 16 * sp + (lane >> 2) + 8 * (lane & 1);  // tile row of this thread (16x64b layout)
-    const int par = (lane >> 1) & 1;                   // this thread's heads: 2i + par
+    const int par = (lane >> 1) & 1;
+    const int hbase = 32 * hh + par;                   // this thread's heads: hbase + 2i, i < 16
     const bool head_row = ((lane >> 2) + 8 * (lane & 1)) == 0;  // lanes 0 and 2: first row of the group
     const uint32_t t_sp = tmem + ((uint32_t)(32 * sp) << 16);
-    float L[32];
+    float L[16];
 #pragma unroll
-    for (int i = 0; i < 32; ++i) L[i] = 0.f;
+    for (int i = 0; i < 16; ++i) L[i] = 0.f;
     for (int t = 0; t < ntiles; ++t) {
       const int x = t & 1;
       const uint32_t ph = (t >> 1) & 1;
@@ -459,36 +463,38 @@ __global__ void __launch_bounds__(NTHREADS, 1) sparse_mla_decode_tc_kernel(const
            mbar_wait(mb_kv_full(x), ph, abort_flag, err, kWaitTimeoutNs);
       ok = __all_sync(0xffffffffu, ok);
       fence_after_sync();
-      uint32_t s[32];
+      uint32_t s[16];
       if (ok) {
-        tmem_ld16x64(t_sp + S_COL + 64 * x, s);
+        tmem_ld16x32(t_sp + S_COL + 64 * x + 32 * hh, s);
         tmem_wait_ld();
       } else {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) s[i] = 0u;
+        for (int i = 0; i < 16; ++i) s[i] = 0u;
       }
       const bool vrow = s_valid[x * TM + row] != 0;
       // in place: score (log2 units) - running max
       bool over = false;
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const float v = (vrow ? __uint_as_float(s[i]) * p.scale_log2 : -INFINITY) - m_ref[2 * i + par];
+      for (int i = 0; i < 16; ++i) {
+        const float v = (vrow ? __uint_as_float(s[i]) * p.scale_log2 : -INFINITY) - m_ref[hbase + 2 * i];
         s[i] = __float_as_uint(v);
         over |= v > kRescaleThreshold;
       }
       const unsigned vote = __ballot_sync(0xffffffffu, over);
-      if (lane == 0) ovf[x * 4 + sp] = vote != 0u;
+      if (lane == 0) ovf[x * 8 + s8] = vote != 0u;
       named_bar(1, SOFTMAX_WARPS * 32);
-      const bool slow = (ovf[x * 4] | ovf[x * 4 + 1] | ovf[x * 4 + 2] | ovf[x * 4 + 3]) != 0;
-      if (slow) {
+      int any_ovf = 0;
+#pragma unroll
+      for (int k = 0; k < SOFTMAX_WARPS; ++k) any_ovf |= ovf[x * 8 + k];
+      if (any_ovf) {
         // exact tile maxima per head (S^T read again); heads whose max grew by
         // more than 2^8 move their running max and rescale what was accumulated
         if (ok) {
-          tmem_ld16x64(t_sp + S_COL + 64 * x, s);
+          tmem_ld16x32(t_sp + S_COL + 64 * x + 32 * hh, s);
           tmem_wait_ld();
         }
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
+        for (int i = 0; i < 16; ++i) {
           const float v = vrow ? __uint_as_float(s[i]) * p.scale_log2 : -INFINITY;
           s[i] = __float_as_uint(v);
           uint32_t m = monotone32(v);
@@ -496,10 +502,10 @@ __global__ void __launch_bounds__(NTHREADS, 1) sparse_mla_decode_tc_kernel(const
           m = max(m, __shfl_xor_sync(0xffffffffu, m, 4));
           m = max(m, __shfl_xor_sync(0xffffffffu, m, 8));
           m = max(m, __shfl_xor_sync(0xffffffffu, m, 16));
-          if (head_row) tmax[sp * 64 + 2 * i + par] = unmono(m);
+          if (head_row) tmax[sp * 64 + hbase + 2 * i] = unmono(m);
         }
         named_bar(1, SOFTMAX_WARPS * 32);
-        if (sp == 0) {
+        if (s8 == 0) {
           bool moved = false;
 #pragma unroll
           for (int k = 0; k < 2; ++k) {
@@ -519,52 +525,55 @@ __global__ void __launch_bounds__(NTHREADS, 1) sparse_mla_decode_tc_kernel(const
         }
         named_bar(1, SOFTMAX_WARPS * 32);
         if (*any_rescale && t > 0) {
-          // O^T holds PV(0..t-1): rescale after PV(t-1) has completed
+          // O^T holds PV(0..t-1): rescale after PV(t-1) has completed; this
+          // warp takes columns [128hh, 128hh + 128) of its sub-partition's lanes
           const int u = t - 1;
           ok = ok && mbar_wait(mb_kv_free(u & 1), (u >> 1) & 1, abort_flag, err, kWaitTimeoutNs);
           ok = __all_sync(0xffffffffu, ok);
           if (ok) {
             fence_after_sync();
 #pragma unroll 1
-            for (int c = 0; c < 16; ++c) {  // columns [16c, 16c+16): heads (16c % 64) ..
+            for (int c = 0; c < 8; ++c) {
+              const int col = 128 * hh + 16 * c;  // heads (col % 64) ..
               uint32_t o[16];
-              tmem_ld16(t_sp + 16 * c, o);
+              tmem_ld16(t_sp + col, o);
               tmem_wait_ld();
 #pragma unroll
-              for (int h = 0; h < 16; ++h) o[h] = __float_as_uint(__uint_as_float(o[h]) * alpha[(16 * c + h) & 63]);
-              tmem_st16(t_sp + 16 * c, o);
+              for (int h = 0; h < 16; ++h) o[h] = __float_as_uint(__uint_as_float(o[h]) * alpha[(col + h) & 63]);
+              tmem_st16(t_sp + col, o);
             }
             tmem_wait_st();
           }
         }
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          s[i] = __float_as_uint(__uint_as_float(s[i]) - m_ref[2 * i + par]);
-          L[i] *= alpha[2 * i + par];
+        for (int i = 0; i < 16; ++i) {
+          s[i] = __float_as_uint(__uint_as_float(s[i]) - m_ref[hbase + 2 * i]);
+          L[i] *= alpha[hbase + 2 * i];
         }
       }
       // probabilities and row sums
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
+      for (int i = 0; i < 16; ++i) {
         const float pe = ex2(__uint_as_float(s[i]));
         s[i] = __float_as_uint(pe);
         L[i] += pe;
       }
-      // P^T row `row`: heads 0..31 from the even-parity thread, 32..63 from
-      // its partner (lane ^ 2), each pairing its values with the partner's;
-      // one 16-byte chunk (8 heads) at a time
+      // P^T row `row`, heads [32hh, 32hh + 32): the even-parity thread writes
+      // the first 16, its partner (lane ^ 2) the last 16, each pairing its
+      // values with the partner's; 16-byte chunks of 8 heads
       uint8_t* preg = sm + SM_KV + x * KV_BUF + 8 * KV_REGION;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 0; c < 2; ++c) {
         uint32_t pk[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const int j = 4 * c + e;
-          const float lo_v = __uint_as_float(s[j]), hi_v = __uint_as_float(s[j + 16]);
+          const float lo_v = __uint_as_float(s[j]), hi_v = __uint_as_float(s[8 + j]);
           const float recv = __shfl_xor_sync(0xffffffffu, par ? lo_v : hi_v, 2);
           pk[e] = par ? pack_half2(recv, hi_v) : pack_half2(lo_v, recv);
         }
-        if (ok) *reinterpret_cast<uint4*>(preg + sw128_off(row, 4 * par + c)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+        if (ok)
+          *reinterpret_cast<uint4*>(preg + sw128_off(row, 4 * hh + 2 * par + c)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
       }
       fence_proxy_async();
       fence_before_sync();
@@ -573,7 +582,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) sparse_mla_decode_tc_kernel(const
     }
     // per-head sums over this sub-partition's rows (threads of one parity)
 #pragma unroll
-    for (int i = 0; i < 32; ++i) {
+    for (int i = 0; i < 16; ++i) {
       float v = L[i];
       v += __shfl_xor_sync(0xffffffffu, v, 1);
       v += __shfl_xor_sync(0xffffffffu, v, 4);
@@ -584,7 +593,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) sparse_mla_decode_tc_kernel(const
     named_bar(1, SOFTMAX_WARPS * 32);  // every warp is past its last use of tmax as tile maxima
     if (head_row) {
 #pragma unroll
-      for (int i = 0; i < 32; ++i) tmax[sp * 64 + 2 * i + par] = L[i];
+      for (int i = 0; i < 16; ++i) tmax[sp * 64 + hbase + 2 * i] = L[i];
     }
   }
   // -------------------------------------------------------------- epilogue
@@ -596,8 +605,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) sparse_mla_decode_tc_kernel(const
   // every thread reads the same decision.
   const bool live = *abort_flag == 0;
   __syncthreads();
-  const int sp = warp & 3;           // TMEM sub-partition: lanes [32*sp, 32*sp+32)
-  const int hb = 16 * (warp >> 2);   // heads [hb, hb + 16)
+  const int sp = warp & 3;                // TMEM sub-partition: lanes [32*sp, 32*sp+32)
+  const int hb = 16 * ((warp >> 2) & 3);  // heads [hb, hb + 16), for warps 0-15
   const uint32_t t_lane = (uint32_t)(32 * sp) << 16;
   if (ntiles > 0 && live) {
     fence_after_sync();
@@ -605,7 +614,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) sparse_mla_decode_tc_kernel(const
       l_sum[threadIdx.x] = (tmax[threadIdx.x] + tmax[64 + threadIdx.x]) + (tmax[128 + threadIdx.x] + tmax[192 + threadIdx.x]);
     __syncthreads();
 #pragma unroll 1
-    for (int j = 0; j < 4; ++j) {
+    for (int j = 0; j < 4 && warp < 16; ++j) {
       uint32_t o[16];
       tmem_ld16(tmem + t_lane + 64 * j + hb, o);
       tmem_wait_ld();
