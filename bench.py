@@ -239,15 +239,14 @@ class DecodeWorkload(Workload):
                                    self.bt, self.seq, self.scale)
 
     def launches_per_step(self, dsa):
-        ws = dsa._lib.lib().dsa_sparse_mla_decode_workspace_bytes(self.B, self.H, self.TOPK)
-        return 2 if ws else 1
+        return dsa.ops.decode_plan(self.B, self.H, self.TOPK, dsa._lib.DSA_FP8_DS_MLA)["launches"]
 
     def algorithmic(self):
         return self.B * self.bytes_per_row, "GB/s", "hbm"
 
     def roofline_note(self, kind):
         return (f"peak {kind} HBM copy; achieved = {self.bytes_per_row} B/row x {self.B} rows per launch / "
-                f"CUDA-event time of the op (decode kernel + merge)")
+                f"CUDA-event time of the op (one kernel: slices merge inside a cluster)")
 
     def e2e_setup(self, dev):
         self.h_q = [t.cpu().pin_memory() for t in self.q]

@@ -41,6 +41,8 @@ SIGNATURES = {
     "dsa_version": (_i, []),
     "dsa_device_error": (_i, [_i]),
     "dsa_sparse_mla_decode_workspace_bytes": (_sz, [_i, _i, _i]),
+    "dsa_sparse_mla_decode_plan": (_i, [_i, _i, _i, _i, ctypes.POINTER(_i), ctypes.POINTER(_i),
+                                        ctypes.POINTER(_sz), ctypes.POINTER(_i)]),
     "dsa_sparse_mla_decode": (_i, [_p, _i, _p, _p, _i, _p, _i, _i64, _i, _p, _i64, _p, _i64, _i, _p,
                                    _i, _i, _i, _d, _p, _sz, _p]),
     "dsa_sparse_mla_decode_noalloc": (_i, [_p, _i, _p, _p, _i, _p, _i, _i64, _i, _p, _i64, _p, _i64, _i,

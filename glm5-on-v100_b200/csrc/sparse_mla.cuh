@@ -29,6 +29,10 @@ struct SparseMlaArgs {
 // the slice count it would use for a problem.
 constexpr int kTcTileRows = 64;
 int tc_choose_splits(int B, int head_tiles, int topk, int nsm);
+// Slices of one row that the tcgen05 kernel merges inside one thread-block
+// cluster: n_splits when that cluster size (2 or 4) is resident on this
+// device, else 1 (partial states + the merge kernel).
+int tc_cluster_size(int n_splits);
 // Launch the tcgen05 kernel; args.n_splits / args.span already chosen.
 int launch_sparse_mla_tc(const SparseMlaArgs& a, cudaStream_t s);
 // Merge per-slice partial states into o / lse (defined with the v1 kernel).

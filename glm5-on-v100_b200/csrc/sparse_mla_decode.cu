@@ -488,6 +488,31 @@ extern "C" size_t dsa_sparse_mla_decode_workspace_bytes(int B, int n_head, int t
   return (size_t)B * n_head * s * (DV + 2) * sizeof(float);
 }
 
+extern "C" int dsa_sparse_mla_decode_plan(int B, int n_head, int topk, int kv_format, int* n_splits,
+                                          int* cluster_size, size_t* workspace_bytes, int* launches) {
+  clear_error();
+  DSA_REQUIRE(B >= 0 && n_head >= 0 && topk >= 0, DSA_ERR_INVALID,
+              "sparse_mla_decode_plan: negative size (B=%d n_head=%d topk=%d)", B, n_head, topk);
+  DSA_REQUIRE(kv_format == DSA_F16 || kv_format == DSA_BF16 || kv_format == DSA_FP8_DS_MLA, DSA_ERR_INVALID,
+              "sparse_mla_decode_plan: kv_format must be f16, bf16 or fp8_ds_mla");
+  int s = 1, c = 1;
+  size_t ws = 0;
+  int n = 0;
+  if (B > 0 && n_head > 0) {
+    s = splits_for(kv_format, B, n_head, std::max(topk, 1), sm_count(current_device()));
+    if (topk == 0) s = 1;
+    if (kv_format == DSA_FP8_DS_MLA && s > 1) c = tc_cluster_size(s);
+    const bool partials = s > 1 && c == 1;
+    if (partials) ws = (size_t)B * n_head * s * (DV + 2) * sizeof(float);
+    n = partials ? 2 : 1;
+  }
+  if (n_splits) *n_splits = s;
+  if (cluster_size) *cluster_size = c;
+  if (workspace_bytes) *workspace_bytes = ws;
+  if (launches) *launches = n;
+  return DSA_OK;
+}
+
 extern "C" int dsa_sparse_mla_decode(void* o, int o_dtype, float* lse, const void* q, int q_dtype,
                                      const void* kv_cache, int kv_format, int64_t n_kv_rows,
                                      int page_size, const int32_t* idx, int64_t idx_stride,
@@ -550,7 +575,10 @@ extern "C" int dsa_sparse_mla_decode(void* o, int o_dtype, float* lse, const voi
   p.q_bf16 = q_dtype == DSA_BF16;
   p.o_bf16 = o_dtype == DSA_BF16;
   p.scale_log2 = (float)(scale * 1.4426950408889634);
-  if (n_splits > 1) {
+  // the tensor-core kernel merges the slices of a row inside a cluster when
+  // it can; otherwise slices leave partial states for the merge kernel
+  const bool partials = n_splits > 1 && !(use_tc && tc_cluster_size(n_splits) > 1);
+  if (partials) {
     const size_t need = (size_t)B * n_head * n_splits * (DV + 2) * sizeof(float);
     DSA_REQUIRE(workspace != nullptr && workspace_bytes >= need, DSA_ERR_WORKSPACE,
                 "sparse_mla_decode: workspace needs %zu bytes, got %zu", need, workspace_bytes);
@@ -571,6 +599,6 @@ extern "C" int dsa_sparse_mla_decode(void* o, int o_dtype, float* lse, const voi
     st = check_launch("sparse_mla_decode_kernel");
   }
   if (st != DSA_OK) return st;
-  if (n_splits > 1) st = launch_sparse_mla_merge(p, s);
+  if (partials) st = launch_sparse_mla_merge(p, s);
   return st;
 }

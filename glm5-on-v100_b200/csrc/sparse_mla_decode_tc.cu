@@ -72,6 +72,7 @@ constexpr uint32_t MISC_BYTES = 2048;
 constexpr uint32_t SMEM_BYTES = SM_MISC + MISC_BYTES + 1024;  // + alignment slack = 232,448
 constexpr uint32_t S_COL = 256;             // S^T of buffer x at [256 + 64x, +64); O^T tile j at [64j, 64j+64)
 constexpr uint32_t TMEM_COLS = 512;
+constexpr uint32_t kSendOff = 112 * 1024;   // epilogue: outgoing rows after received rows + staged output
 constexpr int ROW_BYTES = 656;
 constexpr float kLn2 = 0.69314718055994530942f;
 constexpr float kRescaleThreshold = 8.0f;   // log2 units: P stays <= 256
@@ -85,6 +86,9 @@ constexpr uint32_t IDESC_PV = idesc_f16(128, NH, true, true);
 
 static_assert(TM == 64, "M = 64 QK tiles");
 static_assert(SMEM_BYTES <= 232448, "shared memory budget");
+// cluster epilogue (csize 2 or 4): received (csize-1) x W x 256 B + output 128 W B
+// below kSendOff; (csize-1) x W x 256 B to send above it, below the misc block
+static_assert(3 * 128 * 256 + 128 * 128 <= kSendOff && kSendOff + 3 * 128 * 256 <= SM_MISC, "epilogue layout");
 
 __device__ int32_t g_tc_error;  // sticky: DSA_ERR_TIMEOUT when a bounded wait expired
 
@@ -214,7 +218,49 @@ __device__ __forceinline__ void store_rope(const Tile& T, uint8_t* buf, int w, i
 }
 
 // Row table for slice rows [r0, r0 + n): physical row, kRowZero or kRowSkip;
-// written by threads [0, nthreads) of the block.
+// written by threads [0, nthreads) of the block. Each thread takes four rows
+// at a time and issues their four index loads, then their four block-table
+// loads, so a batch costs two dependent memory round trips.
+__device__ __forceinline__ void resolve_rows_batched(const SparseMlaArgs& p, int b, int seq_len, int r0, int n,
+                                                     int* table, int nthreads) {
+  const int* idx = p.idx + (int64_t)b * p.idx_stride + r0;
+  const int* bt = p.bt + (int64_t)b * p.bt_stride;
+  for (int i0 = threadIdx.x; i0 < n; i0 += 4 * nthreads) {
+    int pos[4], blk[4], code[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int i = i0 + k * nthreads;
+      pos[k] = i < n ? idx[i] : -1;
+    }
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      code[k] = kRowSkip;
+      blk[k] = 0;
+      if (pos[k] >= 0 && pos[k] < seq_len) {
+        code[k] = kRowZero;
+        const int blk_i = pos[k] / p.page_size;
+        if (blk_i < p.max_blocks) {
+          blk[k] = bt[blk_i];
+          pos[k] -= blk_i * p.page_size;  // offset in the page
+          code[k] = 0;                    // resolved below
+        }
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int i = i0 + k * nthreads;
+      if (i >= n) break;
+      if (code[k] == 0) {
+        const int64_t r = (int64_t)blk[k] * p.page_size + pos[k];
+        code[k] = (r >= 0 && r < p.n_kv_rows) ? (int)r : kRowZero;
+      }
+      table[i] = code[k];
+    }
+  }
+}
+
+// Row table for slice rows [r0, r0 + n) (a later window of a long slice), one
+// row per thread at a time.
 __device__ __forceinline__ void resolve_rows(const SparseMlaArgs& p, int b, int seq_len, int r0, int n, int* table,
                                              int nthreads) {
   for (int i = threadIdx.x; i < n; i += nthreads) {
@@ -232,14 +278,15 @@ __device__ __forceinline__ void resolve_rows(const SparseMlaArgs& p, int b, int 
   }
 }
 
-__global__ void __launch_bounds__(NTHREADS, 1) sparse_mla_decode_tc_kernel(const SparseMlaArgs p, int32_t* err) {
+__global__ void __launch_bounds__(NTHREADS, 1) sparse_mla_decode_tc_kernel(const SparseMlaArgs p, int32_t* err,
+                                                                                  int csize) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_base = smem_u32(smem_raw);
   const uint32_t base = (raw_base + 1023u) & ~1023u;
   uint8_t* sm = smem_raw + (base - raw_base);
   int* table = reinterpret_cast<int*>(sm + SM_TABLE);
   uint8_t* misc = sm + SM_MISC;
-  // misc: [0, 72) 9 mbarriers | 80 TMEM base | 84 abort | 88 any_rescale |
+  // misc: [0, 80) 10 mbarriers | 80 TMEM base | 84 abort | 88 any_rescale |
   // [96, 160) ovf | [160, 288) s_valid | [288, 1824) per-head floats
   uint64_t* mbar = reinterpret_cast<uint64_t*>(misc);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(misc + 80);
@@ -257,6 +304,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) sparse_mla_decode_tc_kernel(const
   auto mb_p_full = [&](int x) { return mb0 + 32u + 8u * (uint32_t)x; };    // softmax: P^T written
   auto mb_kv_free = [&](int x) { return mb0 + 48u + 8u * (uint32_t)x; };   // PV done: buffer and O^T released
   const uint32_t mb_done = mb0 + 64u;
+  const uint32_t mb_recv = mb0 + 72u;  // rows sent by the other CTAs of the cluster have landed
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int b = blockIdx.x;
@@ -278,6 +326,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) sparse_mla_decode_tc_kernel(const
         mbar_init(mb_kv_free(x), 1);
       }
       mbar_init(mb_done, 1);
+      mbar_init(mb_recv, 1);
       mbar_init_fence();
       *abort_flag = 0;
       *any_rescale = 0;
@@ -285,26 +334,46 @@ __global__ void __launch_bounds__(NTHREADS, 1) sparse_mla_decode_tc_kernel(const
     __syncwarp();
     tmem_alloc(smem_u32(tmem_slot), TMEM_COLS);
   }
-  {
+  // Setup in two halves that overlap: the producers resolve the first table
+  // window and issue tile 0's loads (held in registers across the barrier)
+  // while warps 16-31 stage Q.
+  Tile T;
+  if (warp < PRODUCERS) {
+    // pad the table so that reads for rows past the slice are "not counted"
+    resolve_rows_batched(p, b, seq_len, lo, min(nrows, TABLE_ROWS), table, PRODUCERS * 32);
+    for (int i = min(nrows, TABLE_ROWS) + threadIdx.x; i < min(ntiles * TM, TABLE_ROWS); i += PRODUCERS * 32)
+      table[i] = kRowSkip;
+    named_bar(2, PRODUCERS * 32);
+    if (ntiles > 0) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) load_group(T, p.kv, table, 0, j, warp, lane);
+      load_tail(T, p.kv, table, 0, warp, lane);
+    }
+  } else {
+    // Q: every 16-byte chunk this thread owns is copied at once (cp.async)
+    // into the second tile buffer, idle until tile 1, then converted to fp16
+    // into the swizzled Q operand; a thread converts only its own chunks
     const int nheads = min(NH, p.n_head - h0);
-    for (int i = threadIdx.x; i < NH * 72; i += NTHREADS) {
+    const int tid = threadIdx.x - PRODUCERS * 32;
+    constexpr int kQThreads = NTHREADS - PRODUCERS * 32;
+    uint8_t* qraw = sm + SM_KV + KV_BUF;
+    const uint8_t* qg = reinterpret_cast<const uint8_t*>(p.q) + ((int64_t)b * p.n_head + h0) * 576 * 2;
+    for (int i = tid; i < nheads * 72; i += kQThreads) cp_async16(smem_u32(qraw + 16 * i), qg + 16 * i);
+    cp_async_commit();
+    cp_async_wait<0>();
+    for (int i = tid; i < NH * 72; i += kQThreads) {
       const int h = i / 72, c = i % 72;
       uint4 v = make_uint4(0, 0, 0, 0);
       if (h < nheads) {
-        v = *reinterpret_cast<const uint4*>(reinterpret_cast<const uint8_t*>(p.q) +
-                                            (((int64_t)b * p.n_head + h0 + h) * 576 + 8 * c) * 2);
+        v = *reinterpret_cast<const uint4*>(qraw + 16 * i);
         if (p.q_bf16) v = bf16x8_to_half8(v);
       }
       *reinterpret_cast<uint4*>(sm + SM_Q + (c >> 3) * Q_REGION + sw128_off(h, c & 7)) = v;
     }
-    if (threadIdx.x < NH) {
-      m_ref[threadIdx.x] = -1e30f;
-      alpha[threadIdx.x] = 1.f;
+    if (tid < NH) {
+      m_ref[tid] = -1e30f;
+      alpha[tid] = 1.f;
     }
-    // pad the table so that reads for rows past the slice are "not counted"
-    resolve_rows(p, b, seq_len, lo, min(nrows, TABLE_ROWS), table, NTHREADS);
-    for (int i = min(nrows, TABLE_ROWS) + threadIdx.x; i < min(ntiles * TM, TABLE_ROWS); i += NTHREADS)
-      table[i] = kRowSkip;
   }
   fence_proxy_async();
   fence_before_sync();
@@ -326,8 +395,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) sparse_mla_decode_tc_kernel(const
   if (warp < PRODUCERS) {
     // ------------------------------------------------------------- producers
     const int w = warp;
-    Tile T;
-    bool have_next = false;  // tile t's data was prefetched during iteration t-1
+    bool have_next = true;  // tile t's data is in registers (tile 0: loaded during setup)
     for (int t = 0; t < ntiles; ++t) {
       const int x = t & 1;
       const uint32_t ph = (t >> 1) & 1;
@@ -602,71 +670,172 @@ __global__ void __launch_bounds__(NTHREADS, 1) sparse_mla_decode_tc_kernel(const
     ok = mbar_wait(mb_kv_free((ntiles - 1) & 1), ((ntiles - 1) >> 1) & 1, abort_flag, err, kWaitTimeoutNs);
   __syncthreads();
   // A thread whose wait failed set the abort flag before this barrier, so
-  // every thread reads the same decision.
+  // every thread reads the same decision; nothing sets it after this point.
   const bool live = *abort_flag == 0;
-  __syncthreads();
-  const int sp = warp & 3;                // TMEM sub-partition: lanes [32*sp, 32*sp+32)
-  const int hb = 16 * ((warp >> 2) & 3);  // heads [hb, hb + 16), for warps 0-15
+  const bool have_o = live && ntiles > 0;  // O^T holds this slice's accumulation
+  const int sp = warp & 3;                 // TMEM sub-partition: lanes [32*sp, 32*sp+32)
   const uint32_t t_lane = (uint32_t)(32 * sp) << 16;
-  if (ntiles > 0 && live) {
-    fence_after_sync();
-    if (threadIdx.x < NH)
-      l_sum[threadIdx.x] = (tmax[threadIdx.x] + tmax[64 + threadIdx.x]) + (tmax[128 + threadIdx.x] + tmax[192 + threadIdx.x]);
+  if (threadIdx.x < NH)
+    l_sum[threadIdx.x] =
+        have_o ? (tmax[threadIdx.x] + tmax[64 + threadIdx.x]) + (tmax[128 + threadIdx.x] + tmax[192 + threadIdx.x])
+               : 0.f;
+  fence_after_sync();
+  if (csize == 1 && p.n_splits > 1) {
+    // ------------------------------------------- partial state of this slice
     __syncthreads();
+    const int hb = 16 * ((warp >> 2) & 3);  // heads [hb, hb + 16), for warps 0-15
 #pragma unroll 1
     for (int j = 0; j < 4 && warp < 16; ++j) {
       uint32_t o[16];
-      tmem_ld16(tmem + t_lane + 64 * j + hb, o);
-      tmem_wait_ld();
+      if (have_o) {
+        tmem_ld16(tmem + t_lane + 64 * j + hb, o);
+        tmem_wait_ld();
+      } else {
+#pragma unroll
+        for (int h = 0; h < 16; ++h) o[h] = 0u;
+      }
       const int d = 128 * j + 32 * sp + lane;
 #pragma unroll 4
       for (int h = 0; h < 16; ++h) {
         const int head = h0 + hb + h;
         if (head >= p.n_head) break;
-        const float val = __uint_as_float(o[h]);
-        if (p.n_splits == 1) {
-          const float l = l_sum[hb + h];
-          const float out = l > 0.f ? val / l : 0.f;
-          const int64_t off = ((int64_t)b * p.n_head + head) * DV + d;
-          if (p.o_bf16)
-            reinterpret_cast<__nv_bfloat16*>(p.o)[off] = __float2bfloat16_rn(out);
-          else
-            reinterpret_cast<__half*>(p.o)[off] = __float2half_rn(out);
-        } else {
-          p.part_o[(((int64_t)b * p.n_head + head) * p.n_splits + split) * DV + d] = val;
-        }
+        p.part_o[(((int64_t)b * p.n_head + head) * p.n_splits + split) * DV + d] = __uint_as_float(o[h]);
       }
     }
     if (threadIdx.x < NH && h0 + (int)threadIdx.x < p.n_head) {
-      const float l = l_sum[threadIdx.x], m = m_ref[threadIdx.x];
       const int64_t bh = (int64_t)b * p.n_head + h0 + threadIdx.x;
-      if (p.n_splits == 1) {
-        p.lse[bh] = l > 0.f ? (m + log2f(l)) * kLn2 : -INFINITY;
-      } else {
-        p.part_ml[(bh * p.n_splits + split) * 2] = m;
-        p.part_ml[(bh * p.n_splits + split) * 2 + 1] = l;
-      }
+      p.part_ml[(bh * p.n_splits + split) * 2] = m_ref[threadIdx.x];
+      p.part_ml[(bh * p.n_splits + split) * 2 + 1] = l_sum[threadIdx.x];
     }
-  } else if (ntiles == 0) {
-    // empty slice: o = 0 / lse = -inf, or an empty partial state
-    for (int i = threadIdx.x; i < NH * DV; i += NTHREADS) {
-      const int head = h0 + i / DV, d = i % DV;
-      if (head >= p.n_head) continue;
-      const int64_t bh = (int64_t)b * p.n_head + head;
-      if (p.n_splits == 1) {
-        if (p.o_bf16)
-          reinterpret_cast<__nv_bfloat16*>(p.o)[bh * DV + d] = __float2bfloat16_rn(0.f);
-        else
-          reinterpret_cast<__half*>(p.o)[bh * DV + d] = __float2half_rn(0.f);
-        if (d == 0) p.lse[bh] = -INFINITY;
+  } else {
+    // ------------------------------------------------- final o and lse
+    // The csize slices of this row form one cluster; CTA `rank` owns value
+    // dims [rank*W, rank*W + W). Each CTA sends the raw O^T rows that other
+    // CTAs own into their shared memory (the tile buffers are free by now),
+    // then combines its own rows with what it received: the flash-decode
+    // reduction o = sum_s w_s o_s / sum_s w_s l_s, w_s = 2^(m_s - max m) over
+    // slices with l_s > 0 (dsa.cu:1136-1184), with lse = -inf and o = 0 when
+    // nothing was counted.
+    const int W = DV / csize;
+    const uint32_t rank = csize > 1 ? cluster_rank() : 0u;
+    const uint32_t xbytes = (uint32_t)W * 256;  // one sender's rows: [W dims][64 heads] f32, 16-byte chunks XOR-swizzled by dim
+    uint8_t* xbuf = sm + SM_KV;                   // [csize - 1 senders] received rows
+    uint8_t* ybuf = xbuf + (csize - 1) * xbytes;  // [64 heads][W dims] in o's type
+    uint8_t* gbuf = sm + SM_KV + kSendOff;        // [csize - 1 receivers] rows to send
+    float* fac = tmax;                            // [csize][64] w_s / sum (tmax is dead once l_sum is formed)
+    const int g = warp >> 2;  // 8 warps per sub-partition: chunks g and g + 8 of its 16 (tile j, 16 heads)
+    if (csize > 1) {
+      // stage the rows other CTAs own, one contiguous block per receiver
+#pragma unroll 1
+      for (int c = g; c < 16; c += 8) {
+        const int j = c >> 2, cb = c & 3;
+        const int dv0 = 128 * j + 32 * sp;  // this warp's 32 dims
+        const int owner = dv0 / W;
+        if (owner == (int)rank) continue;
+        uint32_t o[16];
+        if (have_o) {
+          tmem_ld16(tmem + t_lane + 64 * j + 16 * cb, o);
+          tmem_wait_ld();
+        } else {
+#pragma unroll
+          for (int h = 0; h < 16; ++h) o[h] = 0u;
+        }
+        const int oi = owner < (int)rank ? owner : owner - 1;
+        const int dl = dv0 + lane - owner * W;
+        uint8_t* row = gbuf + oi * xbytes + dl * 256;
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          *reinterpret_cast<uint4*>(row + (((4 * cb + e) ^ (dl & 15)) << 4)) =
+              make_uint4(o[4 * e], o[4 * e + 1], o[4 * e + 2], o[4 * e + 3]);
+      }
+      fence_proxy_async();  // the staged rows are read by the bulk copies
+      if (threadIdx.x == 0) mbar_arrive_expect_tx(mb_recv, (uint32_t)(csize - 1) * xbytes);
+      cluster_sync();  // every CTA of the cluster is past its tile loop, its m, l published and rows staged
+      if (threadIdx.x < (unsigned)(csize - 1)) {
+        const int oi = threadIdx.x;
+        const int owner = oi < (int)rank ? oi : oi + 1;
+        const int slot = (int)rank < owner ? (int)rank : (int)rank - 1;
+        const uint32_t dst = cluster_map(smem_u32(xbuf + slot * xbytes), owner);
+        const uint32_t mb = cluster_map(mb_recv, owner);
+        for (uint32_t off = 0; off < xbytes; off += 16384u)
+          bulk_copy_to_peer(dst + off, smem_u32(gbuf + oi * xbytes) + off, 16384u, mb);
+      }
+    } else {
+      __syncthreads();
+    }
+    if (threadIdx.x < NH) {
+      const int h = threadIdx.x;
+      auto m_of = [&](int q) { return csize > 1 ? ld_cluster_f32(cluster_map(smem_u32(&m_ref[h]), q)) : m_ref[h]; };
+      auto l_of = [&](int q) { return csize > 1 ? ld_cluster_f32(cluster_map(smem_u32(&l_sum[h]), q)) : l_sum[h]; };
+      float M = -INFINITY;
+      for (int q = 0; q < csize; ++q)
+        if (l_of(q) > 0.f) M = fmaxf(M, m_of(q));
+      float L = 0.f;
+      for (int q = 0; q < csize; ++q) {
+        const float l = l_of(q);
+        const float w = l > 0.f ? exp2f(m_of(q) - M) : 0.f;
+        fac[q * 64 + h] = w;
+        L += l * w;
+      }
+      const float inv = L > 0.f ? 1.f / L : 0.f;
+      for (int q = 0; q < csize; ++q) fac[q * 64 + h] *= inv;
+      if (rank == 0 && h0 + h < p.n_head)
+        p.lse[(int64_t)b * p.n_head + h0 + h] = L > 0.f ? (M + log2f(L)) * kLn2 : -INFINITY;
+    }
+    __syncthreads();  // fac visible
+    if (csize > 1) mbar_wait(mb_recv, 0, abort_flag, err, kWaitTimeoutNs);  // received rows landed
+    const int ybytes = W * 2;  // one head's row of ybuf
+#pragma unroll 1
+    for (int c = g; c < 16; c += 8) {
+      const int j = c >> 2, cb = c & 3;
+      const int dv0 = 128 * j + 32 * sp;
+      if (dv0 / W != (int)rank) continue;
+      uint32_t o[16];
+      if (have_o) {
+        tmem_ld16(tmem + t_lane + 64 * j + 16 * cb, o);
+        tmem_wait_ld();
       } else {
-        p.part_o[(bh * p.n_splits + split) * DV + d] = 0.f;
-        if (d == 0) {
-          p.part_ml[(bh * p.n_splits + split) * 2] = -1e30f;
-          p.part_ml[(bh * p.n_splits + split) * 2 + 1] = 0.f;
+#pragma unroll
+        for (int h = 0; h < 16; ++h) o[h] = 0u;
+      }
+      // o[] becomes the combined value in place (f32 bits)
+#pragma unroll
+      for (int h = 0; h < 16; ++h) o[h] = __float_as_uint(fac[rank * 64 + 16 * cb + h] * __uint_as_float(o[h]));
+      const int dl = dv0 + lane - (int)rank * W;
+      for (int q = 0; q < csize; ++q) {
+        if (q == (int)rank) continue;
+        const int slot = q < (int)rank ? q : q - 1;
+        const uint8_t* row = xbuf + ((size_t)slot * W + dl) * 256;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float4 v = *reinterpret_cast<const float4*>(row + (((4 * cb + e) ^ (dl & 15)) << 4));
+          const float* f = fac + q * 64 + 16 * cb + 4 * e;
+          o[4 * e] = __float_as_uint(fmaf(f[0], v.x, __uint_as_float(o[4 * e])));
+          o[4 * e + 1] = __float_as_uint(fmaf(f[1], v.y, __uint_as_float(o[4 * e + 1])));
+          o[4 * e + 2] = __float_as_uint(fmaf(f[2], v.z, __uint_as_float(o[4 * e + 2])));
+          o[4 * e + 3] = __float_as_uint(fmaf(f[3], v.w, __uint_as_float(o[4 * e + 3])));
         }
       }
+      uint8_t* y = ybuf + 16 * cb * ybytes + dl * 2;
+#pragma unroll
+      for (int h = 0; h < 16; ++h) {
+        if (p.o_bf16)
+          *reinterpret_cast<__nv_bfloat16*>(y + h * ybytes) = __float2bfloat16_rn(__uint_as_float(o[h]));
+        else
+          *reinterpret_cast<__half*>(y + h * ybytes) = __float2half_rn(__uint_as_float(o[h]));
+      }
     }
+    __syncthreads();
+    // 16-byte coalesced stores of this CTA's W dims of every head
+    const int cpr = W / 8;  // 16-byte chunks per head
+    for (int i = threadIdx.x; i < NH * cpr; i += NTHREADS) {
+      const int h = i / cpr, c8 = i % cpr;
+      if (h0 + h >= p.n_head) continue;
+      *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(p.o) +
+                                (((int64_t)b * p.n_head + h0 + h) * DV + (int)rank * W + 8 * c8) * 2) =
+          *reinterpret_cast<const uint4*>(ybuf + h * ybytes + c8 * 16);
+    }
+    if (csize > 1) cluster_sync();  // every copy out of this CTA's memory has landed before it exits
   }
   // every MMA of this CTA has completed before TMEM is released (a commit
   // tracks the MMAs of the thread that issues it: lane 0 of the MMA warp
@@ -687,6 +856,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) sparse_mla_decode_tc_kernel(const
 std::once_flag g_once[kMaxDevices];
 int g_status[kMaxDevices];
 int32_t* g_err_ptr[kMaxDevices];
+int g_cluster_ctas[kMaxDevices][3];  // [log2 csize]: CTAs resident at once in clusters of csize (0: unusable)
 
 int ensure_setup(int dev) {
   if (dev < 0 || dev >= kMaxDevices) {
@@ -700,6 +870,27 @@ int ensure_setup(int dev) {
     if (e == cudaSuccess) e = cudaGetSymbolAddress(&ptr, g_tc_error);
     g_err_ptr[dev] = reinterpret_cast<int32_t*>(ptr);
     g_status[dev] = (int)e;
+    g_cluster_ctas[dev][0] = sm_count(dev);
+    for (int l = 1; l < 3 && e == cudaSuccess; ++l) {
+      const int c = 1 << l;
+      cudaLaunchConfig_t cfg{};
+      cfg.gridDim = dim3(1, 1, 16 * c);
+      cfg.blockDim = dim3(NTHREADS);
+      cfg.dynamicSmemBytes = SMEM_BYTES;
+      cudaLaunchAttribute attr{};
+      attr.id = cudaLaunchAttributeClusterDimension;
+      attr.val.clusterDim.x = 1;
+      attr.val.clusterDim.y = 1;
+      attr.val.clusterDim.z = c;
+      cfg.attrs = &attr;
+      cfg.numAttrs = 1;
+      int n = 0;
+      if (cudaOccupancyMaxActiveClusters(&n, sparse_mla_decode_tc_kernel, &cfg) != cudaSuccess) {
+        cudaGetLastError();  // a refused size only disables that size
+        n = 0;
+      }
+      g_cluster_ctas[dev][l] = n * c;
+    }
   });
   if (g_status[dev] != 0) {
     set_error("sparse_mla_decode_tc setup: %s", cudaGetErrorString((cudaError_t)g_status[dev]));
@@ -708,7 +899,17 @@ int ensure_setup(int dev) {
   return DSA_OK;
 }
 
+int log2_csize(int n_splits) { return n_splits == 2 ? 1 : n_splits == 4 ? 2 : -1; }  // the epilogue layout holds 4
+
 }  // namespace
+
+int tc_cluster_size(int n_splits) {
+  const int l = log2_csize(n_splits);
+  if (l < 0) return 1;
+  const int dev = current_device();
+  if (ensure_setup(dev) != DSA_OK) return 1;
+  return g_cluster_ctas[dev][l] > 0 ? n_splits : 1;
+}
 
 int tc_choose_splits(int B, int head_tiles, int topk, int nsm) {
   const int ntiles = (topk + TM - 1) / TM;
@@ -719,10 +920,17 @@ int tc_choose_splits(int B, int head_tiles, int topk, int nsm) {
   for (int s = 1; s <= 32 && s <= ntiles; ++s) {
     const int per = (ntiles + s - 1) / s;
     if ((ntiles + per - 1) / per != s) continue;
-    const double waves = std::ceil(units * s / nsm);
-    // cost in tile times: a tile of TM fp8 rows moves TM x 656 B; a slice's
-    // partial state is written and merged (2 x 128 KB)
-    double cost = waves * per + (s > 1 ? units * s * 2.0 * NH * DV * 4.0 / ((double)nsm * TM * ROW_BYTES) : 0.0);
+    // slices of a row merge in a cluster (s = 2, 4, 8, when clusters of s
+    // fit) or through partial states that a second kernel re-reads
+    const bool cl = s > 1 && tc_cluster_size(s) == s;
+    int cap = nsm;
+    if (cl) cap = g_cluster_ctas[current_device()][log2_csize(s)];
+    const double waves = std::ceil(units * s / std::max(cap, 1));
+    // cost in tile times: a tile of TM fp8 rows moves TM x 656 B; each wave
+    // adds about one tile of setup and epilogue; a partial state is written
+    // and merged (2 x 128 KB)
+    double cost = waves * (per + 1.0);
+    if (s > 1 && !cl) cost += units * s * 2.0 * NH * DV * 4.0 / ((double)nsm * TM * ROW_BYTES);
     if (cost < best_cost - 1e-9) {
       best_cost = cost;
       best = s;
@@ -735,8 +943,24 @@ int launch_sparse_mla_tc(const SparseMlaArgs& a, cudaStream_t s) {
   const int dev = current_device();
   int st = ensure_setup(dev);
   if (st != DSA_OK) return st;
-  const dim3 grid(a.B, (a.n_head + NH - 1) / NH, a.n_splits);
-  sparse_mla_decode_tc_kernel<<<grid, NTHREADS, SMEM_BYTES, s>>>(a, g_err_ptr[dev]);
+  const int csize = a.n_splits > 1 ? tc_cluster_size(a.n_splits) : 1;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(a.B, (a.n_head + NH - 1) / NH, a.n_splits);
+  cfg.blockDim = dim3(NTHREADS);
+  cfg.dynamicSmemBytes = SMEM_BYTES;
+  cfg.stream = s;
+  cudaLaunchAttribute attr{};
+  attr.id = cudaLaunchAttributeClusterDimension;
+  attr.val.clusterDim.x = 1;
+  attr.val.clusterDim.y = 1;
+  attr.val.clusterDim.z = csize;
+  cfg.attrs = &attr;
+  cfg.numAttrs = csize > 1 ? 1 : 0;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, sparse_mla_decode_tc_kernel, a, g_err_ptr[dev], csize);
+  if (e != cudaSuccess) {
+    set_error("sparse_mla_decode_tc_kernel launch: %s", cudaGetErrorString(e));
+    return DSA_ERR_CUDA;
+  }
   return check_launch("sparse_mla_decode_tc_kernel");
 }
 

@@ -54,6 +54,17 @@ def _int32(t, name):
 
 
 # ----------------------------------------------------------------- impls
+def decode_plan(B: int, n_head: int, topk: int, kv_format: int) -> dict:
+    """How the decode op runs a problem on the current device: slices of the
+    top-k axis per row, how many merge inside one thread-block cluster, the
+    workspace bytes and the kernel launches per call."""
+    s, c, n = ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
+    ws = ctypes.c_size_t()
+    L.call("dsa_sparse_mla_decode_plan", B, n_head, topk, kv_format, ctypes.byref(s), ctypes.byref(c),
+           ctypes.byref(ws), ctypes.byref(n))
+    return {"n_splits": s.value, "cluster_size": c.value, "workspace_bytes": ws.value, "launches": n.value}
+
+
 def _sparse_mla_decode_impl(o, lse, q, kv_cache, idx, block_table, seq_lens, scale):
     _check(q.is_cuda and kv_cache.is_cuda, "q and kv_cache must be CUDA tensors")
     _check(q.dtype in (torch.float16, torch.bfloat16), "q must be fp16 or bf16")
@@ -83,7 +94,7 @@ def _sparse_mla_decode_impl(o, lse, q, kv_cache, idx, block_table, seq_lens, sca
     page = kv_cache.size(-2)
     n_rows = kv_cache.numel() // row
     with torch.cuda.device(q.device):
-        ws_bytes = L.lib().dsa_sparse_mla_decode_workspace_bytes(B, H, topk)
+        ws_bytes = decode_plan(B, H, topk, fmt)["workspace_bytes"]
         ws = torch.empty(ws_bytes, dtype=torch.uint8, device=q.device) if ws_bytes else None
         L.call("dsa_sparse_mla_decode", _vp(o), _DTYPE[o.dtype], _vp(lse), _vp(q), _DTYPE[q.dtype],
                _vp(kv_cache), fmt, n_rows, page, _vp(idx), idx.stride(0), _vp(block_table),

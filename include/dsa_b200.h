@@ -86,6 +86,17 @@ int dsa_device_error(int reset);
  * ===================================================================== */
 size_t dsa_sparse_mla_decode_workspace_bytes(int B, int n_head, int topk);
 
+/* How dsa_sparse_mla_decode runs a problem with this cache format: the
+ * slices of the top-k axis per row (n_splits), how many of them merge inside
+ * one thread-block cluster (cluster_size; 1 = partial states merged by a
+ * second kernel), the workspace that needs (0 when none) and the kernel
+ * launches per call. No reference counterpart (the reference picks its split
+ * count and allocates the partial buffers inside the op, dsa.cu:2579-2590);
+ * any output pointer may be NULL. */
+int dsa_sparse_mla_decode_plan(int B, int n_head, int topk, int kv_format,
+                               int* n_splits, int* cluster_size,
+                               size_t* workspace_bytes, int* launches);
+
 int dsa_sparse_mla_decode(void* o, int o_dtype, float* lse, const void* q,
                           int q_dtype, const void* kv_cache, int kv_format,
                           int64_t n_kv_rows, int page_size,

@@ -180,6 +180,30 @@ def test_decode_mtp_rows_and_sparse_equals_dense(dsa):
     assert_attn_close(o, lse, o_ref, lse_ref)
 
 
+def test_decode_plan_cluster_and_partial_paths(dsa):
+    """The fp8 path merges the slices of a row inside a thread-block cluster
+    (no workspace, one launch) when the split count is 2 or 4, and falls back
+    to partial states + the merge kernel otherwise; the shapes of
+    test_decode_shapes_and_splits reach both."""
+    from importlib import import_module
+
+    ops = import_module("glm5-on-v100_b200.ops")
+    L = import_module("glm5-on-v100_b200._lib")
+    big = ops.decode_plan(64, 64, 2048, L.DSA_FP8_DS_MLA)
+    assert big["n_splits"] == 2 and big["cluster_size"] == 2
+    assert big["workspace_bytes"] == 0 and big["launches"] == 1
+    seen = set()
+    for B, H, topk in [(1, 8, 2048), (2, 16, 512), (3, 128, 256), (6, 72, 64), (200, 64, 96), (64, 64, 2048)]:
+        pl = ops.decode_plan(B, H, topk, L.DSA_FP8_DS_MLA)
+        assert (pl["cluster_size"] > 1) == (pl["n_splits"] in (2, 4))
+        assert (pl["launches"] == 2) == (pl["n_splits"] > 1 and pl["cluster_size"] == 1)
+        assert (pl["workspace_bytes"] > 0) == (pl["launches"] == 2)
+        seen.add("cluster" if pl["cluster_size"] > 1 else ("partial" if pl["n_splits"] > 1 else "single"))
+    assert seen == {"cluster", "partial", "single"}, seen
+    empty = ops.decode_plan(4, 64, 0, L.DSA_FP8_DS_MLA)
+    assert empty["n_splits"] == 1 and empty["launches"] == 1
+
+
 def test_decode_full_size_sampled_rows(dsa):
     """BASELINE config 2 at 128k context: B=64, H=64, topk=2048, fp8 cache."""
     B, H, S, page, topk = 64, 64, 131072, 64, 2048
