@@ -112,14 +112,34 @@ def test_no_alloc_matches_workspace_entry_twice(fmt):
         assert_close(o, lse, o_ref, lse_ref)
 
 
+def plan(B, topk, kv_format):
+    s, c, n = ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
+    ws = ctypes.c_size_t()
+    assert L.lib().dsa_sparse_mla_decode_plan(B, H, topk, kv_format, ctypes.byref(s), ctypes.byref(c),
+                                              ctypes.byref(ws), ctypes.byref(n)) == L.DSA_OK
+    return s.value, c.value, ws.value
+
+
+def test_no_alloc_cases_use_partial_states():
+    # the fp8 cases above split into slice counts the kernel merges through
+    # partial states (not inside a cluster), so they exercise the scratch
+    for B, topk in [(4, 2048), (6, 1536)]:
+        s, c, ws = plan(B, topk, L.DSA_FP8_DS_MLA)
+        assert s > 1 and c == 1 and 0 < ws <= SCRATCH_BYTES, (B, topk, s, c, ws)
+
+
 def test_no_alloc_rejects_calls_beyond_the_scratch():
-    # many rows with long top-k lists: find one whose slices need > 32 MiB
-    B, topk = 200, 16384
+    # many rows with long top-k lists on the bf16 cache (whose kernel always
+    # merges slices through partial states): one that needs > 32 MiB
+    cand = [(B, topk) for B, topk in [(200, 16384), (400, 16384), (1000, 8192)]
+            if plan(B, topk, L.DSA_BF16)[2] > SCRATCH_BYTES]
+    assert cand, "no candidate shape needs more than the static scratch"
+    B, topk = cand[0]
     q = torch.zeros(B, H, 576, dtype=torch.bfloat16, device=DEV)
-    kv = torch.zeros(1, PAGE, 656, dtype=torch.uint8, device=DEV)
+    kv = torch.zeros(1, PAGE, 576, dtype=torch.bfloat16, device=DEV)
     idx = torch.zeros(B, topk, dtype=torch.int32, device=DEV)
     bt = torch.zeros(B, 1, dtype=torch.int32, device=DEV)
-    x = dict(q=q, kv=kv, kv_format=L.DSA_FP8_DS_MLA, bt=bt, idx=idx,
+    x = dict(q=q, kv=kv, kv_format=L.DSA_BF16, bt=bt, idx=idx,
              seq_lens=torch.ones(B, dtype=torch.int32, device=DEV), B=B, topk=topk)
     o, lse = outputs(B)
     stream = torch.cuda.current_stream().cuda_stream
