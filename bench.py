@@ -445,8 +445,7 @@ class SparsePrefillWorkload(Workload):
         return self.flops(self.T) / 1e12
 
     def launches_per_step(self, dsa):
-        ws = dsa._lib.lib().dsa_sparse_mla_decode_workspace_bytes(self.T, self.H, self.TOPK)
-        return 2 + (1 if ws else 0)
+        return 1 + dsa.ops.decode_plan(self.T, self.H, self.TOPK, dsa._lib.DSA_FP8_DS_MLA)["launches"]
 
     def algorithmic(self):
         return self.flops(self.T), "TFLOP/s", "tensor"
@@ -506,8 +505,190 @@ class SparsePrefillWorkload(Workload):
                 f"(oracle/ref_port.py, fp8 rows dequantised on the host; K scatter not included)")
 
 
+class IndexerDecodeWorkload(Workload):
+    """The indexer half of a BASELINE config 2 decode step: per row, logits
+    with the fused level-1 histogram over its 128k keys in the fp8 indexer-K
+    cache, then the exact top-2048 from that histogram."""
+
+    metric = "decode indexer tok/s @128k ctx (logits + fused histogram + top-2048)"
+    unit = "tok/s"
+    data = "synthetic (seeded random fp8 indexer-K cache, N(0,1) bf16 q, w ~ N(0, 1/32))"
+    B, HI, HD, PAGE, TOPK, NSETS = 64, 32, 128, 64, 2048, 4
+    S = 131072
+    nsets = NSETS
+
+    def bytes_per_row(self):
+        # keys (fp8 + scale), scores written and read back, q, w, histogram,
+        # indices, block table
+        return (self.S * (132 + 4 + 4) + self.HI * self.HD * 2 + self.HI * 4 + 4096 * 4 * 2 + self.TOPK * 4
+                + (self.S // self.PAGE) * 4)
+
+    def config(self):
+        return {"workload": "indexer_decode", "batch": self.B, "indexer_heads": self.HI, "head_dim": self.HD,
+                "ctx": self.S, "topk": self.TOPK, "page": self.PAGE, "k_cache": "fp8 (128 e4m3 + f32 scale)",
+                "q_dtype": "bf16", "w_dtype": "f32",
+                "l2": f"inputs larger than L2: a {self.B * self.S * 132 / 1e9:.1f} GB key cache"}
+
+    def setup(self, dev, seed):
+        g = torch.Generator(device=dev).manual_seed(seed)
+        nb = self.B * (self.S // self.PAGE)
+        kc = torch.randint(0, 256, (nb, self.PAGE, 132), dtype=torch.uint8, device=dev, generator=g)
+        codes = kc[..., :128]
+        codes[(codes & 0x7F) == 0x7F] = 0x7E  # no NaN codes
+        sc = (torch.rand(nb, self.PAGE, 1, device=dev, generator=g) + 0.5) / 448.0
+        kc[..., 128:132] = sc.view(torch.uint8).view(nb, self.PAGE, 4)
+        self.k_cache = kc
+        self.bt = torch.randperm(nb, device=dev, generator=g).view(self.B, -1).to(torch.int32)
+        self.seq = torch.full((self.B,), self.S, dtype=torch.int32, device=dev)
+        self.q = [torch.randn(self.B, self.HI, self.HD, device=dev, generator=g).to(torch.bfloat16)
+                  for _ in range(self.NSETS)]
+        self.w = torch.randn(self.B, self.HI, device=dev, generator=g) / (self.HI ** 0.5)
+        self.score = torch.empty(self.B, self.S, dtype=torch.float32, device=dev)
+        self.hist = torch.zeros(self.B, 4096, dtype=torch.int32, device=dev)
+        self.idx = torch.empty(self.B, self.TOPK, dtype=torch.int32, device=dev)
+
+    def step_on(self, dsa, q, w):
+        self.hist.zero_()
+        dsa.sm70_indexer_logits(self.score, q, self.k_cache, w, self.bt, self.seq, self.hist)
+        dsa.sm70_decode_topk(self.idx, self.score, self.seq, self.hist, self.TOPK)
+
+    def step(self, dsa, i):
+        self.step_on(dsa, self.q[i % self.NSETS], self.w)
+
+    def units_per_step(self):
+        return self.B
+
+    def launches_per_step(self, dsa):
+        return 2  # logits, top-k (the histogram memset is torch's)
+
+    def algorithmic(self):
+        return self.B * self.bytes_per_row(), "GB/s", "hbm"
+
+    def roofline_note(self, kind):
+        return (f"peak {kind} HBM copy; achieved = {self.bytes_per_row()} B/row x {self.B} rows / CUDA-event time "
+                f"of the whole step (logits + top-k)")
+
+    def e2e_setup(self, dev):
+        self.h_q = [t.cpu().pin_memory() for t in self.q]
+        self.h_w = self.w.cpu().pin_memory()
+        self.h_idx = torch.empty(self.idx.shape, dtype=torch.int32).pin_memory()
+        self.d_q = torch.empty_like(self.q[0])
+        self.d_w = torch.empty_like(self.w)
+        return self.h_q[0].numel() * 2 + self.h_w.numel() * 4, self.h_idx.numel() * 4
+
+    def e2e_step(self, dsa, i):
+        self.d_q.copy_(self.h_q[i % self.NSETS], non_blocking=True)
+        self.d_w.copy_(self.h_w, non_blocking=True)
+        self.step_on(dsa, self.d_q, self.d_w)
+        self.h_idx.copy_(self.idx, non_blocking=True)
+
+    def cpu_setup(self, rows):
+        g = torch.Generator().manual_seed(7)
+        self.cpu_rows = rows
+        self.c_k = [torch.randn(self.S, self.HD, generator=g).to(torch.bfloat16) for _ in range(rows)]
+        self.c_q = torch.randn(rows, self.HI, self.HD, generator=g).to(torch.bfloat16)
+        self.c_w = torch.randn(rows, self.HI, generator=g) / (self.HI ** 0.5)
+
+    def cpu_step(self):
+        from oracle.ref_port import indexer_prefill_cpu
+
+        lens = torch.tensor([self.S])
+        for r in range(self.cpu_rows):  # each decode row has keys of its own
+            indexer_prefill_cpu(self.c_q[r:r + 1], self.c_k[r], self.c_w[r:r + 1], lens, self.TOPK)
+
+    def cpu_units(self):
+        return self.cpu_rows
+
+    def cpu_sample(self, steps):
+        return (f"{steps} steps x {self.cpu_rows} rows, each over 131,072 keys of its own (logits + torch.topk, "
+                f"oracle/ref_port.py; keys already decoded to bf16)")
+
+
+class ShardMergeWorkload(Workload):
+    """The exact merge of the key-sharded indexer (BASELINE config 5's
+    8-way key split) on one GPU: for each of R query rows, the global top-2048
+    of 8 shards' local top-2048 (value, position) lists, lowest position first
+    on ties, positions ascending."""
+
+    metric = "indexer shard merge rows/s (8 shards x top-2048)"
+    unit = "rows/s"
+    data = "synthetic (seeded N(0,1) candidate values, distinct positions per shard)"
+    TP, R, TOPK, S = 8, 4096, 2048, 184320
+    nsets = 2
+
+    def bytes_per_row(self):
+        return self.TP * 2 * self.TOPK * 4 + self.TOPK * 4
+
+    def config(self):
+        return {"workload": "shard_merge", "shards": self.TP, "rows": self.R, "topk": self.TOPK,
+                "keys": self.S, "l2": f"inputs larger than L2: {self.nsets} candidate sets of "
+                f"{self.TP * self.R * 2 * self.TOPK * 4 / 1e6:.0f} MB"}
+
+    def _candidates(self, dev, g, R):
+        span = self.S // self.TP
+        vals = torch.randn(self.TP, R, self.TOPK, device=dev, generator=g)
+        base = torch.arange(self.TP, device=dev).view(self.TP, 1, 1) * span
+        off = torch.randint(0, span, (self.TP, R, 1), device=dev, generator=g)
+        pos = (base + (torch.arange(self.TOPK, device=dev).view(1, 1, -1) * 89 + off) % span).to(torch.int32)
+        return torch.cat([vals, pos.view(torch.float32)], dim=2).contiguous()
+
+    def setup(self, dev, seed):
+        g = torch.Generator(device=dev).manual_seed(seed)
+        self.allf = [self._candidates(dev, g, self.R) for _ in range(self.nsets)]
+        self.out = torch.empty(self.R, self.TOPK, dtype=torch.int32, device=dev)
+        self.rows = torch.empty(0, dtype=torch.int32, device=dev)
+
+    def step_on(self, dsa, allf):
+        dsa.sm70_indexer_shard_merge(self.out, allf, self.rows, 0, self.TOPK)
+
+    def step(self, dsa, i):
+        self.step_on(dsa, self.allf[i % self.nsets])
+
+    def units_per_step(self):
+        return self.R
+
+    def launches_per_step(self, dsa):
+        return 1
+
+    def algorithmic(self):
+        return self.R * self.bytes_per_row(), "GB/s", "hbm"
+
+    def roofline_note(self, kind):
+        return (f"peak {kind} HBM copy; achieved = {self.bytes_per_row()} B/row (8 x 2048 candidates in, 2048 "
+                f"positions out) x {self.R} rows / CUDA-event time of the merge launch")
+
+    def e2e_setup(self, dev):
+        self.h_allf = [t.cpu().pin_memory() for t in self.allf]
+        self.h_out = torch.empty(self.out.shape, dtype=torch.int32).pin_memory()
+        self.d_allf = torch.empty_like(self.allf[0])
+        return self.h_allf[0].numel() * 4, self.h_out.numel() * 4
+
+    def e2e_step(self, dsa, i):
+        self.d_allf.copy_(self.h_allf[i % self.nsets], non_blocking=True)
+        self.step_on(dsa, self.d_allf)
+        self.h_out.copy_(self.out, non_blocking=True)
+
+    def cpu_setup(self, rows):
+        g = torch.Generator().manual_seed(7)
+        self.cpu_rows = rows
+        self.c_allf = self._candidates(torch.device("cpu"), g, rows).numpy()
+
+    def cpu_step(self):
+        from oracle.dsa_oracle import shard_merge_torch_epilogue
+
+        shard_merge_torch_epilogue(self.c_allf, self.TOPK)
+
+    def cpu_units(self):
+        return self.cpu_rows
+
+    def cpu_sample(self, steps):
+        return (f"{steps} steps x {self.cpu_rows} rows through the reference's torch merge epilogue "
+                f"(torch.topk over the 8 x 2048 candidates, oracle/dsa_oracle.py)")
+
+
 WORKLOADS = {"decode": DecodeWorkload, "indexer_prefill": IndexerPrefillWorkload,
-             "sparse_prefill": SparsePrefillWorkload}
+             "sparse_prefill": SparsePrefillWorkload, "indexer_decode": IndexerDecodeWorkload,
+             "shard_merge": ShardMergeWorkload}
 
 
 def capture(fn, stream):
@@ -662,7 +843,8 @@ def main():
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.cpu_rows is None:
-        args.cpu_rows = {"decode": 8, "indexer_prefill": 8, "sparse_prefill": 8}[args.workload]
+        args.cpu_rows = {"decode": 8, "indexer_prefill": 8, "sparse_prefill": 8, "indexer_decode": 1,
+                         "shard_merge": 512}[args.workload]
     DecodeWorkload.S = args.ctx
     world, rank, local = dist_setup(args)
     try:

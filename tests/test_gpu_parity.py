@@ -303,6 +303,56 @@ def test_indexer_rows_kernel(dsa, fmt, Hi):
     np.testing.assert_array_equal(h, O.level1_hist(s, c["seq"]))
 
 
+def _logits_cabi(dsa, score, q, kc_ptr, n_kv_rows, page, w, bt, seq, B, Hi, hist):
+    L = dsa._lib
+    L.call("dsa_indexer_logits", score.data_ptr(), score.stride(0), score.size(1), q.data_ptr(), L.DSA_F16,
+           kc_ptr, L.DSA_FP8_IDXK, n_kv_rows, page, w.data_ptr(), L.DSA_F32, bt.data_ptr(), bt.stride(0),
+           bt.size(1), seq.data_ptr(), B, Hi, hist.data_ptr(), torch.cuda.current_stream().cuda_stream)
+
+
+@pytest.mark.parametrize("Hi", [8, 32, 64])
+def test_indexer_paged_rows_kernel_edges(dsa, Hi):
+    """The decode rows kernel for fp8 caches with 64-token pages (bulk page
+    copies, 2048 positions per CTA): missing blocks, a last page partly past
+    the cache, a row of length 0, a row longer than max_kv, a row ending on a
+    CTA boundary and an unaligned score stride. Scores and histogram equal,
+    bit for bit, those of the per-key rows kernel on the same bytes viewed as
+    32-token pages, and match the oracle; nothing is written past max_kv."""
+    B, S = 6, 4500
+    c = logits_case(700 + Hi, B=B, Hi=Hi, S=S, page=64)
+    nb = c["k"].shape[0] // 64
+    n_kv_rows = nb * 64 - 10  # the last page is only partly inside the cache
+    bt = c["bt"].copy()
+    bt[2, 5], bt[2, 9] = -1, nb + 7
+    bt[4, 3] = nb - 1
+    seq = c["seq"].copy()
+    seq[0], seq[1], seq[3], seq[5] = 4500, 0, c["max_kv"] + 50, 2048
+    rows = O.idxk_encode_rows(c["k"])
+    kc = to_dev(rows.reshape(nb, 64, 132))
+    q = to_dev(c["q"], torch.float16)
+    w = to_dev(c["w"], torch.float32)
+    pad = 3
+    out = {}
+    for page in (64, 32):
+        btp = bt if page == 64 else np.stack([2 * bt, 2 * bt + 1], axis=2).reshape(B, -1)
+        btp = np.where((bt if page == 64 else np.repeat(bt, 2, axis=1)) < 0, -1, btp).astype(np.int32)
+        buf = torch.full((B, c["max_kv"] + pad), float("nan"), device=DEV)
+        hist = torch.zeros(B, 4096, dtype=torch.int32, device=DEV)
+        _logits_cabi(dsa, buf[:, : c["max_kv"]], q, kc.data_ptr(), n_kv_rows, page, w, to_dev(btp), to_dev(seq),
+                     B, Hi, hist)
+        torch.cuda.synchronize()
+        assert torch.isnan(buf[:, c["max_kv"]:]).all()
+        out[page] = (buf[:, : c["max_kv"]].cpu().numpy(), hist.cpu().numpy())
+    s64, h64 = out[64]
+    s32, h32 = out[32]
+    np.testing.assert_array_equal(s64.view(np.uint32), s32.view(np.uint32))
+    np.testing.assert_array_equal(h64, h32)
+    k_ref = O.idxk_decode_rows(rows)[:n_kv_rows]
+    ref = O.indexer_logits(c["q"], k_ref, c["w"], bt, seq, 64, c["max_kv"])
+    assert_scores_close(s64, ref)
+    np.testing.assert_array_equal(h64, O.level1_hist(s64, seq))
+
+
 @pytest.mark.parametrize("fmt", ["f16", "bf16", "fp8"])
 def test_indexer_tiles_kernel_causal(dsa, fmt):
     c = logits_case(200, B=150, Hi=32, S=3000, page=64, shared_bt=True, causal=True)
