@@ -839,13 +839,14 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
     ap.add_argument("--ctx", type=int, default=DecodeWorkload.S,
-                    help="decode context length (smaller values make the ncu profiling case)")
+                    help="decode / decode-indexer context length (smaller values make the ncu profiling case)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.cpu_rows is None:
         args.cpu_rows = {"decode": 8, "indexer_prefill": 8, "sparse_prefill": 8, "indexer_decode": 1,
                          "shard_merge": 512}[args.workload]
     DecodeWorkload.S = args.ctx
+    IndexerDecodeWorkload.S = args.ctx
     world, rank, local = dist_setup(args)
     try:
         if args.impl == "reference":

@@ -381,7 +381,7 @@ constexpr int PG = 64;
 constexpr int PG_BYTES = PG * IDXK_ROW;  // 8,448 (a multiple of 16)
 constexpr int PG_SUB = 128;              // keys per sub-tile (two pages)
 constexpr int PG_STAGES = 4;             // sub-tiles in flight
-constexpr int PG_CTA_KEYS = 2048;        // keys per CTA
+constexpr int PG_CTA_KEYS = 4096;        // keys per CTA
 constexpr int PG_NT = 256;               // 8 warps x 16 keys
 constexpr uint64_t kPgTimeoutNs = 2000000000ull;
 

@@ -28,11 +28,14 @@
 namespace dsa {
 namespace {
 
-constexpr int NT = 512;
-constexpr int NWARP = NT / 32;
+// Threads per row: 512 (two CTAs per SM) when rows fill the GPU, 1024 when
+// there are fewer rows than half the SMs (decode batches).
+constexpr int NT_SMALL = 512;
+constexpr int NT_LARGE = 1024;
 constexpr int NBIN1 = 4096;
 constexpr int CAP = 8192;  // candidates of the threshold bin kept in shared memory
 constexpr int KMAX = 4096;
+constexpr int SWEEP_U = 4;  // 128-position steps whose loads a warp issues together
 
 struct TopkParams {
   int32_t* idx;
@@ -52,15 +55,17 @@ struct TopkSmem {
   int32_t sure[KMAX];
   int32_t sel[KMAX];
   uint32_t warp[64];
-  uint32_t warp_off[NWARP];
+  uint32_t warp_off[32];
   int T;
   uint32_t above, total;
 };
 
 // Block-wide: find the largest bin T with count(bins >= T) >= need, scanning
 // `nbins` bins (contiguous runs per thread). Writes T and count(bins > T).
+template <int NT>
 __device__ void find_threshold(const uint32_t* hist, int nbins, uint32_t need, uint32_t* s_warp, int* s_T,
                                uint32_t* s_above) {
+  constexpr int NWARP = NT / 32;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int per = (nbins + NT - 1) / NT;
   if (tid == 0) {  // defined result even for an inconsistent caller histogram
@@ -111,7 +116,9 @@ __device__ void find_threshold(const uint32_t* hist, int nbins, uint32_t need, u
 }
 
 // Block-wide exclusive prefix of v in thread order; *s_total gets the sum.
+template <int NT>
 __device__ __forceinline__ uint32_t block_exclusive(uint32_t v, uint32_t* s_warp, uint32_t* s_total) {
+  constexpr int NWARP = NT / 32;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   uint32_t inc = v;
 #pragma unroll
@@ -167,6 +174,7 @@ __device__ __forceinline__ int count_below(const int32_t* a, int m, int32_t x) {
 
 // Rows whose threshold bin overflows the candidate buffer: two more radix
 // levels and an ordered compaction, all over global memory.
+template <int NT>
 __device__ void select_global(const float* row, int n, int K, uint32_t T1, uint32_t need2, int32_t* out,
                               TopkSmem& s) {
   const int tid = threadIdx.x;
@@ -177,7 +185,7 @@ __device__ void select_global(const float* row, int n, int K, uint32_t T1, uint3
     if ((key >> 20) == T1) atomicAdd(&s.hist[(key >> 8) & 0xFFFu], 1u);
   }
   __syncthreads();
-  find_threshold(s.hist, NBIN1, need2, s.warp, &s.T, &s.above);
+  find_threshold<NT>(s.hist, NBIN1, need2, s.warp, &s.T, &s.above);
   const uint32_t pre2 = (T1 << 12) | (uint32_t)s.T;
   const uint32_t need3 = need2 - s.above;
   for (int i = tid; i < 256; i += NT) s.hist[i] = 0;
@@ -187,7 +195,7 @@ __device__ void select_global(const float* row, int n, int K, uint32_t T1, uint3
     if ((key >> 8) == pre2) atomicAdd(&s.hist[key & 0xFFu], 1u);
   }
   __syncthreads();
-  find_threshold(s.hist, 256, need3, s.warp, &s.T, &s.above);
+  find_threshold<NT>(s.hist, 256, need3, s.warp, &s.T, &s.above);
   const uint32_t kth = (pre2 << 8) | (uint32_t)s.T;
   const uint32_t n_ties = need3 - s.above;
   uint32_t out_base = 0, tie_base = 0;
@@ -196,17 +204,19 @@ __device__ void select_global(const float* row, int n, int K, uint32_t T1, uint3
     const bool in = i < n;
     const uint32_t key = in ? monotone32(__ldg(row + i)) : 0u;
     const bool eq = in && key == kth;
-    const uint32_t tie_rank = tie_base + block_exclusive(eq ? 1u : 0u, s.warp, &s.total);
+    const uint32_t tie_rank = tie_base + block_exclusive<NT>(eq ? 1u : 0u, s.warp, &s.total);
     const uint32_t n_eq = s.total;
     const bool sel = in && (key > kth || (eq && tie_rank < n_ties));
-    const uint32_t pos = out_base + block_exclusive(sel ? 1u : 0u, s.warp, &s.total);
+    const uint32_t pos = out_base + block_exclusive<NT>(sel ? 1u : 0u, s.warp, &s.total);
     if (sel && pos < (uint32_t)K) out[pos] = i;
     out_base += s.total;
     tie_base += n_eq;
   }
 }
 
-__global__ void __launch_bounds__(NT, 2) topk_rows_kernel(const TopkParams p) {
+template <int NT>
+__global__ void __launch_bounds__(NT, 1024 / NT) topk_rows_kernel(const TopkParams p) {
+  constexpr int NWARP = NT / 32;
   extern __shared__ __align__(16) unsigned char smem_raw[];
   TopkSmem& s = *reinterpret_cast<TopkSmem*>(smem_raw);
   const int b = blockIdx.x;
@@ -231,39 +241,47 @@ __global__ void __launch_bounds__(NT, 2) topk_rows_kernel(const TopkParams p) {
   } else {
     for (int i = tid; i < NBIN1; i += NT) s.hist[i] = 0;
     __syncthreads();
-    for (int i0 = w0; i0 < w1; i0 += 128) {
-      const int i = i0 + 4 * lane;
-      uint32_t k[4];
-      load4(row, i, w1, vec, k);
+    for (int i0 = w0; i0 < w1; i0 += 128 * SWEEP_U) {
+      uint32_t kq[SWEEP_U][4];
 #pragma unroll
-      for (int e = 0; e < 4; ++e)
-        if (i + e < w1) atomicAdd(&s.hist[k[e] >> 20], 1u);
+      for (int u = 0; u < SWEEP_U; ++u) load4(row, i0 + 128 * u + 4 * lane, w1, vec, kq[u]);
+#pragma unroll
+      for (int u = 0; u < SWEEP_U; ++u) {
+        const int i = i0 + 128 * u + 4 * lane;
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          if (i + e < w1) atomicAdd(&s.hist[kq[u][e] >> 20], 1u);
+      }
     }
   }
   __syncthreads();
-  find_threshold(s.hist, NBIN1, (uint32_t)K, s.warp, &s.T, &s.above);
+  find_threshold<NT>(s.hist, NBIN1, (uint32_t)K, s.warp, &s.T, &s.above);
   const uint32_t T1 = (uint32_t)s.T;
   const uint32_t n_above1 = s.above;
   const uint32_t need2 = (uint32_t)K - n_above1;
   const uint32_t cnt1 = s.hist[T1];
   __syncthreads();
   if (cnt1 > (uint32_t)CAP || n_above1 > (uint32_t)KMAX) {
-    select_global(row, n, K, T1, need2, out, s);
+    select_global<NT>(row, n, K, T1, need2, out, s);
     return;
   }
 
   // ---- 2. ordered sweep: sure positions (bin > T1) and candidates (bin == T1)
   uint32_t ns = 0, nc = 0;
-  for (int i0 = w0; i0 < w1; i0 += 128) {
-    const int i = i0 + 4 * lane;
-    uint32_t k[4];
-    load4(row, i, w1, vec, k);
+  for (int i0 = w0; i0 < w1; i0 += 128 * SWEEP_U) {
+    uint32_t kq[SWEEP_U][4];
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      if (i + e >= w1) continue;
-      const uint32_t bin = k[e] >> 20;
-      ns += bin > T1;
-      nc += bin == T1;
+    for (int u = 0; u < SWEEP_U; ++u) load4(row, i0 + 128 * u + 4 * lane, w1, vec, kq[u]);
+#pragma unroll
+    for (int u = 0; u < SWEEP_U; ++u) {
+      const int i = i0 + 128 * u + 4 * lane;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        if (i + e >= w1) continue;
+        const uint32_t bin = kq[u][e] >> 20;
+        ns += bin > T1;
+        nc += bin == T1;
+      }
     }
   }
   // per-warp totals -> warp offsets (sure in the low half, candidates high)
@@ -293,43 +311,48 @@ __global__ void __launch_bounds__(NT, 2) topk_rows_kernel(const TopkParams p) {
   const uint32_t n_cand = min(s.total >> 16, (uint32_t)CAP);
   // every lane takes the same number of steps (the shuffles below need the
   // whole warp); positions past w1 count as absent
-  for (int i0 = w0; i0 < w1; i0 += 128) {
-    const int i = i0 + 4 * lane;
-    uint32_t k[4];
-    load4(row, i, w1, vec, k);
-    uint32_t cs = 0, cc = 0;
+  for (int i0 = w0; i0 < w1; i0 += 128 * SWEEP_U) {
+    uint32_t kq[SWEEP_U][4];
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      if (i + e >= w1) continue;
-      cs += (k[e] >> 20) > T1;
-      cc += (k[e] >> 20) == T1;
-    }
-    uint32_t inc = cs | (cc << 16);
+    for (int u = 0; u < SWEEP_U; ++u) load4(row, i0 + 128 * u + 4 * lane, w1, vec, kq[u]);
 #pragma unroll
-    for (int off = 1; off < 32; off <<= 1) {
-      const uint32_t u = __shfl_up_sync(0xffffffffu, inc, off);
-      if (lane >= off) inc += u;
-    }
-    const uint32_t tot = __shfl_sync(0xffffffffu, inc, 31);
-    const uint32_t ex = inc - (cs | (cc << 16));
-    uint32_t ps = off_s + (ex & 0xFFFFu), pc = off_c + (ex >> 16);
+    for (int u = 0; u < SWEEP_U; ++u) {
+      const int i = i0 + 128 * u + 4 * lane;
+      const uint32_t* k = kq[u];
+      uint32_t cs = 0, cc = 0;
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      if (i + e >= w1) continue;
-      const uint32_t bin = k[e] >> 20;
-      if (bin > T1) {
-        if (ps < (uint32_t)KMAX) s.sure[ps] = i + e;
-        ++ps;
-      } else if (bin == T1) {
-        if (pc < (uint32_t)CAP) {
-          s.cand_key[pc] = k[e];
-          s.cand_pos[pc] = i + e;
-        }
-        ++pc;
+      for (int e = 0; e < 4; ++e) {
+        if (i + e >= w1) continue;
+        cs += (k[e] >> 20) > T1;
+        cc += (k[e] >> 20) == T1;
       }
+      uint32_t inc = cs | (cc << 16);
+#pragma unroll
+      for (int off = 1; off < 32; off <<= 1) {
+        const uint32_t up = __shfl_up_sync(0xffffffffu, inc, off);
+        if (lane >= off) inc += up;
+      }
+      const uint32_t tot = __shfl_sync(0xffffffffu, inc, 31);
+      const uint32_t ex = inc - (cs | (cc << 16));
+      uint32_t ps = off_s + (ex & 0xFFFFu), pc = off_c + (ex >> 16);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        if (i + e >= w1) continue;
+        const uint32_t bin = k[e] >> 20;
+        if (bin > T1) {
+          if (ps < (uint32_t)KMAX) s.sure[ps] = i + e;
+          ++ps;
+        } else if (bin == T1) {
+          if (pc < (uint32_t)CAP) {
+            s.cand_key[pc] = k[e];
+            s.cand_pos[pc] = i + e;
+          }
+          ++pc;
+        }
+      }
+      off_s += tot & 0xFFFFu;
+      off_c += tot >> 16;
     }
-    off_s += tot & 0xFFFFu;
-    off_c += tot >> 16;
   }
   __syncthreads();
 
@@ -338,7 +361,7 @@ __global__ void __launch_bounds__(NT, 2) topk_rows_kernel(const TopkParams p) {
   __syncthreads();
   for (int i = tid; i < (int)n_cand; i += NT) atomicAdd(&s.hist[(s.cand_key[i] >> 8) & 0xFFFu], 1u);
   __syncthreads();
-  find_threshold(s.hist, NBIN1, need2, s.warp, &s.T, &s.above);
+  find_threshold<NT>(s.hist, NBIN1, need2, s.warp, &s.T, &s.above);
   const uint32_t T2 = (uint32_t)s.T;
   const uint32_t need3 = need2 - s.above;
   __syncthreads();
@@ -349,7 +372,7 @@ __global__ void __launch_bounds__(NT, 2) topk_rows_kernel(const TopkParams p) {
     if (((key >> 8) & 0xFFFu) == T2) atomicAdd(&s.hist[key & 0xFFu], 1u);
   }
   __syncthreads();
-  find_threshold(s.hist, 256, need3, s.warp, &s.T, &s.above);
+  find_threshold<NT>(s.hist, 256, need3, s.warp, &s.T, &s.above);
   const uint32_t kth = (T1 << 20) | (T2 << 8) | (uint32_t)s.T;
   const uint32_t n_ties = need3 - s.above;
   __syncthreads();
@@ -360,14 +383,14 @@ __global__ void __launch_bounds__(NT, 2) topk_rows_kernel(const TopkParams p) {
   const int c0 = min((int)n_cand, tid * per), c1 = min((int)n_cand, c0 + per);
   uint32_t my_eq = 0;
   for (int i = c0; i < c1; ++i) my_eq += s.cand_key[i] == kth;
-  uint32_t tie = block_exclusive(my_eq, s.warp, &s.total);
+  uint32_t tie = block_exclusive<NT>(my_eq, s.warp, &s.total);
   uint32_t my_sel = 0;
   for (int i = c0; i < c1; ++i) {
     const uint32_t key = s.cand_key[i];
     if (key > kth || (key == kth && tie < n_ties)) ++my_sel;
     tie += key == kth;
   }
-  uint32_t sp = block_exclusive(my_sel, s.warp, &s.total);
+  uint32_t sp = block_exclusive<NT>(my_sel, s.warp, &s.total);
   const uint32_t n_sel = min(s.total, (uint32_t)KMAX);
   tie -= my_eq;
   for (int i = c0; i < c1; ++i) {
@@ -407,14 +430,21 @@ int run_topk(const TopkParams& p, int B, cudaStream_t s) {
   const int dev = current_device();
   DSA_REQUIRE(dev >= 0 && dev < kMaxDevices, DSA_ERR_UNSUPPORTED, "topk: device %d out of range", dev);
   std::call_once(g_once[dev], [dev] {
-    g_status[dev] = (int)cudaFuncSetAttribute(topk_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                              (int)sizeof(TopkSmem));
+    cudaError_t e = cudaFuncSetAttribute(topk_rows_kernel<NT_SMALL>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)sizeof(TopkSmem));
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(topk_rows_kernel<NT_LARGE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               (int)sizeof(TopkSmem));
+    g_status[dev] = (int)e;
   });
   if (g_status[dev] != 0) {
     set_error("cudaFuncSetAttribute(topk): %s", cudaGetErrorString((cudaError_t)g_status[dev]));
     return DSA_ERR_CUDA;
   }
-  topk_rows_kernel<<<B, NT, sizeof(TopkSmem), s>>>(p);
+  if (2 * B < sm_count(dev))
+    topk_rows_kernel<NT_LARGE><<<B, NT_LARGE, sizeof(TopkSmem), s>>>(p);
+  else
+    topk_rows_kernel<NT_SMALL><<<B, NT_SMALL, sizeof(TopkSmem), s>>>(p);
   return check_launch("topk_rows_kernel");
 }
 

@@ -313,7 +313,7 @@ def _logits_cabi(dsa, score, q, kc_ptr, n_kv_rows, page, w, bt, seq, B, Hi, hist
 @pytest.mark.parametrize("Hi", [8, 32, 64])
 def test_indexer_paged_rows_kernel_edges(dsa, Hi):
     """The decode rows kernel for fp8 caches with 64-token pages (bulk page
-    copies, 2048 positions per CTA): missing blocks, a last page partly past
+    copies, 4096 positions per CTA): missing blocks, a last page partly past
     the cache, a row of length 0, a row longer than max_kv, a row ending on a
     CTA boundary and an unaligned score stride. Scores and histogram equal,
     bit for bit, those of the per-key rows kernel on the same bytes viewed as
@@ -326,7 +326,7 @@ def test_indexer_paged_rows_kernel_edges(dsa, Hi):
     bt[2, 5], bt[2, 9] = -1, nb + 7
     bt[4, 3] = nb - 1
     seq = c["seq"].copy()
-    seq[0], seq[1], seq[3], seq[5] = 4500, 0, c["max_kv"] + 50, 2048
+    seq[0], seq[1], seq[3], seq[5] = 4500, 0, c["max_kv"] + 50, 4096  # 4096 = one CTA's positions
     rows = O.idxk_encode_rows(c["k"])
     kc = to_dev(rows.reshape(nb, 64, 132))
     q = to_dev(c["q"], torch.float16)
