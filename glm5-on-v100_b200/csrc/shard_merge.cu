@@ -78,6 +78,7 @@ __global__ void __launch_bounds__(MNT) shard_merge_kernel(const MergeParams p) {
   __shared__ uint32_t s_cnt;
   __shared__ unsigned long long s_prefix;
   __shared__ uint32_t s_target;
+  __shared__ uint32_t s_eq;  // keys matching the new prefix
   __shared__ int s_ok;
 
   const int r = blockIdx.x;
@@ -157,6 +158,7 @@ __global__ void __launch_bounds__(MNT) shard_merge_kernel(const MergeParams p) {
           if (run + c >= tgt) {
             s_prefix = pfx | ((unsigned long long)(8 * tid + j) << sh);
             s_target = tgt - run;
+            s_eq = c;
             break;
           }
           run += c;
@@ -164,6 +166,9 @@ __global__ void __launch_bounds__(MNT) shard_merge_kernel(const MergeParams p) {
       }
     }
     __syncthreads();
+    // after the value bytes: when every key with the K-th value is needed the
+    // column bytes (which only order equal values) cannot change the cut
+    if (byte == 4 && s_target == s_eq) break;
   }
   const unsigned long long T = s_prefix;
 #pragma unroll
