@@ -103,6 +103,18 @@ __global__ void __launch_bounds__(MNT) shard_merge_kernel(const MergeParams p) {
            (int64_t)r * 2 * K;
   };
 
+  // all of this thread's candidate values are loaded before any is used, so
+  // the loads are in flight together
+  float val[MAX_PER];
+#pragma unroll
+  for (int i = 0; i < MAX_PER; ++i) {
+    const int col = tid + i * MNT;
+    val[i] = 0.f;
+    if (i < nper && col < ncand) {
+      const int s = col / K, c = col - s * K;
+      val[i] = __ldg(slab(s) + c);
+    }
+  }
   unsigned long long key[MAX_PER];
   uint32_t act = 0;
 #pragma unroll
@@ -110,9 +122,7 @@ __global__ void __launch_bounds__(MNT) shard_merge_kernel(const MergeParams p) {
     key[i] = 0ull;
     const int col = tid + i * MNT;
     if (i < nper && col < ncand) {
-      const int s = col / K, c = col - s * K;
-      const float v = slab(s)[c];
-      key[i] = ((unsigned long long)monotone32(v) << 32) | (uint32_t)(ncand - 1 - col);
+      key[i] = ((unsigned long long)monotone32(val[i]) << 32) | (uint32_t)(ncand - 1 - col);
       act |= 1u << i;
     }
   }
