@@ -513,6 +513,7 @@ class IndexerDecodeWorkload(Workload):
     metric = "decode indexer tok/s @128k ctx (logits + fused histogram + top-2048)"
     unit = "tok/s"
     data = "synthetic (seeded random fp8 indexer-K cache, N(0,1) bf16 q, w ~ N(0, 1/32))"
+    traffic_profile = "indexer_decode_b64_ctx128k"
     B, HI, HD, PAGE, TOPK, NSETS = 64, 32, 128, 64, 2048, 4
     S = 131072
     nsets = NSETS
@@ -613,6 +614,7 @@ class ShardMergeWorkload(Workload):
     metric = "indexer shard merge rows/s (8 shards x top-2048)"
     unit = "rows/s"
     data = "synthetic (seeded N(0,1) candidate values, distinct positions per shard)"
+    traffic_profile = "shard_merge_r4096_tp8"
     TP, R, TOPK, S = 8, 4096, 2048, 184320
     nsets = 2
 
