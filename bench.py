@@ -215,8 +215,10 @@ class DecodeWorkload(Workload):
     def config(self):
         return {"workload": "sparse_mla_decode", "batch": self.B, "heads": self.H, "ctx": self.S, "topk": self.TOPK,
                 "page": self.PAGE, "kv_cache": "fp8_ds_mla", "q_dtype": "bf16", "o_dtype": "bf16",
-                "l2": f"inputs larger than L2: idx rotates over {self.NSETS} sets of {self.B}x{self.TOPK} rows "
-                      f"of a {self.B * self.S * ROW_BYTES / 1e9:.1f} GB cache"}
+                "l2": (f"inputs larger than L2: idx rotates over {self.NSETS} sets of {self.B}x{self.TOPK} rows "
+                       f"of a {self.B * self.S * ROW_BYTES / 1e9:.1f} GB cache")
+                if self.B * self.S * ROW_BYTES > 126e6 else
+                f"the whole {self.B * self.S * ROW_BYTES / 1e6:.0f} MB cache fits in L2 at this size"}
 
     def setup(self, dev, seed):
         g = torch.Generator(device=dev).manual_seed(seed)
@@ -840,6 +842,7 @@ def main():
     ap.add_argument("--cpu-steps", type=int, default=5)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
+    ap.add_argument("--batch", type=int, default=None, help="decode / decode-indexer rows per step (default 64)")
     ap.add_argument("--ctx", type=int, default=DecodeWorkload.S,
                     help="decode / decode-indexer context length (smaller values make the ncu profiling case)")
     args = ap.parse_args()
@@ -849,6 +852,9 @@ def main():
                          "shard_merge": 512}[args.workload]
     DecodeWorkload.S = args.ctx
     IndexerDecodeWorkload.S = args.ctx
+    if args.batch is not None:
+        DecodeWorkload.B = args.batch
+        IndexerDecodeWorkload.B = args.batch
     world, rank, local = dist_setup(args)
     try:
         if args.impl == "reference":
