@@ -4,7 +4,10 @@
 // decode kernel :150-329, staged prefill kernel :345-458) and
 // sm70_indexer_logits_packed (:2771-2836, kernel :542-653).
 //
-// Two kernels, both on the tensor cores (m16n8k16, fp32 accumulate):
+// Three kernels here, all on the tensor cores (m16n8k16, fp32 accumulate),
+// beside the tcgen05 prefill kernel of indexer_logits_tc.cu:
+//   * paged rows kernel (decode with an fp8 cache of 64-token pages): bulk
+//     page copies into shared memory, described at the kernel;
 //   * rows kernel (decode, or whenever the caller asks for the fused
 //     histogram): one CTA = one query row x 128 key positions; every row uses
 //     its own block-table row. The q rows of all heads are the MMA's M side,

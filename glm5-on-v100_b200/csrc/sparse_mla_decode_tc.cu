@@ -7,9 +7,9 @@
 //
 // One CTA = one query row x 64 heads x one slice of the top-k axis, processed
 // in tiles of 64 selected latent rows that alternate between two shared-memory
-// buffers, so that one tile is loaded while the previous one is in softmax and
-// PV. The MMAs are "transposed" so that latent rows are the M side and the 64
-// heads are N:
+// buffers, so that one tile is stored while the previous one is in QK, softmax
+// and PV. The MMAs are "transposed" so that latent rows are the M side and the
+// 64 heads are N:
 //   S^T[64 x 64]   = KV[64 x 576] . Q^T          (M = 64; A = KV tile,
 //                                                 K-major; B = Q, K-major)
 //   O^T[512 x 64] += V^T[512 x 64] . P^T         (M = 128 per value tile;
@@ -21,26 +21,32 @@
 // tile's rope columns after QK has consumed them. Q (72 KB) + two tiles
 // (2 x 72 KB) + the slice's row table (8 KB) fill one SM's shared memory.
 //
-// Warp roles (16 warps):
-//   * warps 0-7, producers: 8 rows of every tile each; the 656-byte rows are
+// Warp roles (32 warps, 64 registers each):
+//   * warps 0-15, producers: 4 rows of every tile each; the 656-byte rows are
 //     read with 16-byte coalesced loads into registers, and as soon as a
 //     128-wide scale group of tile t is stored (dequantised: e4m3 bits
 //     expanded to fp16 with integer ops, times the per-group scale, rounded
-//     once) the same registers receive that group of tile t+1, so the next
-//     tile's reads stay in flight while this one is stored.
-//   * warp 12, lane 0: issues QK(t) when tile t is stored and PV(t-1) when its
+//     once) the same registers receive that group of tile t+1; tile t+2's
+//     rows are prefetched into L2 with bulk prefetches.
+//   * warp 24, lane 0: issues QK(t) when tile t is stored and PV(t-1) when its
 //     P^T is written, committing mbarriers that release S, the tile buffer
 //     and (for the softmax) the accumulated O^T.
-//   * warps 8-11, softmax: each thread owns one tile row and 32 heads of S^T
-//     (tcgen05.ld 16x64b). Probabilities use a lazily updated running max per
-//     head, moved (with an in-TMEM rescale of O^T after PV(t-1) completes) only
-//     when a score exceeds it by more than 2^8, so P <= 256 in fp16 while o and
-//     lse stay exact; row sums accumulate in registers.
-// At the start the block resolves the slice's selected positions through the
-// block table into a row table in shared memory, so no dependent index loads
-// sit on the tile pipeline. Every wait on another role or the tensor core is an
-// mbarrier wait bounded by a device-time limit that reports DSA_ERR_TIMEOUT
-// instead of hanging.
+//   * warps 16-23, softmax: two per TMEM sub-partition, each thread one tile
+//     row and 16 heads of S^T (tcgen05.ld 16x64b). Probabilities use a lazily
+//     updated running max per head, moved (with an in-TMEM rescale of O^T
+//     after PV(t-1) completes) only when a score exceeds it by more than 2^8,
+//     so P <= 256 in fp16 while o and lse stay exact; row sums accumulate in
+//     registers.
+//   * the other warps join the block barriers and the epilogue.
+// Setup overlaps its two dependent chains: the producers resolve the slice's
+// selected positions through the block table into a row table in shared
+// memory and issue tile 0's loads while the other warps stage Q (cp.async).
+// When a row's top-k axis is split in 2 or 4 slices, the slices form one
+// thread-block cluster and merge on chip (one DSMEM bulk copy per receiver,
+// see the epilogue); other slice counts write partial states for the merge
+// kernel. Every wait on another role or the tensor core is an mbarrier wait
+// bounded by a device-time limit that reports DSA_ERR_TIMEOUT instead of
+// hanging.
 #include "sparse_mla.cuh"
 #include "tc_common.cuh"
 

@@ -5,7 +5,8 @@
 // calls for prefill (reference/sparse_attn_indexer.py:632-639, :841-848,
 // :873-880).
 //
-// One CTA of 512 threads owns one row, so no cross-CTA arrival counters or
+// One CTA owns one row (512 threads when the rows fill the GPU, 1024 when
+// there are fewer rows than half the SMs), so no cross-CTA arrival counters or
 // spin-waits are needed (the reference's decode kernel spins on co-resident
 // CTAs, dsa.cu:1372-1375). Keys are the 32-bit monotone images of the
 // scores; the K-th largest key is found exactly, keys equal to it are taken
