@@ -304,6 +304,7 @@ class IndexerPrefillWorkload(Workload):
     metric = "indexer prefill TFLOPS (causal QK FLOPs, logits + top-2048)"
     unit = "TFLOP/s"
     data = "synthetic (seeded N(0,1) bf16 q and keys, w ~ N(0, 1/32))"
+    traffic_profile = "indexer_prefill_n65536"
     N, HI, HD, PAGE, TOPK, SUB = 65536, 32, 128, 64, 2048, 4096
 
     def flops(self, rows_lens):
@@ -405,6 +406,7 @@ class SparsePrefillWorkload(Workload):
     metric = "sparse prefill attention TFLOPS (top-2048, 64 heads)"
     unit = "TFLOP/s"
     data = "synthetic (seeded random fp8_ds_mla cache, N(0,1) bf16 q and k)"
+    traffic_profile = "sparse_prefill_t16384_ctx180k"
     T, H, S, PAGE, TOPK = 16384, 64, 180224, 64, 2048
     scale = 1.0 / (192 ** 0.5)
 
