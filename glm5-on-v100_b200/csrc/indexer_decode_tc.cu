@@ -1,0 +1,350 @@
+// Lightning-indexer logits for decode rows on the 5th-generation tensor cores,
+// fp8 indexer-K cache (128 e4m3 + f32 scale per key) in 64-token pages:
+//   score[b, p] = scale_p * sum_h w[b,h] * relu(q[b,h,:] . k_p)  for p < seq_lens[b]
+//   score[b, p] = -inf                                         for seq_lens[b] <= p < max_kv
+// plus the level-1 top-k histogram of the scores (4096 bins of
+// monotone32(score) >> 20). Same function as the reference's decode kernel
+// (csrc/attention/sm70_mla_decode.cu:150-329, histogram :309-319).
+//
+// One CTA = one query row x 4096 positions, in sub-tiles of 128 keys (two
+// pages), 8 warps, two CTAs per SM:
+//   * a page is 64 x 132 = 8,448 contiguous bytes, so each arrives with one
+//     bulk copy (cp.async.bulk, completing on an mbarrier), DSTAGES sub-tiles
+//     ahead;
+//   * all warps expand the staged e4m3 bytes exactly to fp16 into a
+//     128-byte-swizzled key tile (and the key scales into shared memory);
+//   * one thread issues S^T[128 keys x NQ heads] = K . Q^T as eight M=128,
+//     N=NQ, K=16 tcgen05 MMAs (fp32 accumulation in TMEM);
+//   * each thread of the epilogue owns one key and half of the heads: one
+//     tcgen05.ld, then w * relu(s) summed over its heads, the halves combined
+//     through shared memory, times the key's scale.
+// q and w are loaded once per CTA and the histogram is accumulated in shared
+// memory and added to the global one once per CTA. Every wait is bounded by
+// device time; on expiry the CTA records DSA_ERR_TIMEOUT in the sticky status
+// word, drains its own MMAs, frees TMEM and returns.
+#include "indexer_tc.cuh"
+#include "sparse_mla.cuh"
+#include "tc_common.cuh"
+
+namespace dsa {
+namespace {
+
+using namespace tc;
+
+constexpr int HD = 128;
+constexpr int IDXK_ROW = 132;
+constexpr int NBIN = 4096;
+constexpr int DP = 64;                        // page size served
+constexpr int DP_BYTES = DP * IDXK_ROW;       // 8,448
+constexpr int DSUB = 128;                     // keys per sub-tile (MMA M)
+constexpr int DSTAGES = 3;                    // staged sub-tiles
+constexpr int DCTA_KEYS = 4096;               // positions per CTA
+constexpr int DNT = 256;                      // 8 warps
+constexpr uint32_t KT_REGION = DSUB * 128;    // one 64-dim region of the key tile: 16 KB
+constexpr uint64_t kWaitTimeoutNs = 2000000000ull;
+
+template <int NQ>
+struct DecodeTcLayout {
+  static constexpr uint32_t Q_REGION = NQ * 128;                 // one 64-dim region of q
+  static constexpr uint32_t OFF_K = 0;                           // key tile, 2 regions
+  static constexpr uint32_t OFF_Q = OFF_K + 2 * KT_REGION;       // q, 2 regions
+  static constexpr uint32_t OFF_STAGE = OFF_Q + 2 * Q_REGION;    // [DSTAGES][2 pages]
+  static constexpr uint32_t OFF_HIST = OFF_STAGE + DSTAGES * 2 * DP_BYTES;
+  static constexpr uint32_t OFF_W = OFF_HIST + NBIN * 4;         // [NQ]
+  static constexpr uint32_t OFF_SCALE = OFF_W + NQ * 4;          // [DSUB] key scales
+  static constexpr uint32_t OFF_PART = OFF_SCALE + DSUB * 4;     // [DSUB] second-half head sums
+  static constexpr uint32_t OFF_BASE = OFF_PART + DSUB * 4;      // [DSTAGES][2] int64 page bases
+  static constexpr uint32_t OFF_MBAR = OFF_BASE + DSTAGES * 2 * 8;  // [DSTAGES] copies, mma, done
+  static constexpr uint32_t OFF_SLOT = OFF_MBAR + (DSTAGES + 2) * 8;
+  static constexpr uint32_t BYTES = OFF_SLOT + 16 + 1024;        // + alignment slack
+  static constexpr uint32_t TMEM_COLS = NQ < 32 ? 32 : NQ;
+  static_assert(Q_REGION % 1024 == 0 && OFF_STAGE % 1024 == 0, "swizzled regions stay 1024-aligned");
+};
+
+__device__ __forceinline__ float load_weight(const IndexerDecodeTcArgs& a, int64_t i) {
+  if (a.w_dtype == DSA_F32) return reinterpret_cast<const float*>(a.w)[i];
+  if (a.w_dtype == DSA_BF16) return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(a.w)[i]);
+  return __half2float(reinterpret_cast<const __half*>(a.w)[i]);
+}
+
+__device__ __forceinline__ uint32_t e4m3x2_to_half2(uint32_t two_bytes) {
+  const __half2_raw r = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)two_bytes, __NV_E4M3);
+  return *reinterpret_cast<const uint32_t*>(&r);
+}
+
+// NQ/2 consecutive TMEM columns of this thread's lane.
+template <int N>
+__device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, uint32_t (&r)[N]) {
+  if constexpr (N == 32) {
+    tmem_ld32(taddr, r);
+  } else if constexpr (N == 16) {
+    tmem_ld16(taddr, r);
+  } else {
+    static_assert(N == 8, "8, 16 or 32 columns");
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+                 : "r"(taddr));
+  }
+}
+
+template <int NQ>
+__global__ void __launch_bounds__(DNT, 2) indexer_decode_tc_kernel(const IndexerDecodeTcArgs a, int32_t* err) {
+  using Lay = DecodeTcLayout<NQ>;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_base = smem_u32(smem_raw);
+  const uint32_t base = (raw_base + 1023u) & ~1023u;
+  uint8_t* sm = smem_raw + (base - raw_base);
+  uint8_t* ktile = sm + Lay::OFF_K;
+  uint8_t* stage = sm + Lay::OFF_STAGE;
+  uint32_t* sHist = reinterpret_cast<uint32_t*>(sm + Lay::OFF_HIST);
+  float* sW = reinterpret_cast<float*>(sm + Lay::OFF_W);
+  float* sScale = reinterpret_cast<float*>(sm + Lay::OFF_SCALE);
+  float* sPart = reinterpret_cast<float*>(sm + Lay::OFF_PART);
+  int64_t* sBase = reinterpret_cast<int64_t*>(sm + Lay::OFF_BASE);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + Lay::OFF_SLOT);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + Lay::OFF_SLOT + 4);
+  const uint32_t mb0 = base + Lay::OFF_MBAR;        // copies of stage s at mb0 + 8 s
+  const uint32_t mb_mma = mb0 + 8u * DSTAGES;      // MMAs of a sub-tile done
+  const uint32_t mb_done = mb_mma + 8u;            // drain on abort
+
+  const int b = blockIdx.x;
+  const int p0 = blockIdx.y * DCTA_KEYS;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  float* score_row = a.score + (int64_t)b * a.score_stride;
+  const int p_end = min(p0 + DCTA_KEYS, a.max_kv);
+  const int valid_len = min(a.seq_lens[b], a.max_kv);
+  const int v_end = min(p_end, valid_len);  // positions [p0, v_end) are scored
+  for (int i = max(p0, v_end) + tid; i < p_end; i += DNT) score_row[i] = -INFINITY;
+  if (v_end <= p0) return;
+  const int nsub = (v_end - p0 + DSUB - 1) / DSUB;
+  const int32_t* bt_row = a.bt + (int64_t)b * a.bt_stride;
+
+  // Thread 0: bulk copies of sub-tile i's two pages into stage i % DSTAGES.
+  // Page base codes: row of the page's first key (whole page in the cache);
+  // -1: no key of the page is read; -2: the page runs past the cache end
+  // (keys copied one by one).
+  auto issue = [&](int i) {
+    const int st = i % DSTAGES;
+    const uint32_t mb = mb0 + 8u * (uint32_t)st;
+    uint32_t bytes = 0;
+    int64_t pb[2];
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const int pos = p0 + DSUB * i + DP * j;
+      pb[j] = -1;
+      if (pos < v_end) {
+        const int blk_i = pos / DP;
+        if (blk_i < a.max_blocks) {
+          const int64_t r = (int64_t)bt_row[blk_i] * DP;
+          if (r >= 0 && r + DP <= a.n_kv_rows)
+            pb[j] = r;
+          else if (r >= 0 && r < a.n_kv_rows)
+            pb[j] = -2;
+        }
+      }
+      sBase[2 * st + j] = pb[j];  // read after the mbarrier wait
+      if (pb[j] >= 0) bytes += DP_BYTES;
+    }
+    mbar_arrive_expect_tx(mb, bytes);
+#pragma unroll
+    for (int j = 0; j < 2; ++j)
+      if (pb[j] >= 0)
+        asm volatile(
+            "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                smem_u32(stage + (2 * st + j) * DP_BYTES)),
+            "l"(a.k + pb[j] * IDXK_ROW), "r"((uint32_t)DP_BYTES), "r"(mb)
+            : "memory");
+  };
+
+  if (warp == 0) {
+    if (lane == 0) {
+      for (int s = 0; s < DSTAGES; ++s) mbar_init(mb0 + 8u * s, 1);
+      mbar_init(mb_mma, 1);
+      mbar_init(mb_done, 1);
+      mbar_init_fence();
+      *abort_flag = 0;
+    }
+    __syncwarp();
+    tmem_alloc(smem_u32(tmem_slot), Lay::TMEM_COLS);
+  }
+  for (int i = tid; i < NBIN; i += DNT) sHist[i] = 0;
+  // q as the MMA's B operand: NQ rows (heads, zero past n_ihead) x 128 dims,
+  // two 64-dim regions of 128-byte swizzled rows
+  for (int i = tid; i < NQ * 16; i += DNT) {
+    const int h = i >> 4, c = i & 15;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (h < a.n_ihead) {
+      v = *reinterpret_cast<const uint4*>(reinterpret_cast<const uint8_t*>(a.q) +
+                                          (((int64_t)b * a.n_ihead + h) * HD + 8 * c) * 2);
+      if (a.q_bf16) v = bf16x8_to_half8(v);
+    }
+    *reinterpret_cast<uint4*>(sm + Lay::OFF_Q + (c >> 3) * Lay::Q_REGION + sw128_off(h, c & 7)) = v;
+  }
+  for (int h = tid; h < NQ; h += DNT) sW[h] = h < a.n_ihead ? load_weight(a, (int64_t)b * a.n_ihead + h) : 0.f;
+  fence_proxy_async();
+  fence_before_sync();
+  __syncthreads();
+  fence_after_sync();
+  const uint32_t tmem = *tmem_slot;
+  if (tid == 0)
+    for (int i = 0; i < DSTAGES && i < nsub; ++i) issue(i);
+  const uint64_t desc_k = sw128_desc(base + Lay::OFF_K, 16, 1024);
+  const uint64_t desc_q = sw128_desc(base + Lay::OFF_Q, 16, 1024);
+  constexpr uint32_t IDESC = idesc_f16(DSUB, NQ, false, false);
+
+  bool ok = true;
+  bool issued = false;
+  const int sp = warp & 3, half = warp >> 2;  // epilogue: key 32 sp + lane, heads [half NQ/2, +NQ/2)
+  for (int i = 0; i < nsub; ++i) {
+    const int st = i % DSTAGES;
+    const int k0 = p0 + DSUB * i;
+    ok = ok && mbar_wait(mb0 + 8u * (uint32_t)st, (uint32_t)((i / DSTAGES) & 1), abort_flag, err, kWaitTimeoutNs);
+    const uint8_t* sst = stage + 2 * st * DP_BYTES;
+    // expand: item = (key, 16-dim chunk); 4 words in, two 16-byte fp16 chunks out
+#pragma unroll
+    for (int it = tid; it < DSUB * 8; it += DNT) {
+      const int key = it >> 3, c16 = it & 7;
+      const int j = key >> 6;
+      const int64_t pbase = sBase[2 * st + j];
+      uint32_t w[4] = {0u, 0u, 0u, 0u};
+      float sc = 0.f;
+      if (ok && k0 + key < v_end && pbase != -1) {
+        if (pbase >= 0) {  // the staged page (shared-memory loads)
+          // 132-byte rows are only 4-byte aligned: four 32-bit loads
+          const uint32_t src = smem_u32(sst + j * DP_BYTES + (key & 63) * IDXK_ROW) + 16 * c16;
+#pragma unroll
+          for (int e = 0; e < 4; ++e) asm volatile("ld.shared.u32 %0, [%1];" : "=r"(w[e]) : "r"(src + 4 * e));
+          if (c16 == 0)
+            asm volatile("ld.shared.f32 %0, [%1];" : "=f"(sc) : "r"(smem_u32(sst + j * DP_BYTES + (key & 63) * IDXK_ROW) + 128));
+        } else {  // a page that runs past the cache end: this key's own row, if inside
+          const int pos = k0 + key;
+          const int64_t r = (int64_t)bt_row[pos / DP] * DP + (pos % DP);
+          if (r < a.n_kv_rows) {
+            const uint32_t* g = reinterpret_cast<const uint32_t*>(a.k + r * IDXK_ROW + 16 * c16);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) w[e] = __ldg(g + e);
+            if (c16 == 0) sc = __ldg(reinterpret_cast<const float*>(a.k + r * IDXK_ROW + 128));
+          }
+        }
+      }
+      uint32_t hv[8];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        hv[2 * e] = e4m3x2_to_half2(w[e] & 0xFFFFu);
+        hv[2 * e + 1] = e4m3x2_to_half2(w[e] >> 16);
+      }
+      uint8_t* region = ktile + (c16 >> 2) * KT_REGION;
+      *reinterpret_cast<uint4*>(region + sw128_off(key, 2 * (c16 & 3))) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
+      *reinterpret_cast<uint4*>(region + sw128_off(key, 2 * (c16 & 3) + 1)) =
+          make_uint4(hv[4], hv[5], hv[6], hv[7]);
+      if (c16 == 0) sScale[key] = sc;
+    }
+    fence_proxy_async();
+    fence_before_sync();
+    __syncthreads();  // key tile written; stage st fully read
+    if (tid == 0) {
+      if (i + DSTAGES < nsub) issue(i + DSTAGES);
+      if (ok) {
+        fence_after_sync();
+#pragma unroll
+        for (int kb = 0; kb < 2; ++kb)
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            mma_f16_ss(tmem, desc_k + ((kb * KT_REGION + 32 * k) >> 4), desc_q + ((kb * Lay::Q_REGION + 32 * k) >> 4),
+                       IDESC, (kb | k) != 0);
+        mma_commit(mb_mma);
+        issued = true;
+      }
+    }
+    // the commit is skipped only after an abort, which every later wait sees
+    ok = ok && mbar_wait(mb_mma, (uint32_t)(i & 1), abort_flag, err, kWaitTimeoutNs);
+    ok = __all_sync(0xffffffffu, ok);  // tcgen05.ld below is warp-wide
+    fence_after_sync();
+    float s = 0.f;
+    if (ok) {
+      uint32_t acc[NQ / 2];
+      tmem_ld_cols<NQ / 2>(tmem + ((uint32_t)(32 * sp) << 16) + (uint32_t)(half * (NQ / 2)), acc);
+      tmem_wait_ld();
+#pragma unroll
+      for (int h = 0; h < NQ / 2; ++h) s += sW[half * (NQ / 2) + h] * fmaxf(__uint_as_float(acc[h]), 0.f);
+    }
+    const int key = 32 * sp + lane;
+    if (half == 1) sPart[key] = s;
+    __syncthreads();
+    if (half == 0) {
+      const int pos = k0 + key;
+      if (pos < v_end) {
+        const float v = (s + sPart[key]) * sScale[key];
+        atomicAdd(&sHist[monotone32(v) >> 20], 1u);
+        score_row[pos] = v;
+      }
+    }
+    fence_before_sync();
+    __syncthreads();  // the key tile, scales and partial sums are rewritten next
+  }
+  for (int i = tid; i < NBIN; i += DNT) {
+    const uint32_t c = sHist[i];
+    if (c && a.hist) atomicAdd(a.hist + (int64_t)b * NBIN + i, (int)c);
+  }
+  if (tid == 0 && issued && *abort_flag) {  // drain this thread's MMAs before TMEM is freed
+    mma_commit(mb_done);
+    mbar_wait_drain(mb_done, 0, kWaitTimeoutNs);
+  }
+  fence_before_sync();
+  __syncthreads();
+  if (warp == 0) {
+    fence_after_sync();
+    tmem_dealloc(tmem, Lay::TMEM_COLS);
+  }
+}
+
+std::once_flag g_once[kMaxDevices];
+int g_status[kMaxDevices];
+
+int ensure_setup(int dev) {
+  if (dev < 0 || dev >= kMaxDevices) {
+    set_error("indexer_decode_tc: device index %d out of range", dev);
+    return DSA_ERR_UNSUPPORTED;
+  }
+  std::call_once(g_once[dev], [dev] {
+    cudaError_t e = cudaFuncSetAttribute(indexer_decode_tc_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)DecodeTcLayout<16>::BYTES);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(indexer_decode_tc_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               (int)DecodeTcLayout<32>::BYTES);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(indexer_decode_tc_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               (int)DecodeTcLayout<64>::BYTES);
+    g_status[dev] = (int)e;
+  });
+  if (g_status[dev] != 0) {
+    set_error("indexer_decode_tc setup: %s", cudaGetErrorString((cudaError_t)g_status[dev]));
+    return DSA_ERR_CUDA;
+  }
+  return DSA_OK;
+}
+
+}  // namespace
+
+bool indexer_decode_tc_eligible(int k_format, int page_size, int n_ihead, int packed) {
+  return k_format == DSA_FP8_IDXK && page_size == DP && n_ihead >= 1 && n_ihead <= 64 && !packed;
+}
+
+int launch_indexer_decode_tc(const IndexerDecodeTcArgs& a, cudaStream_t s) {
+  const int dev = current_device();
+  int st = ensure_setup(dev);
+  if (st != DSA_OK) return st;
+  int32_t* err = nullptr;
+  st = tc_error_word(dev, &err);
+  if (st != DSA_OK) return st;
+  const dim3 grid(a.B, (a.max_kv + DCTA_KEYS - 1) / DCTA_KEYS);
+  if (a.n_ihead <= 16)
+    indexer_decode_tc_kernel<16><<<grid, DNT, DecodeTcLayout<16>::BYTES, s>>>(a, err);
+  else if (a.n_ihead <= 32)
+    indexer_decode_tc_kernel<32><<<grid, DNT, DecodeTcLayout<32>::BYTES, s>>>(a, err);
+  else
+    indexer_decode_tc_kernel<64><<<grid, DNT, DecodeTcLayout<64>::BYTES, s>>>(a, err);
+  return check_launch("indexer_decode_tc_kernel");
+}
+
+}  // namespace dsa

@@ -4,12 +4,12 @@
 // decode kernel :150-329, staged prefill kernel :345-458) and
 // sm70_indexer_logits_packed (:2771-2836, kernel :542-653).
 //
-// Three kernels here, all on the tensor cores (m16n8k16, fp32 accumulate),
-// beside the tcgen05 prefill kernel of indexer_logits_tc.cu:
-//   * paged rows kernel (decode with an fp8 cache of 64-token pages): bulk
-//     page copies into shared memory, described at the kernel;
-//   * rows kernel (decode, or whenever the caller asks for the fused
-//     histogram): one CTA = one query row x 128 key positions; every row uses
+// Two kernels here, both on the tensor cores (m16n8k16, fp32 accumulate),
+// beside the tcgen05 kernels of indexer_logits_tc.cu (prefill, 16-bit caches)
+// and indexer_decode_tc.cu (decode, fp8 cache in 64-token pages):
+//   * rows kernel (decode rows of the other caches, or whenever the caller
+//     asks for the fused histogram): one CTA = one query row x 128 key
+//     positions; every row uses
 //     its own block-table row. The q rows of all heads are the MMA's M side,
 //     the key tile the N side; relu * w and the head sum are done on the
 //     accumulators in registers, and the level-1 top-k histogram is built
@@ -25,8 +25,6 @@
 // per-key scale is applied to the dot product (scale > 0 commutes with relu).
 #include "common.cuh"
 #include "indexer_tc.cuh"
-#include "sparse_mla.cuh"
-#include "tc_common.cuh"
 
 namespace dsa {
 namespace {
@@ -58,7 +56,6 @@ struct LogitsParams {
   int w_dtype;    // DSA_F16 / DSA_BF16 / DSA_F32
   int packed;     // q in the [32, ceil(B/16), 8, 16, 16] layout
   int nqt;        // ceil(B/16) for the packed layout
-  int32_t* err;   // sticky device status word (bounded waits)
 };
 
 __device__ __forceinline__ float load_w(const LogitsParams& p, int64_t i) {
@@ -369,215 +366,6 @@ __global__ void __launch_bounds__(TILES_NT) indexer_tiles_kernel(const LogitsPar
   }
 }
 
-// ------------------------------------------------------------ paged rows
-// Decode rows over an fp8 cache with 64-token pages (the reference's
-// layout): one CTA = one query row x PG_CTA_KEYS positions, in sub-tiles of
-// two pages (128 keys). A page is 64 x 132 = 8,448 contiguous bytes, so each
-// one arrives with a single bulk copy (cp.async.bulk, completing on an
-// mbarrier), PG_STAGES sub-tiles ahead. The MMA's key fragments are built
-// straight from the staged e4m3 bytes (two bytes -> one f16x2 register, the
-// values the rows kernel expands into shared memory), so every score is
-// computed with the rows kernel's arithmetic in the same order. q and w are
-// loaded once per CTA, and the level-1 histogram is accumulated in shared
-// memory and added to the global one once per CTA.
-constexpr int PG = 64;
-constexpr int PG_BYTES = PG * IDXK_ROW;  // 8,448 (a multiple of 16)
-constexpr int PG_SUB = 128;              // keys per sub-tile (two pages)
-constexpr int PG_STAGES = 4;             // sub-tiles in flight
-constexpr int PG_CTA_KEYS = 4096;        // keys per CTA
-constexpr int PG_NT = 256;               // 8 warps x 16 keys
-constexpr uint64_t kPgTimeoutNs = 2000000000ull;
-
-template <int MT>
-constexpr size_t paged_smem() {
-  return (size_t)PG_STAGES * 2 * PG_BYTES              // staged pages [stage][2 pages]
-         + (size_t)16 * MT * KSTR * 2                   // q
-         + (size_t)NBIN * 4                             // histogram
-         + (size_t)16 * MT * 4                          // w
-         + (size_t)PG_STAGES * 8 + (size_t)PG_STAGES * 2 * 8 + 16;  // mbarriers, page bases, flag
-}
-
-__device__ __forceinline__ uint32_t e4m3x2_to_half2_bits(uint16_t v) {
-  const __half2_raw r = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)v, __NV_E4M3);
-  return *reinterpret_cast<const uint32_t*>(&r);
-}
-
-template <int MT>
-__global__ void __launch_bounds__(PG_NT, 2) indexer_rows_paged_kernel(const LogitsParams p) {
-  extern __shared__ __align__(16) unsigned char smem[];
-  uint8_t* stage = smem;                                                      // [PG_STAGES][2][PG_BYTES]
-  __half* sQ = reinterpret_cast<__half*>(smem + PG_STAGES * 2 * PG_BYTES);    // [16*MT][KSTR]
-  uint32_t* sHist = reinterpret_cast<uint32_t*>(sQ + 16 * MT * KSTR);         // [4096]
-  float* sW = reinterpret_cast<float*>(sHist + NBIN);                         // [16*MT]
-  uint64_t* mbar = reinterpret_cast<uint64_t*>(sW + 16 * MT);                 // [PG_STAGES]
-  int64_t* sBase = reinterpret_cast<int64_t*>(mbar + PG_STAGES);              // [PG_STAGES][2]
-  int* abort_flag = reinterpret_cast<int*>(sBase + 2 * PG_STAGES);
-
-  const int b = blockIdx.x;
-  const int p0 = blockIdx.y * PG_CTA_KEYS;
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  float* score_row = p.score + (int64_t)b * p.score_stride;
-  const int p_end = min(p0 + PG_CTA_KEYS, p.max_kv);
-  const int valid_len = min(p.seq_lens[b], p.max_kv);
-  const int v_end = min(p_end, valid_len);  // positions [p0, v_end) are scored
-  for (int i = max(p0, v_end) + tid; i < p_end; i += PG_NT) score_row[i] = -INFINITY;
-  if (v_end <= p0) return;
-  const int nsub = (v_end - p0 + PG_SUB - 1) / PG_SUB;
-  const int32_t* bt_row = p.bt + (int64_t)b * p.bt_stride;
-  const uint32_t mb0 = smem_u32(&mbar[0]);
-
-  // Thread 0: bulk copies of sub-tile i's pages into stage i % PG_STAGES.
-  // Page base codes: row of the page's first key (whole page in the cache,
-  // bulk-copied); -1: no key of the page is read (past the row, or its block
-  // is missing); -2: the page runs past the cache end (keys copied one by one).
-  auto issue = [&](int i) {
-    const int st = i % PG_STAGES;
-    const uint32_t mb = mb0 + 8u * (uint32_t)st;
-    uint32_t bytes = 0;
-    int64_t base[2];
-#pragma unroll
-    for (int j = 0; j < 2; ++j) {
-      const int pos = p0 + PG_SUB * i + PG * j;
-      base[j] = -1;
-      if (pos < v_end) {
-        const int blk_i = pos >> 6;
-        if (blk_i < p.max_blocks) {
-          const int64_t r = (int64_t)bt_row[blk_i] * PG;
-          if (r >= 0 && r + PG <= p.n_kv_rows)
-            base[j] = r;
-          else if (r >= 0 && r < p.n_kv_rows)
-            base[j] = -2;
-        }
-      }
-      sBase[2 * st + j] = base[j];  // read after the mbarrier wait
-      if (base[j] >= 0) bytes += PG_BYTES;
-    }
-    tc::mbar_arrive_expect_tx(mb, bytes);
-#pragma unroll
-    for (int j = 0; j < 2; ++j)
-      if (base[j] >= 0)
-        asm volatile(
-            "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                smem_u32(stage + (2 * st + j) * PG_BYTES)),
-            "l"(p.k + base[j] * IDXK_ROW), "r"((uint32_t)PG_BYTES), "r"(mb)
-            : "memory");
-  };
-
-  if (tid == 0) {
-    for (int st = 0; st < PG_STAGES; ++st) tc::mbar_init(mb0 + 8u * st, 1);
-    tc::mbar_init_fence();
-    *abort_flag = 0;
-  }
-  for (int i = tid; i < NBIN; i += PG_NT) sHist[i] = 0;
-  for (int i = tid; i < 16 * MT * 16; i += PG_NT) {
-    const int h = i >> 4, c = i & 15;
-    uint4 v = make_uint4(0, 0, 0, 0);
-    if (h < p.n_ihead)
-      v = q_to_mma<false>(
-          *reinterpret_cast<const uint4*>(reinterpret_cast<const uint8_t*>(p.q) + q_chunk_offset(p, b, h, c)),
-          p.q_bf16);
-    *reinterpret_cast<uint4*>(sQ + h * KSTR + 8 * c) = v;
-  }
-  for (int h = tid; h < 16 * MT; h += PG_NT) sW[h] = h < p.n_ihead ? load_w(p, (int64_t)b * p.n_ihead + h) : 0.f;
-  __syncthreads();
-  if (tid == 0)
-    for (int i = 0; i < PG_STAGES && i < nsub; ++i) issue(i);
-  bool ok = true;
-  const int g = lane >> 2, t4 = lane & 3;
-  for (int i = 0; i < nsub; ++i) {
-    const int st = i % PG_STAGES;
-    const int k0 = p0 + PG_SUB * i;  // first position of the sub-tile
-    ok = ok && tc::mbar_wait(mb0 + 8u * (uint32_t)st, (uint32_t)((i / PG_STAGES) & 1), abort_flag, p.err,
-                             kPgTimeoutNs);
-    uint8_t* sst = stage + 2 * st * PG_BYTES;
-    if (sBase[2 * st] == -2 || sBase[2 * st + 1] == -2) {
-      // a page that runs past the cache: copy its keys one by one (zeros past the cache)
-#pragma unroll 1
-      for (int j = 0; j < 2; ++j) {
-        if (sBase[2 * st + j] != -2) continue;
-        for (int e = tid; e < PG * (IDXK_ROW / 4); e += PG_NT) {
-          const int r = e / (IDXK_ROW / 4), wd = e % (IDXK_ROW / 4);
-          const int64_t row = key_row(p, bt_row, k0 + PG * j + r);
-          *reinterpret_cast<uint32_t*>(sst + j * PG_BYTES + r * IDXK_ROW + 4 * wd) =
-              row >= 0 ? __ldg(reinterpret_cast<const uint32_t*>(p.k + row * IDXK_ROW) + wd) : 0u;
-        }
-      }
-      __syncthreads();
-    }
-    // this warp's 16 keys (two n-tiles of 8): key kk = 16 * warp + 8 * n + g
-    float acc[MT][2][4];
-#pragma unroll
-    for (int m = 0; m < MT; ++m)
-#pragma unroll
-      for (int n = 0; n < 2; ++n) acc[m][n][0] = acc[m][n][1] = acc[m][n][2] = acc[m][n][3] = 0.f;
-    const uint8_t* krow[2];
-    bool kval[2];
-#pragma unroll
-    for (int n = 0; n < 2; ++n) {
-      const int kk = 16 * warp + 8 * n + g;
-      const int j = kk >> 6;
-      kval[n] = ok && k0 + kk < v_end && sBase[2 * st + j] != -1;
-      krow[n] = sst + j * PG_BYTES + (kk & 63) * IDXK_ROW + 2 * t4;
-    }
-#pragma unroll
-    for (int ks = 0; ks < HD / 16; ++ks) {
-      uint32_t bfr[2][2];
-#pragma unroll
-      for (int n = 0; n < 2; ++n) {
-        const uint16_t lo = kval[n] ? *reinterpret_cast<const uint16_t*>(krow[n] + 16 * ks) : (uint16_t)0;
-        const uint16_t hi = kval[n] ? *reinterpret_cast<const uint16_t*>(krow[n] + 16 * ks + 8) : (uint16_t)0;
-        bfr[n][0] = e4m3x2_to_half2_bits(lo);
-        bfr[n][1] = e4m3x2_to_half2_bits(hi);
-      }
-#pragma unroll
-      for (int m = 0; m < MT; ++m) {
-        uint32_t a0, a1, a2, a3;
-        ldmatrix_x4(smem_u32(sQ + (16 * m + (lane & 15)) * KSTR + 16 * ks + 8 * (lane >> 4)), a0, a1, a2, a3);
-        mma16816<false>(acc[m][0], a0, a1, a2, a3, bfr[0][0], bfr[0][1]);
-        mma16816<false>(acc[m][1], a0, a1, a2, a3, bfr[1][0], bfr[1][1]);
-      }
-    }
-#pragma unroll
-    for (int n = 0; n < 2; ++n) {
-      const int c0 = 16 * warp + 8 * n + 2 * t4;
-      float s0 = 0.f, s1 = 0.f;
-#pragma unroll
-      for (int m = 0; m < MT; ++m) {
-        const float w0 = sW[16 * m + g], w1 = sW[16 * m + g + 8];
-        s0 += w0 * fmaxf(acc[m][n][0], 0.f) + w1 * fmaxf(acc[m][n][2], 0.f);
-        s1 += w0 * fmaxf(acc[m][n][1], 0.f) + w1 * fmaxf(acc[m][n][3], 0.f);
-      }
-#pragma unroll
-      for (int off = 4; off < 32; off <<= 1) {
-        s0 += __shfl_xor_sync(0xffffffffu, s0, off);
-        s1 += __shfl_xor_sync(0xffffffffu, s1, off);
-      }
-      if (g == 0) {
-#pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          const int kk = c0 + e, pos = k0 + kk;
-          if (pos < v_end) {
-            const int j = kk >> 6;
-            const float sc = (ok && sBase[2 * st + j] != -1)
-                                 ? *reinterpret_cast<const float*>(sst + j * PG_BYTES + (kk & 63) * IDXK_ROW + 128)
-                                 : 0.f;
-            const float v = (e == 0 ? s0 : s1) * sc;
-            if (p.hist) atomicAdd(&sHist[monotone32(v) >> 20], 1u);
-            score_row[pos] = v;
-          }
-        }
-      }
-    }
-    __syncthreads();  // stage st fully read
-    if (tid == 0 && i + PG_STAGES < nsub) issue(i + PG_STAGES);
-  }
-  if (p.hist)
-    for (int i = tid; i < NBIN; i += PG_NT) {
-      const uint32_t c = sHist[i];
-      if (c) atomicAdd(p.hist + (int64_t)b * NBIN + i, (int)c);
-    }
-}
-
 size_t rows_smem(int mt) {
   return (size_t)16 * mt * KSTR * 2 + (size_t)ROWS_KEYS * KSTR * 2 + (size_t)16 * mt * 4 +
          (size_t)ROWS_KEYS * 4 + (size_t)ROWS_KEYS * 8;
@@ -611,9 +399,6 @@ int ensure_attrs(int dev) {
     DSA_SET_ROWS(K_BF16, true, 1) DSA_SET_ROWS(K_BF16, true, 2) DSA_SET_ROWS(K_BF16, true, 4)
     DSA_SET_ROWS(K_FP8, false, 1) DSA_SET_ROWS(K_FP8, false, 2) DSA_SET_ROWS(K_FP8, false, 4)
 #undef DSA_SET_ROWS
-    if (e == cudaSuccess) e = set_smem(indexer_rows_paged_kernel<1>, paged_smem<1>());
-    if (e == cudaSuccess) e = set_smem(indexer_rows_paged_kernel<2>, paged_smem<2>());
-    if (e == cudaSuccess) e = set_smem(indexer_rows_paged_kernel<4>, paged_smem<4>());
     g_status[dev] = (int)e;
   });
   if (g_status[dev] != 0) {
@@ -665,17 +450,25 @@ int run_logits(LogitsParams p, int k_format, int page_size, bool use_rows, cudaS
   const bool bf = p.q_bf16 && k_format == DSA_BF16;
   if (use_rows) {
     const int mt = p.n_ihead <= 16 ? 1 : (p.n_ihead <= 32 ? 2 : 4);
-    if (k_format == DSA_FP8_IDXK && page_size == PG && !p.packed) {
-      st = tc_error_word(current_device(), &p.err);
-      if (st != DSA_OK) return st;
-      const dim3 grid(p.B, (p.max_kv + PG_CTA_KEYS - 1) / PG_CTA_KEYS);
-      if (mt == 1)
-        indexer_rows_paged_kernel<1><<<grid, PG_NT, paged_smem<1>(), s>>>(p);
-      else if (mt == 2)
-        indexer_rows_paged_kernel<2><<<grid, PG_NT, paged_smem<2>(), s>>>(p);
-      else
-        indexer_rows_paged_kernel<4><<<grid, PG_NT, paged_smem<4>(), s>>>(p);
-      return check_launch("indexer_rows_paged_kernel");
+    if (indexer_decode_tc_eligible(k_format, page_size, p.n_ihead, p.packed)) {
+      IndexerDecodeTcArgs t{};
+      t.score = p.score;
+      t.score_stride = p.score_stride;
+      t.max_kv = p.max_kv;
+      t.q = p.q;
+      t.q_bf16 = p.q_bf16;
+      t.n_ihead = p.n_ihead;
+      t.B = p.B;
+      t.k = p.k;
+      t.n_kv_rows = p.n_kv_rows;
+      t.w = p.w;
+      t.w_dtype = p.w_dtype;
+      t.bt = p.bt;
+      t.bt_stride = p.bt_stride;
+      t.max_blocks = p.max_blocks;
+      t.seq_lens = p.seq_lens;
+      t.hist = p.hist;
+      return launch_indexer_decode_tc(t, s);
     }
     if (k_format == DSA_FP8_IDXK)
       launch_rows<K_FP8, false>(p, mt, s);

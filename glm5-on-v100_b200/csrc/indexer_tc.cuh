@@ -30,4 +30,28 @@ bool indexer_tc_eligible(int k_format, int q_bf16, int page_size, int n_ihead, i
                          int max_kv);
 int launch_indexer_logits_tc(const IndexerTcArgs& a, cudaStream_t s);
 
+// Decode rows over an fp8 indexer-K cache (132-byte keys) in 64-token pages:
+// each row with its own block table; scores plus the fused level-1 histogram.
+struct IndexerDecodeTcArgs {
+  float* score;
+  int64_t score_stride;
+  int max_kv;
+  const void* q;       // [B, n_ihead, 128] f16 or bf16
+  int q_bf16;
+  int n_ihead;
+  int B;
+  const uint8_t* k;    // [n_kv_rows / 64, 64, 132] u8
+  int64_t n_kv_rows;
+  const void* w;       // [B, n_ihead]
+  int w_dtype;
+  const int32_t* bt;   // [B, max_blocks]
+  int64_t bt_stride;
+  int max_blocks;
+  const int32_t* seq_lens;
+  int32_t* hist;       // [B, 4096] or null
+};
+
+bool indexer_decode_tc_eligible(int k_format, int page_size, int n_ihead, int packed);
+int launch_indexer_decode_tc(const IndexerDecodeTcArgs& a, cudaStream_t s);
+
 }  // namespace dsa
