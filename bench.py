@@ -692,9 +692,122 @@ class ShardMergeWorkload(Workload):
                 f"(torch.topk over the 8 x 2048 candidates, oracle/dsa_oracle.py)")
 
 
+class DecodeLayerWorkload(Workload):
+    """One DSA decode layer step per row: the indexer (logits with the fused
+    histogram over the row's keys in the fp8 indexer-K cache, exact top-2048)
+    and sparse MLA decode attention over the selected rows of the
+    fp8_ds_mla latent cache; both caches share the block table, as the
+    reference's layer does. At B = 8 and 180k keys this is BASELINE config 5's
+    layer on one GPU."""
+
+    metric = "DSA decode layer tok/s @128k ctx (indexer + top-2048 + sparse MLA)"
+    unit = "tok/s"
+    data = "synthetic (seeded random fp8 indexer-K and fp8_ds_mla caches, N(0,1) q)"
+    B, H, HI, S, PAGE, TOPK, NSETS = 64, 64, 32, 131072, 64, 2048, 4
+    nsets = NSETS
+    scale = 1.0 / (192 ** 0.5)
+
+    def bytes_per_row(self):
+        idx = (self.S * (132 + 4 + 4) + self.HI * 128 * 2 + self.HI * 4 + 4096 * 4 * 2 + self.TOPK * 4
+               + (self.S // self.PAGE) * 4)
+        return idx + DecodeWorkload.bytes_per_row
+
+    def config(self):
+        return {"workload": "decode_layer", "batch": self.B, "heads": self.H, "indexer_heads": self.HI,
+                "ctx": self.S, "topk": self.TOPK, "page": self.PAGE, "kv_cache": "fp8_ds_mla",
+                "k_cache": "fp8 (128 e4m3 + f32 scale)", "q_dtype": "bf16", "o_dtype": "bf16",
+                "l2": f"inputs larger than L2: {self.B * self.S * (ROW_BYTES + 132) / 1e9:.1f} GB of caches"}
+
+    def setup(self, dev, seed):
+        g = torch.Generator(device=dev).manual_seed(seed)
+        nb = self.B * (self.S // self.PAGE)
+        self.kv = random_dsmla_cache(nb, self.PAGE, dev, g)
+        kc = torch.randint(0, 256, (nb, self.PAGE, 132), dtype=torch.uint8, device=dev, generator=g)
+        codes = kc[..., :128]
+        codes[(codes & 0x7F) == 0x7F] = 0x7E
+        sc = (torch.rand(nb, self.PAGE, 1, device=dev, generator=g) + 0.5) / 448.0
+        kc[..., 128:132] = sc.view(torch.uint8).view(nb, self.PAGE, 4)
+        self.k_cache = kc
+        self.bt = torch.randperm(nb, device=dev, generator=g).view(self.B, -1).to(torch.int32)
+        self.seq = torch.full((self.B,), self.S, dtype=torch.int32, device=dev)
+        self.q = [torch.randn(self.B, self.H, 576, device=dev, generator=g).to(torch.bfloat16)
+                  for _ in range(self.NSETS)]
+        self.qi = [torch.randn(self.B, self.HI, 128, device=dev, generator=g).to(torch.bfloat16)
+                   for _ in range(self.NSETS)]
+        self.w = torch.randn(self.B, self.HI, device=dev, generator=g) / (self.HI ** 0.5)
+        self.score = torch.empty(self.B, self.S, dtype=torch.float32, device=dev)
+        self.hist = torch.zeros(self.B, 4096, dtype=torch.int32, device=dev)
+        self.idx = torch.empty(self.B, self.TOPK, dtype=torch.int32, device=dev)
+        self.o = torch.empty(self.B, self.H, 512, dtype=torch.bfloat16, device=dev)
+        self.lse = torch.empty(self.B, self.H, dtype=torch.float32, device=dev)
+
+    def step_on(self, dsa, q, qi, w):
+        self.hist.zero_()
+        dsa.sm70_indexer_logits(self.score, qi, self.k_cache, w, self.bt, self.seq, self.hist)
+        dsa.sm70_decode_topk(self.idx, self.score, self.seq, self.hist, self.TOPK)
+        dsa.sm70_sparse_mla_decode(self.o, self.lse, q, self.kv, self.idx, self.bt, self.seq, self.scale)
+
+    def step(self, dsa, i):
+        self.step_on(dsa, self.q[i % self.NSETS], self.qi[i % self.NSETS], self.w)
+
+    def units_per_step(self):
+        return self.B
+
+    def launches_per_step(self, dsa):
+        return 2 + dsa.ops.decode_plan(self.B, self.H, self.TOPK, dsa._lib.DSA_FP8_DS_MLA)["launches"]
+
+    def algorithmic(self):
+        return self.B * self.bytes_per_row(), "GB/s", "hbm"
+
+    def roofline_note(self, kind):
+        return (f"peak {kind} HBM copy; achieved = {self.bytes_per_row()} B/row (indexer + attention) x {self.B} "
+                f"rows / CUDA-event time of the whole layer step")
+
+    def e2e_setup(self, dev):
+        self.h_q = [t.cpu().pin_memory() for t in self.q]
+        self.h_qi = [t.cpu().pin_memory() for t in self.qi]
+        self.h_w = self.w.cpu().pin_memory()
+        self.h_o = torch.empty(self.o.shape, dtype=self.o.dtype).pin_memory()
+        self.h_lse = torch.empty(self.lse.shape, dtype=self.lse.dtype).pin_memory()
+        self.d_q, self.d_qi, self.d_w = (torch.empty_like(self.q[0]), torch.empty_like(self.qi[0]),
+                                         torch.empty_like(self.w))
+        h2d = self.h_q[0].numel() * 2 + self.h_qi[0].numel() * 2 + self.h_w.numel() * 4
+        return h2d, self.h_o.numel() * 2 + self.h_lse.numel() * 4
+
+    def e2e_step(self, dsa, i):
+        k = i % self.NSETS
+        self.d_q.copy_(self.h_q[k], non_blocking=True)
+        self.d_qi.copy_(self.h_qi[k], non_blocking=True)
+        self.d_w.copy_(self.h_w, non_blocking=True)
+        self.step_on(dsa, self.d_q, self.d_qi, self.d_w)
+        self.h_o.copy_(self.o, non_blocking=True)
+        self.h_lse.copy_(self.lse, non_blocking=True)
+
+    # CPU legs: the two reference CPU paths in sequence on a bounded sample
+    def cpu_setup(self, rows):
+        self._ci = IndexerDecodeWorkload()
+        self._ci.S, self._ci.TOPK = self.S, self.TOPK
+        self._ci.cpu_setup(rows)
+        self._cd = DecodeWorkload()
+        self._cd.S, self._cd.TOPK = self.S, self.TOPK
+        self._cd.cpu_setup(rows)
+        self.cpu_rows = rows
+
+    def cpu_step(self):
+        self._ci.cpu_step()
+        self._cd.cpu_step()
+
+    def cpu_units(self):
+        return self.cpu_rows
+
+    def cpu_sample(self, steps):
+        return (f"{steps} steps x {self.cpu_rows} rows: logits over 131,072 keys + torch.topk, then the reference "
+                f"torch decode path over 2048 rows (oracle/ref_port.py)")
+
+
 WORKLOADS = {"decode": DecodeWorkload, "indexer_prefill": IndexerPrefillWorkload,
              "sparse_prefill": SparsePrefillWorkload, "indexer_decode": IndexerDecodeWorkload,
-             "shard_merge": ShardMergeWorkload}
+             "shard_merge": ShardMergeWorkload, "decode_layer": DecodeLayerWorkload}
 
 
 def capture(fn, stream):
@@ -851,12 +964,14 @@ def main():
     args.warmup = max(args.warmup, 3)
     if args.cpu_rows is None:
         args.cpu_rows = {"decode": 8, "indexer_prefill": 8, "sparse_prefill": 8, "indexer_decode": 1,
-                         "shard_merge": 512}[args.workload]
+                         "shard_merge": 512, "decode_layer": 1}[args.workload]
     DecodeWorkload.S = args.ctx
     IndexerDecodeWorkload.S = args.ctx
+    DecodeLayerWorkload.S = args.ctx
     if args.batch is not None:
         DecodeWorkload.B = args.batch
         IndexerDecodeWorkload.B = args.batch
+        DecodeLayerWorkload.B = args.batch
     world, rank, local = dist_setup(args)
     try:
         if args.impl == "reference":

@@ -26,13 +26,14 @@ def run_ref(*args):
 
 # --workload name -> the config's workload name
 NAMES = {"decode": "sparse_mla_decode", "indexer_prefill": "indexer_prefill", "sparse_prefill": "sparse_prefill",
-         "indexer_decode": "indexer_decode", "shard_merge": "shard_merge"}
+         "indexer_decode": "indexer_decode", "shard_merge": "shard_merge", "decode_layer": "decode_layer"}
 
 
 @pytest.mark.parametrize("workload,extra,unit", [
     ("decode", ["--ctx", "4096", "--cpu-rows", "1"], "tok/s"),
     ("indexer_decode", ["--ctx", "4096", "--cpu-rows", "1"], "tok/s"),
     ("shard_merge", ["--cpu-rows", "16"], "rows/s"),
+    ("decode_layer", ["--ctx", "4096", "--cpu-rows", "1"], "tok/s"),
 ])
 def test_reference_arm_json_line(workload, extra, unit):
     d = run_ref("--workload", workload, *extra)
