@@ -3,7 +3,7 @@
 Run in the build container (it imports the read-only reference checkout, which
 does not exist on GPU boxes):
 
-    python tests/golden/make_golden.py [/path/to/reference]
+    python tests/golden/make_golden.py /path/to/reference
 
 Writes tests/golden/*.npz. Each fixture stores the generator parameters, a
 digest of the regenerated inputs and the reference outputs:
@@ -132,7 +132,9 @@ def shard_merge_fixture(sai_path):
 
 
 def main():
-    ref = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    if len(sys.argv) < 2:
+        sys.exit("usage: python tests/golden/make_golden.py /path/to/reference")
+    ref = sys.argv[1]
     tmla = _load("ref_triton_mla", os.path.join(ref, "reference/triton_mla.py"))
     st = _load("ref_sm70_triton",
                os.path.join(ref, "vllm/v1/attention/backends/mla/prefill/sm70_triton.py"))
