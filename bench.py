@@ -195,6 +195,7 @@ class Workload:
     nsets = 1
     data = "synthetic (seeded)"
     traffic_profile = None
+    graph = True  # steps replayed from CUDA graphs; False: launched eagerly (host-side sequencing)
 
     def roofline_part(self):
         """None, or (graph-capturable callable, its algorithmic amount) for the
@@ -805,9 +806,88 @@ class DecodeLayerWorkload(Workload):
                 f"torch decode path over 2048 rows (oracle/ref_port.py)")
 
 
+class ShardMergeP2PWorkload(ShardMergeWorkload):
+    """The key-sharded indexer's merge over peer memory (one rank per GPU under
+    torchrun): every rank stages its local top-2048 (value, position) lists
+    of R rows in a CUDA IPC slot and merges all ranks' slots with plain peer
+    loads after bounded waits on the peers' staged flags, so each rank ends
+    with the global top-2048 of every row. Launched eagerly: the exchange's
+    sequence numbers live on the host."""
+
+    metric = "indexer P2P shard merge rows/s (tp shards x top-2048, per-rank output)"
+    data = "synthetic (seeded N(0,1) candidate values, distinct positions per shard)"
+    traffic_profile = None
+    graph = False
+    R = 1024  # the P2P slot capacity (the reference's max_num_batched_tokens)
+
+    def config(self):
+        return {"workload": "shard_merge_p2p", "shards": getattr(self, "tp", None), "rows": self.R,
+                "topk": self.TOPK,
+                "keys": self.S, "merge": "p2p (CUDA IPC slots, plain peer loads)",
+                "l2": "each rank's slot is written once per step and read by every rank"}
+
+    def setup(self, dev, seed):
+        import importlib as _il
+
+        import torch.distributed as dist
+
+        if not dist.is_initialized() or dist.get_world_size() < 2:
+            raise SystemExit("shard_merge_p2p needs torchrun with 2 or more ranks (one per GPU)")
+        self.tp = dist.get_world_size()
+        self.rank = dist.get_rank()
+        self.TP = self.tp
+        sai = _il.import_module("glm5-on-v100_b200.sparse_attn_indexer")
+        cpu = dist.new_group(backend="gloo")
+        self.shard = sai.ShardConfig(tp=self.tp, rank=self.rank, cpu_group=cpu, merge="p2p", rows_cap=self.R)
+        self._merge = sai.merge_shards
+        g = torch.Generator(device=dev).manual_seed(seed)
+        span = self.S // max(self.tp, 1)
+        self.vals = [torch.randn(self.R, self.TOPK, device=dev, generator=g) for _ in range(self.nsets)]
+        off = torch.randint(0, span, (self.R, 1), device=dev, generator=g)
+        self.pos = ((self.rank * span + (torch.arange(self.TOPK, device=dev).view(1, -1) * 89 + off) % span)
+                    .to(torch.int32).contiguous())
+        self.out = torch.empty(self.R, self.TOPK, dtype=torch.int32, device=dev)
+
+    def bytes_per_row(self):
+        return self.tp * 2 * self.TOPK * 4 + self.TOPK * 4
+
+    def step_on(self, dsa, vals):
+        self._merge([(0, self.R, vals, self.pos)], self.out, self.TOPK, self.shard)
+
+    def step(self, dsa, i):
+        self.step_on(dsa, self.vals[i % self.nsets])
+
+    def units_per_step(self):
+        return self.R
+
+    def launches_per_step(self, dsa):
+        return 4  # staged and merged flags, slot-reuse wait, merge kernel
+
+    def roofline_note(self, kind):
+        return (f"peak {kind} HBM copy; achieved = {self.bytes_per_row()} B/row ({self.tp} slots of 2 x 2048 x 4 B "
+                f"read, {self.tp - 1} of them over NVLink, 2048 positions written) x {self.R} rows / CUDA-event time "
+                f"of the eager step")
+
+    def e2e_setup(self, dev):
+        self.h_vals = [t.cpu().pin_memory() for t in self.vals]
+        self.h_out = torch.empty(self.out.shape, dtype=torch.int32).pin_memory()
+        self.d_vals = torch.empty_like(self.vals[0])
+        return self.h_vals[0].numel() * 4, self.h_out.numel() * 4
+
+    def e2e_step(self, dsa, i):
+        self.d_vals.copy_(self.h_vals[i % self.nsets], non_blocking=True)
+        self.step_on(dsa, self.d_vals)
+        self.h_out.copy_(self.out, non_blocking=True)
+
+    def cpu_setup(self, rows):
+        self.TP = getattr(self, "tp", 2)
+        super().cpu_setup(rows)
+
+
 WORKLOADS = {"decode": DecodeWorkload, "indexer_prefill": IndexerPrefillWorkload,
              "sparse_prefill": SparsePrefillWorkload, "indexer_decode": IndexerDecodeWorkload,
-             "shard_merge": ShardMergeWorkload, "decode_layer": DecodeLayerWorkload}
+             "shard_merge": ShardMergeWorkload, "decode_layer": DecodeLayerWorkload,
+             "shard_merge_p2p": ShardMergeP2PWorkload}
 
 
 def capture(fn, stream):
@@ -836,20 +916,32 @@ def run_ours(args, world, rank, local):
     hbm_peak, tf_burst, tf_sustained, peak_kind = load_peaks()
 
     stream = torch.cuda.Stream(dev)
+    graphs = []
     with torch.cuda.stream(stream):
         for i in range(args.warmup):
             wl.step(dsa, i)
         stream.synchronize()
-        graphs = [capture(lambda k=k: wl.step(dsa, k), stream) for k in range(wl.nsets)]
-        for i in range(max(3, args.warmup)):
-            graphs[i % wl.nsets].replay()
+        if wl.graph:
+            graphs = [capture(lambda k=k: wl.step(dsa, k), stream) for k in range(wl.nsets)]
+            for i in range(max(3, args.warmup)):
+                graphs[i % wl.nsets].replay()
     torch.cuda.synchronize()
 
     barrier(world)
     torch.cuda.synchronize()
     sampler = ClockSampler(torch.cuda.current_device())
     with sampler:
-        ms = time_graphs(graphs, args.steps, stream)
+        if wl.graph:
+            ms = time_graphs(graphs, args.steps, stream)
+        else:
+            with torch.cuda.stream(stream):
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+                for i in range(args.steps):
+                    wl.step(dsa, i)
+                e1.record(stream)
+                e1.synchronize()
+                ms = e0.elapsed_time(e1)
     torch.cuda.synchronize()
     barrier(world)
     ms = max_over_ranks(ms, world)
@@ -964,7 +1056,7 @@ def main():
     args.warmup = max(args.warmup, 3)
     if args.cpu_rows is None:
         args.cpu_rows = {"decode": 8, "indexer_prefill": 8, "sparse_prefill": 8, "indexer_decode": 1,
-                         "shard_merge": 512, "decode_layer": 1}[args.workload]
+                         "shard_merge": 512, "decode_layer": 1, "shard_merge_p2p": 512}[args.workload]
     DecodeWorkload.S = args.ctx
     IndexerDecodeWorkload.S = args.ctx
     DecodeLayerWorkload.S = args.ctx

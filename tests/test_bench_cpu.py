@@ -26,7 +26,8 @@ def run_ref(*args):
 
 # --workload name -> the config's workload name
 NAMES = {"decode": "sparse_mla_decode", "indexer_prefill": "indexer_prefill", "sparse_prefill": "sparse_prefill",
-         "indexer_decode": "indexer_decode", "shard_merge": "shard_merge", "decode_layer": "decode_layer"}
+         "indexer_decode": "indexer_decode", "shard_merge": "shard_merge", "decode_layer": "decode_layer",
+         "shard_merge_p2p": "shard_merge_p2p"}
 
 
 @pytest.mark.parametrize("workload,extra,unit", [
