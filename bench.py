@@ -196,6 +196,12 @@ class Workload:
     data = "synthetic (seeded)"
     traffic_profile = None
     graph = True  # steps replayed from CUDA graphs; False: launched eagerly (host-side sequencing)
+    scaling = "weak"  # "weak": per-GPU work fixed as N grows; "strong": total work fixed
+    cpu_rows_default = 8
+    cpu_steps_default = None  # None: --cpu-steps
+
+    def after_timing(self, dsa, dev):
+        """Checks that the timed work ran as claimed (raises otherwise)."""
 
     def roofline_part(self):
         """None, or (graph-capturable callable, its algorithmic amount) for the
@@ -511,6 +517,7 @@ class SparsePrefillWorkload(Workload):
 
 
 class IndexerDecodeWorkload(Workload):
+    cpu_rows_default = 1
     """The indexer half of a BASELINE config 2 decode step: per row, logits
     with the fused level-1 histogram over its 128k keys in the fp8 indexer-K
     cache, then the exact top-2048 from that histogram."""
@@ -611,6 +618,7 @@ class IndexerDecodeWorkload(Workload):
 
 
 class ShardMergeWorkload(Workload):
+    cpu_rows_default = 512
     """The exact merge of the key-sharded indexer (BASELINE config 5's
     8-way key split) on one GPU: for each of R query rows, the global top-2048
     of 8 shards' local top-2048 (value, position) lists, lowest position first
@@ -694,6 +702,7 @@ class ShardMergeWorkload(Workload):
 
 
 class DecodeLayerWorkload(Workload):
+    cpu_rows_default = 1
     """One DSA decode layer step per row: the indexer (logits with the fused
     histogram over the row's keys in the fp8 indexer-K cache, exact top-2048)
     and sparse MLA decode attention over the selected rows of the
@@ -884,10 +893,112 @@ class ShardMergeP2PWorkload(ShardMergeWorkload):
         super().cpu_setup(rows)
 
 
+class ShardedLayerWorkload(DecodeLayerWorkload):
+    """A DSA decode layer step at 180k context, batch 8, on N GPUs (one rank
+    per GPU). Every rank holds the replicated fp8 indexer-K and fp8_ds_mla
+    caches; rank r scores the contiguous key span r of every row (S / N keys,
+    logits + fused histogram), writes its local top-2048 straight into its
+    P2P exchange slot, and the exact merge over all ranks' slots (plain peer
+    loads, device-side sequence numbers) gives every rank the global top-2048;
+    sparse MLA decode then runs on the rank's 64 / N heads. At N = 1 the same
+    layer runs unsharded (logits + top-2048 + decode over all 64 heads). One
+    CUDA graph replay per step; total work is fixed as N grows (strong
+    scaling)."""
+
+    metric = "DSA decode layer tok/s @180k ctx, batch 8 (key-sharded indexer + P2P top-2048 merge + head-split sparse MLA)"
+    data = "synthetic (seeded random fp8 indexer-K and fp8_ds_mla caches, replicated on every rank; N(0,1) q)"
+    scaling = "strong"
+    B, H, HI, S, PAGE, TOPK, NSETS = 8, 64, 32, 180224, 64, 2048, 4
+    nsets = NSETS
+
+    def config(self):
+        tp = getattr(self, "tp", 1)
+        return {"workload": "dsa_decode_layer", "batch": self.B, "heads": self.H, "heads_per_gpu": self.H // tp,
+                "indexer_heads": self.HI, "ctx": self.S, "keys_per_gpu": self.span if tp > 1 else self.S,
+                "topk": self.TOPK, "page": self.PAGE, "kv_cache": "fp8_ds_mla", "k_cache": "fp8 (128 e4m3 + f32)",
+                "q_dtype": "bf16", "o_dtype": "bf16",
+                "merge": "p2p exchange (IPC slots, plain peer loads, device sequence)" if tp > 1 else "none (1 GPU)",
+                "l2": f"inputs larger than L2: {self.B * self.S * (ROW_BYTES + 132) / 1e9:.2f} GB of caches, "
+                      f"{self.NSETS} rotating q sets"}
+
+    def setup(self, dev, seed):
+        import importlib as _il
+
+        import torch.distributed as dist
+
+        self.tp = dist.get_world_size() if dist.is_initialized() else 1
+        self.rank = dist.get_rank() if dist.is_initialized() else 0
+        super().setup(dev, 1234)  # identical caches and queries on every rank
+        h0, h1 = self.rank * self.H // self.tp, (self.rank + 1) * self.H // self.tp
+        self.q = [t[:, h0:h1].contiguous() for t in self.q]
+        self.o = torch.empty(self.B, h1 - h0, 512, dtype=torch.bfloat16, device=dev)
+        self.lse = torch.empty(self.B, h1 - h0, dtype=torch.float32, device=dev)
+        self.span = self.S
+        if self.tp > 1:
+            sai = _il.import_module("glm5-on-v100_b200.sparse_attn_indexer")
+            self._sai = sai
+            cpu = dist.new_group(backend="gloo")
+            self.shard = sai.ShardConfig(tp=self.tp, rank=self.rank, cpu_group=cpu, merge="p2p", decode=True,
+                                         rows_cap=self.B)
+            self.bufs = {}
+            _, self.span, _, _ = sai.decode_span(self.bt.shape[1] * self.PAGE, self.shard, self.PAGE)
+            del self.score
+
+    def step_on(self, dsa, q, qi, w):
+        if self.tp == 1:
+            super().step_on(dsa, q, qi, w)
+            return
+        self._sai.decode_indexer_sharded(qi, self.k_cache, w, self.bt, self.seq, self.TOPK, self.idx, self.shard,
+                                         self.bufs)
+        dsa.sm70_sparse_mla_decode(self.o, self.lse, q, self.kv, self.idx, self.bt, self.seq, self.scale)
+
+    def units_per_step(self):
+        return self.B / self.tp  # every rank finishes the same B rows (its heads): B rows per step for the job
+
+    def launches_per_step(self, dsa):
+        heads = self.H // getattr(self, "tp", 1)
+        attn = dsa.ops.decode_plan(self.B, heads, self.TOPK, dsa._lib.DSA_FP8_DS_MLA)["launches"]
+        return 2 + attn if getattr(self, "tp", 1) == 1 else 3 + attn
+
+    def indexer_bytes(self):
+        return self.B * (self.span * (132 + 4) + self.HI * 128 * 2 + self.HI * 4)
+
+    def roofline_part(self):
+        """The indexer logits over this rank's key span (the O(S) scan)."""
+        if self.tp == 1:
+            def fn(dsa):
+                dsa.sm70_indexer_logits(self.score, self.qi[0], self.k_cache, self.w, self.bt, self.seq, None)
+        else:
+            off, span, lo, hi = self._sai.decode_span(self.bt.shape[1] * self.PAGE, self.shard, self.PAGE)
+            score = torch.empty(self.B, span, dtype=torch.float32, device=self.bt.device)
+            seg = self.bt[:, lo:hi]
+            sl = (self.seq - off).clamp(0, span)
+
+            def fn(dsa):
+                dsa.sm70_indexer_logits(score, self.qi[0], self.k_cache, self.w, seg, sl, None)
+        return fn, self.indexer_bytes()
+
+    def roofline_note(self, kind):
+        return (f"peak {kind} HBM copy; dominant kernel = the indexer logits over this rank's {self.span} keys per "
+                f"row, timed alone: achieved = {self.B} rows x {self.span} keys x (132 B key + 4 B score) + q/w "
+                f"/ its CUDA-event time")
+
+    def after_timing(self, dsa, dev):
+        if self.tp > 1 and dsa.ops.p2p_failed(dev):
+            raise RuntimeError("a bounded P2P exchange wait expired during the run: the measurement is invalid")
+
+    def cpu_setup(self, rows):
+        super().cpu_setup(rows)
+
+    def cpu_sample(self, steps):
+        return (f"{steps} steps x {self.cpu_rows} row: indexer logits over {self.S} keys + torch.topk(2048), then "
+                f"the reference torch decode path over the 2048 selected rows, 64 heads (oracle/ref_port.py)")
+
+
 WORKLOADS = {"decode": DecodeWorkload, "indexer_prefill": IndexerPrefillWorkload,
              "sparse_prefill": SparsePrefillWorkload, "indexer_decode": IndexerDecodeWorkload,
              "shard_merge": ShardMergeWorkload, "decode_layer": DecodeLayerWorkload,
-             "shard_merge_p2p": ShardMergeP2PWorkload}
+             "shard_merge_p2p": ShardMergeP2PWorkload, "dsa_layer": ShardedLayerWorkload}
 
 
 def capture(fn, stream):
@@ -908,22 +1019,23 @@ def time_graphs(graphs, steps, stream):
     return start.elapsed_time(stop)
 
 
-def run_ours(args, world, rank, local):
-    dsa = importlib.import_module("glm5-on-v100_b200")
-    dev = torch.device("cuda", local)
-    wl = WORKLOADS[args.workload]()
+def measure(wl, dsa, args, world, rank, dev, steps, warmup, e2e_steps, cpu):
+    """Time one workload: W eager warm-up steps, then K steps (CUDA-graph
+    replays unless the workload sequences on the host) between CUDA events on
+    the launching stream, barrier + synchronize on both sides, max over ranks;
+    the dominant kernel alone for the roofline; the end-to-end leg through the
+    public op with pinned host buffers; the CPU baseline on rank 0 at N = 1."""
     wl.setup(dev, seed=1234 + rank)
     hbm_peak, tf_burst, tf_sustained, peak_kind = load_peaks()
-
     stream = torch.cuda.Stream(dev)
     graphs = []
     with torch.cuda.stream(stream):
-        for i in range(args.warmup):
+        for i in range(warmup):
             wl.step(dsa, i)
         stream.synchronize()
         if wl.graph:
             graphs = [capture(lambda k=k: wl.step(dsa, k), stream) for k in range(wl.nsets)]
-            for i in range(max(3, args.warmup)):
+            for i in range(max(3, warmup)):
                 graphs[i % wl.nsets].replay()
     torch.cuda.synchronize()
 
@@ -932,21 +1044,22 @@ def run_ours(args, world, rank, local):
     sampler = ClockSampler(torch.cuda.current_device())
     with sampler:
         if wl.graph:
-            ms = time_graphs(graphs, args.steps, stream)
+            ms = time_graphs(graphs, steps, stream)
         else:
             with torch.cuda.stream(stream):
                 e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                 e0.record(stream)
-                for i in range(args.steps):
+                for i in range(steps):
                     wl.step(dsa, i)
                 e1.record(stream)
                 e1.synchronize()
                 ms = e0.elapsed_time(e1)
     torch.cuda.synchronize()
     barrier(world)
+    wl.after_timing(dsa, dev)
     ms = max_over_ranks(ms, world)
-    ms_per_step = ms / args.steps
-    value = wl.units_per_step() * args.steps * world / (ms / 1e3)
+    ms_per_step = ms / steps
+    value = wl.units_per_step() * steps * world / (ms / 1e3)
 
     # the dominant kernel alone, where the step holds more than it
     part = wl.roofline_part()
@@ -957,7 +1070,7 @@ def run_ours(args, world, rank, local):
             pg = [capture(lambda: fn(dsa), stream)]
             pg[0].replay()
         torch.cuda.synchronize()
-        part_steps = max(3, min(args.steps, 20))
+        part_steps = max(3, min(steps, 20))
         part_ms = max_over_ranks(time_graphs(pg, part_steps, stream), world) / part_steps
         pg.clear()
     else:
@@ -976,39 +1089,82 @@ def run_ours(args, world, rank, local):
         torch.cuda.synchronize()
         barrier(world)
         e_start, e_stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e_steps = args.steps if args.workload == "decode" else max(3, min(args.steps, 10))
         e_start.record()
-        for i in range(e_steps):
+        for i in range(e2e_steps):
             wl.e2e_step(dsa, i)
         e_stop.record()
         e_stop.synchronize()
         barrier(world)
+        wl.after_timing(dsa, dev)
         e_ms = max_over_ranks(e_start.elapsed_time(e_stop), world)
-        e2e = {"value": wl.units_per_step() * e_steps * world / (e_ms / 1e3), "unit": wl.unit,
+        e2e = {"value": wl.units_per_step() * e2e_steps * world / (e_ms / 1e3), "unit": wl.unit,
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h}
 
-    line = {
-        "metric": wl.metric, "value": value, "unit": wl.unit, "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "bf16", "data": wl.data,
-        "config": dict(wl.config(), parallelism=f"dp{world} (independent work per rank)"),
-        "e2e": e2e,
-        "gpu_launches": args.steps * wl.launches_per_step(dsa),
+    rec = {
+        "metric": wl.metric, "value": value, "unit": wl.unit, "steps": steps, "warmup": warmup,
+        "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": wl.scaling, "data": wl.data,
+        "config": wl.config(), "e2e": e2e, "gpu_launches": int(steps * wl.launches_per_step(dsa)),
         "roofline": {"bound": bound, "achieved": achieved, "peak": peak, "unit": unit, "frac": achieved / peak,
                      "traffic": profile_traffic(wl.traffic_profile), "note": wl.roofline_note(peak_kind)},
         "clocks": sampler.summary(),
     }
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_baseline(wl, args)
+    if cpu and rank == 0 and world == 1 and not args.no_cpu_baseline:
+        rec["cpu_baseline"] = cpu_baseline(wl, args, steps=wl.cpu_steps_default, rows=wl.cpu_rows_default)
+    graphs.clear()
+    return rec
+
+
+# Named sub-records of the default line (N = 1): the rest of the reference's
+# headline metric on its own configurations, each timed alone.
+SUB_RECORDS = [
+    ("sparse_mla_decode_b64_ctx128k", "decode", {"B": 64, "S": 131072}, 200),
+    ("sparse_mla_decode_b16_ctx128k", "decode", {"B": 16, "S": 131072}, 200),
+    ("sparse_mla_decode_b4_ctx128k", "decode", {"B": 4, "S": 131072}, 200),
+    ("indexer_prefill_n65536", "indexer_prefill", {}, 5),
+    ("sparse_prefill_t16384_ctx180k", "sparse_prefill", {}, 5),
+]
+
+
+def run_ours(args, world, rank, local):
+    dsa = importlib.import_module("glm5-on-v100_b200")
+    dev = torch.device("cuda", local)
+    wl = WORKLOADS[args.workload]()
+    e2e_steps = args.steps if args.workload in ("decode", "dsa_layer") else max(3, min(args.steps, 10))
+    rec = measure(wl, dsa, args, world, rank, dev, args.steps, args.warmup, e2e_steps, cpu=True)
+    par = (f"tp{world}: keys split {world} ways, heads {wl.H // world} per GPU, P2P top-k merge"
+           if getattr(wl, "scaling", "weak") == "strong" and world > 1 else
+           ("1 GPU" if world == 1 else f"dp{world} (independent work per rank)"))
+    line = {"metric": rec["metric"], "value": rec["value"], "unit": rec["unit"], "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": rec["ms_per_step"], "higher_is_better": True,
+            "scaling": rec["scaling"], "vs_baseline": None, "dtype": "bf16", "data": rec["data"],
+            "config": dict(rec["config"], parallelism=par), "e2e": rec["e2e"], "gpu_launches": rec["gpu_launches"],
+            "roofline": rec["roofline"], "clocks": rec["clocks"]}
+    if "cpu_baseline" in rec:
+        line["cpu_baseline"] = rec["cpu_baseline"]
+    del wl
+    if world == 1 and args.workload == "dsa_layer" and not args.no_sub_records:
+        subs = {}
+        for name, kind, attrs, steps in SUB_RECORDS:
+            torch.cuda.empty_cache()
+            sw = WORKLOADS[kind]()
+            for k, v in attrs.items():
+                setattr(sw, k, v)
+            sw.cpu_steps_default = 2
+            r = measure(sw, dsa, args, world, rank, dev, steps, args.warmup,
+                        steps if kind == "decode" else 3, cpu=True)
+            r["n_gpus"] = 1
+            subs[name] = r
+            del sw
+        line["sub_records"] = subs
+        line["gpu_launches"] = rec["gpu_launches"] + sum(r["gpu_launches"] for r in subs.values())
     if rank == 0:
         print(json.dumps(line), flush=True)
-    graphs.clear()
 
 
 def cpu_baseline(wl, args, steps=None, rows=None):
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    rows = rows or args.cpu_rows
+    rows = rows or args.cpu_rows or wl.cpu_rows_default
     wl.cpu_setup(rows)
     wl.cpu_step()  # warm-up
     steps = steps or args.cpu_steps
@@ -1029,7 +1185,7 @@ def run_reference(args, world, rank):
     ms_per_step = 1e3 * wl.cpu_units() / cb["value"]
     line = {
         "metric": wl.metric, "value": cb["value"], "unit": wl.unit, "n_gpus": world, "steps": steps,
-        "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+        "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": wl.scaling,
         "vs_baseline": None, "dtype": "f32 (host)", "data": "synthetic", "impl": "reference",
         "config": dict(wl.config(), parallelism="host cores"),
         "cpu_baseline": cb,
@@ -1041,29 +1197,25 @@ def run_reference(args, world, rank):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=400)
+    ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="decode")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="dsa_layer")
     ap.add_argument("--cpu-rows", type=int, default=None, help="rows per CPU-baseline step")
-    ap.add_argument("--cpu-steps", type=int, default=5)
+    ap.add_argument("--cpu-steps", type=int, default=3)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
-    ap.add_argument("--batch", type=int, default=None, help="decode / decode-indexer rows per step (default 64)")
-    ap.add_argument("--ctx", type=int, default=DecodeWorkload.S,
-                    help="decode / decode-indexer context length (smaller values make the ncu profiling case)")
+    ap.add_argument("--no-sub-records", action="store_true", help="default line without the per-config records")
+    ap.add_argument("--batch", type=int, default=None, help="decode / decode-indexer rows per step")
+    ap.add_argument("--ctx", type=int, default=None,
+                    help="decode / decode-indexer / layer context length (smaller values make the ncu profiling case)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
-    if args.cpu_rows is None:
-        args.cpu_rows = {"decode": 8, "indexer_prefill": 8, "sparse_prefill": 8, "indexer_decode": 1,
-                         "shard_merge": 512, "decode_layer": 1, "shard_merge_p2p": 512}[args.workload]
-    DecodeWorkload.S = args.ctx
-    IndexerDecodeWorkload.S = args.ctx
-    DecodeLayerWorkload.S = args.ctx
-    if args.batch is not None:
-        DecodeWorkload.B = args.batch
-        IndexerDecodeWorkload.B = args.batch
-        DecodeLayerWorkload.B = args.batch
+    for cls in (DecodeWorkload, IndexerDecodeWorkload, DecodeLayerWorkload, ShardedLayerWorkload):
+        if args.ctx is not None:
+            cls.S = args.ctx
+        if args.batch is not None:
+            cls.B = args.batch
     world, rank, local = dist_setup(args)
     try:
         if args.impl == "reference":

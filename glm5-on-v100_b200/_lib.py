@@ -60,8 +60,12 @@ SIGNATURES = {
     "dsa_ipc_free": (_i, [_p]),
     "dsa_ipc_open": (_i, [ctypes.c_char_p, ctypes.POINTER(ctypes.c_void_p)]),
     "dsa_ipc_close": (_i, [_p]),
-    "dsa_ipc_flag_set": (_i, [ctypes.c_uint64, _i, _i, _p]),
+    "dsa_ipc_flag_set": (_i, [ctypes.c_uint64, _i, _i, _p, _p]),
     "dsa_ipc_slot_wait": (_i, [_p, _i, _i, _i64, _p, _p]),
+    "dsa_indexer_shard_stage": (_i, [_p, _p, _i64, _p, _i64, _i, _i, _p, _p]),
+    "dsa_topk_rows_payload": (_i, [_p, _i64, _p, _i64, _i, _p, _p, _i, _i, _i, _p]),
+    "dsa_shard_exchange_topk": (_i, [_p, _i64, _i, _p, _p, _i, _i, _i, _p, _i64, _p, _i, _i, _p, _i64, _p, _p]),
+    "dsa_shard_exchange_merge": (_i, [_p, _i64, _p, _p, _i, _i, _i, _i, _i64, _p, _i64, _p, _p]),
 }
 
 

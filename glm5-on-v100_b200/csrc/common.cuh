@@ -158,4 +158,38 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
   return t;
 }
 
+// ------------------------------------------- cross-GPU flags (P2P exchange)
+__device__ __forceinline__ int ld_acquire_sys_s32(const int* p) {
+  int v;
+  asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void st_release_sys_s32(int* p, int v) {
+  asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ int read_err_word(const int32_t* err) {
+  return err ? *reinterpret_cast<const volatile int32_t*>(err) : 0;
+}
+
+// Bounded wait until *flag >= target. Returns false after timeout_ns of
+// device time (recording DSA_ERR_TIMEOUT in *err) or as soon as the error
+// word is set by another wait.
+__device__ __forceinline__ bool wait_flag_geq(const int* flag, int target, int64_t timeout_ns, int32_t* err) {
+  const uint64_t t0 = globaltimer_ns();
+  uint32_t spins = 0;
+  while (ld_acquire_sys_s32(flag) < target) {
+    if ((++spins & 63u) == 0) {
+      if (read_err_word(err) != 0) return false;
+      if ((int64_t)(globaltimer_ns() - t0) > timeout_ns) {
+        if (err) atomicExch(err, (int32_t)DSA_ERR_TIMEOUT);
+        return false;
+      }
+      __nanosleep(200);
+    }
+  }
+  return true;
+}
+
 }  // namespace dsa

@@ -1,19 +1,37 @@
-// Exact merge of key-sharded indexer top-k candidates, local or over peer
-// memory, and the CUDA IPC helpers of the P2P shard exchange.
+// Exact merge of key-sharded indexer top-k candidates (local buffers or peer
+// memory) and the CUDA IPC helpers of the P2P shard exchange.
 //
 // Replaces sm70_indexer_shard_merge / sm70_indexer_shard_merge_p2p and the
-// IPC helpers (csrc/attention/sm70_mla_decode.cu:2054-2434) and the torch.topk
-// epilogue they fuse (reference/sparse_attn_indexer.py:1007-1030).
+// IPC helpers (csrc/attention/sm70_mla_decode.cu:2184-2434) and the torch.topk
+// epilogue they fuse (reference/sparse_attn_indexer.py:1007-1030). The
+// selection contract is the reference's: candidate column col = s*K + c is
+// ordered by (float value, then lower column first), so the result equals
+// torch.topk over the [R, tp*K] layout; -inf picks emit -1; the K positions
+// are written ascending with the -1s first.
 //
-// One CTA (512 threads) per row. Every candidate column col = s*K + c gets the
-// distinct 64-bit key (monotone32(val) << 32) | (tp*K - 1 - col), so an
-// MSB-first byte radix walk finds the exact K-th key and ties resolve to the
-// lower column. Keys stay in registers (<= 32 per thread, tp <= 8); each pass
-// only visits candidates still matching the prefix. The selected positions
-// (-1 for -inf values) are sorted ascending with a bitonic network in shared
-// memory. The P2P variant reads each shard straight from the peer's buffer
-// with plain loads (no TMA) after a bounded acquire-wait on the
-// peer's staged flag.
+// Design (one 512-thread CTA per row, thread t owns columns c = 4t..4t+3 of
+// every shard, loaded as one 16-byte vector per shard):
+//   1. Values become 32-bit order-preserving keys. Keys at or below the -inf
+//      key all emit -1, so only the "high" keys are ranked; when there are at
+//      most K of them they are all taken.
+//   2. Otherwise a radix select over the high keys finds the K-th largest
+//      key. Its digits are 11 bits wide and start at the highest bit in which
+//      the block's min and max high keys differ, so real score distributions
+//      spread over the first pass's 2048 bins instead of piling into a few;
+//      each further pass only sees the keys of the chosen bin, and the walk
+//      stops as soon as a whole bin is taken.
+//   3. Keys equal to the K-th key are ranked in column order with one
+//      block-wide scan of per-shard counts packed 16 bits per shard, so the
+//      lower-column rule costs O(candidates), whatever the number of ties.
+//   4. The selected positions are compacted per shard, in column order, into
+//      shared memory. When every shard's run is ascending (always so for lists
+//      the top-k kernels write), the output rank of a position is its index in
+//      its run plus, per other run, a count found from the run's first/last
+//      entries (disjoint key shards) or a binary search. Runs that are not
+//      ascending are ranked by counting over all selected positions.
+// The P2P variant checks the error word once, waits (bounded) on every peer's
+// staged flag with acquire loads, and then reads the peers' slots with
+// relaxed system-scope loads (plain peer loads; no TMA, no multicast).
 #include <climits>
 
 #include "common.cuh"
@@ -21,209 +39,459 @@
 namespace dsa {
 namespace {
 
-constexpr int MNT = 512;
-constexpr int MAX_PER = 32;  // tp * K / MNT <= 32  (tp <= 8, K <= 2048)
+constexpr int MT = 512;               // threads per row
+constexpr int NW = MT / 32;
+constexpr int PER = 4;                // columns per thread per shard
 constexpr int MAX_TP = 8;
-constexpr int MAX_K = 2048;
+constexpr int MAX_K = MT * PER;       // 2048
+constexpr int DIGIT = 11;
+constexpr int NBIN = 1 << DIGIT;      // 2048
+constexpr uint32_t NEG_KEY = 0x007FFFFFu;  // monotone32(-inf); keys <= it emit -1
 
-struct ShardSrc {
-  const uint8_t* base[MAX_TP];  // shard s slab: [R, 2K] f32 at base[s] (+ slot_off)
-  const int* staged[MAX_TP];    // P2P only: &flags[s][0]
-};
-
-struct MergeParams {
-  ShardSrc src;
+struct MergeArgs {
+  const uint8_t* base[MAX_TP];  // shard s, row 0 of the slab, before slot_off
+  const int* staged[MAX_TP];    // P2P: &flags_s[0]
   int32_t* out;
   const int32_t* dst_rows;
-  int32_t* err;
+  int32_t* err;                 // P2P: error word (DSA_ERR_TIMEOUT on an expired wait)
+  int* ctl;                     // exchange mode: [0] last completed seq, [2] CTA done counter
+  int* my_flags;                // exchange mode: this rank's {staged, merged}
   int64_t out_stride;
-  int64_t shard_stride;  // bytes between shards for the local [tp, R, 2K] layout (0 for P2P)
+  int64_t shard_stride;         // bytes between shards (local [tp, R, 2K] layout)
+  int64_t slot_off;             // bytes added to every base (P2P slot)
+  int64_t slot_bytes;           // exchange mode: slot (seq & 1) starts at base + (seq & 1) * slot_bytes
   int64_t timeout_ns;
   int R, tp, K, dst_base, seq;
-  int p2p;
+  int p2p, vec;
 };
 
-__device__ __forceinline__ int ld_acquire_sys(const int* p) {
-  int v;
-  asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+struct MergeSmem {
+  uint32_t hist[NBIN];
+  int32_t pos[MAX_K];
+  uint32_t red[3][NW];
+  unsigned long long scan[2][NW];
+  int seg[MAX_TP + 1];          // run s of pos[] is [seg[s], seg[s+1])
+  uint32_t bin, above, cnt;
+  int ok;
+};
+
+__device__ __forceinline__ float4 ld_sys_f4(const float* p) {
+  float4 v;
+  asm volatile("ld.relaxed.sys.global.v4.f32 {%0,%1,%2,%3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "l"(p)
+               : "memory");
   return v;
 }
 
-__device__ __forceinline__ void st_release_sys(int* p, int v) {
-  asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+__device__ __forceinline__ float ld_sys_f32(const float* p) {
+  float v;
+  asm volatile("ld.relaxed.sys.global.f32 %0, [%1];" : "=f"(v) : "l"(p) : "memory");
+  return v;
 }
 
-// Bounded wait: returns false (and records DSA_ERR_TIMEOUT in *err) when
-// flag < target after timeout_ns of device time, or when another wait of the
-// same launch already gave up.
-__device__ bool wait_flag_geq(const int* flag, int target, int64_t timeout_ns, int32_t* err) {
-  const uint64_t t0 = globaltimer_ns();
-  uint32_t spins = 0;
-  while (ld_acquire_sys(flag) < target) {
-    if ((++spins & 63u) == 0) {
-      if (err && *reinterpret_cast<volatile int32_t*>(err) != 0) return false;
-      if ((int64_t)(globaltimer_ns() - t0) > timeout_ns) {
-        if (err) atomicExch(err, (int32_t)DSA_ERR_TIMEOUT);
-        return false;
-      }
-      __nanosleep(200);
-    }
-  }
-  return true;
+// 16-bit field s of a pair of packed per-shard counters.
+__device__ __forceinline__ uint32_t field(unsigned long long lo, unsigned long long hi, int s) {
+  return (uint32_t)(((s < 4 ? lo : hi) >> (16 * (s & 3))) & 0xFFFFull);
 }
 
-__global__ void __launch_bounds__(MNT) shard_merge_kernel(const MergeParams p) {
-  __shared__ uint32_t s_hist[256];
-  __shared__ int32_t s_sel[MAX_K];
-  __shared__ uint32_t s_cnt;
-  __shared__ unsigned long long s_prefix;
-  __shared__ uint32_t s_target;
-  __shared__ uint32_t s_eq;  // keys matching the new prefix
-  __shared__ int s_ok;
+// Block-wide exclusive scan of two packed 64-bit counters in thread order;
+// the block totals are returned through tot_lo / tot_hi.
+__device__ __forceinline__ void scan_packed(unsigned long long& lo, unsigned long long& hi,
+                                            unsigned long long& tot_lo, unsigned long long& tot_hi,
+                                            MergeSmem& s) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  unsigned long long il = lo, ih = hi;
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+    const unsigned long long ul = __shfl_up_sync(0xffffffffu, il, d);
+    const unsigned long long uh = __shfl_up_sync(0xffffffffu, ih, d);
+    if (lane >= d) {
+      il += ul;
+      ih += uh;
+    }
+  }
+  if (lane == 31) {
+    s.scan[0][warp] = il;
+    s.scan[1][warp] = ih;
+  }
+  __syncthreads();
+  unsigned long long pl = 0, ph = 0, tl = 0, th = 0;
+#pragma unroll
+  for (int w = 0; w < NW; ++w) {
+    const unsigned long long a = s.scan[0][w], b = s.scan[1][w];
+    if (w < warp) {
+      pl += a;
+      ph += b;
+    }
+    tl += a;
+    th += b;
+  }
+  __syncthreads();
+  lo = pl + il - lo;
+  hi = ph + ih - hi;
+  tot_lo = tl;
+  tot_hi = th;
+}
 
-  const int r = blockIdx.x;
-  const int tid = threadIdx.x;
-  const int K = p.K;
-  const int ncand = p.tp * K;
-  const int nper = (ncand + MNT - 1) / MNT;
-
-  if (p.p2p) {
-    if (tid == 0) s_ok = 1;
-    __syncthreads();
-    if (tid < p.tp) {
-      if (!wait_flag_geq(p.src.staged[tid], p.seq, p.timeout_ns, p.err)) s_ok = 0;
-    }
-    __syncthreads();
-    if (!s_ok) return;  // output undefined; the host reads *err
-    __threadfence_system();
-  }
-
-  auto slab = [&](int s) -> const float* {
-    return reinterpret_cast<const float*>(p.src.base[s] + (p.p2p ? 0 : (int64_t)s * p.shard_stride)) +
-           (int64_t)r * 2 * K;
-  };
-
-  // all of this thread's candidate values are loaded before any is used, so
-  // the loads are in flight together
-  float val[MAX_PER];
+// The bin of the K-th largest key: with bins counted in s.hist[0..nbins),
+// the largest bin b with count(bins >= b) >= need. Thread t owns bins
+// [4t, 4t + 4). Leaves b, count(bins > b) and count(b) in s.bin/above/cnt.
+__device__ __forceinline__ void pick_bin(int nbins, uint32_t need, MergeSmem& s) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  uint32_t h[4], c = 0;
 #pragma unroll
-  for (int i = 0; i < MAX_PER; ++i) {
-    const int col = tid + i * MNT;
-    val[i] = 0.f;
-    if (i < nper && col < ncand) {
-      const int s = col / K, c = col - s * K;
-      val[i] = __ldg(slab(s) + c);
-    }
+  for (int j = 0; j < 4; ++j) {
+    const int b = 4 * tid + j;
+    h[j] = b < nbins ? s.hist[b] : 0u;
+    c += h[j];
   }
-  unsigned long long key[MAX_PER];
-  uint32_t act = 0;
+  uint32_t suf = c;  // inclusive suffix over the lanes of this warp
 #pragma unroll
-  for (int i = 0; i < MAX_PER; ++i) {
-    key[i] = 0ull;
-    const int col = tid + i * MNT;
-    if (i < nper && col < ncand) {
-      key[i] = ((unsigned long long)monotone32(val[i]) << 32) | (uint32_t)(ncand - 1 - col);
-      act |= 1u << i;
-    }
+  for (int d = 1; d < 32; d <<= 1) {
+    const uint32_t v = __shfl_down_sync(0xffffffffu, suf, d);
+    if (lane + d < 32) suf += v;
   }
-  if (tid == 0) {
-    s_prefix = 0ull;
-    s_target = (uint32_t)K;
-    s_cnt = 0;
-  }
-  const uint32_t valid_mask = act;
-  for (int byte = 7; byte >= 0; --byte) {
-    for (int i = tid; i < 256; i += MNT) s_hist[i] = 0;
-    __syncthreads();
-    const int sh = 8 * byte;
-    const unsigned long long hi_mask = byte == 7 ? 0ull : (~0ull << (sh + 8));
-    const unsigned long long pfx = s_prefix;
+  if (lane == 0) s.red[0][warp] = suf;
+  __syncthreads();
+  uint32_t later = 0;
 #pragma unroll
-    for (int i = 0; i < MAX_PER; ++i) {
-      if (!(act & (1u << i))) continue;
-      if ((key[i] & hi_mask) != (pfx & hi_mask)) {
-        act &= ~(1u << i);
-        continue;
+  for (int w = 0; w < NW; ++w)
+    if (w > warp) later += s.red[0][w];
+  suf += later;
+  uint32_t above = suf - c;
+  if (above < need && suf >= need) {
+#pragma unroll
+    for (int j = 3; j >= 0; --j) {
+      if (above + h[j] >= need) {
+        s.bin = 4 * tid + j;
+        s.above = above;
+        s.cnt = h[j];
+        break;
       }
-      atomicAdd(&s_hist[(key[i] >> sh) & 0xFFu], 1u);
-    }
-    __syncthreads();
-    if (tid < 32) {  // warp 0: lane owns bins [8*lane, 8*lane+8)
-      const uint32_t tgt = s_target;
-      __syncwarp();
-      uint32_t cs = 0;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) cs += s_hist[8 * tid + j];
-      uint32_t suf = cs;
-#pragma unroll
-      for (int off = 1; off < 32; off <<= 1) {
-        const uint32_t v = __shfl_down_sync(0xffffffffu, suf, off);
-        if (tid + off < 32) suf += v;
-      }
-      const uint32_t above = suf - cs;
-      if (above < tgt && suf >= tgt) {
-        uint32_t run = above;
-        for (int j = 7; j >= 0; --j) {
-          const uint32_t c = s_hist[8 * tid + j];
-          if (run + c >= tgt) {
-            s_prefix = pfx | ((unsigned long long)(8 * tid + j) << sh);
-            s_target = tgt - run;
-            s_eq = c;
-            break;
-          }
-          run += c;
-        }
-      }
-    }
-    __syncthreads();
-    // after the value bytes: when every key with the K-th value is needed the
-    // column bytes (which only order equal values) cannot change the cut
-    if (byte == 4 && s_target == s_eq) break;
-  }
-  const unsigned long long T = s_prefix;
-#pragma unroll
-  for (int i = 0; i < MAX_PER; ++i) {
-    if (!(valid_mask & (1u << i))) continue;
-    if (key[i] >= T) {
-      const uint32_t slot = atomicAdd(&s_cnt, 1u);
-      int32_t pos = -1;
-      if ((uint32_t)(key[i] >> 32) > 0x007FFFFFu) {  // not -inf
-        const int col = tid + i * MNT;
-        const int s = col / K, c = col - s * K;
-        pos = __float_as_int(slab(s)[K + c]);
-      }
-      if (slot < (uint32_t)K) s_sel[slot] = pos;
+      above += h[j];
     }
   }
   __syncthreads();
-  // ascending bitonic sort over the next power of two (padding sorts last)
-  int np2 = 1;
-  while (np2 < K) np2 <<= 1;
-  for (int i = K + tid; i < np2; i += MNT) s_sel[i] = INT_MAX;
-  __syncthreads();
-  for (int k2 = 2; k2 <= np2; k2 <<= 1) {
-    for (int j = k2 >> 1; j > 0; j >>= 1) {
-      for (int i = tid; i < np2; i += MNT) {
-        const int ixj = i ^ j;
-        if (ixj > i) {
-          const int32_t a = s_sel[i], c = s_sel[ixj];
-          const bool up = (i & k2) == 0;
-          if ((a > c) == up) {
-            s_sel[i] = c;
-            s_sel[ixj] = a;
-          }
+}
+
+// Number of entries of the ascending run a[0..n) that are < x (strict) or
+// <= x (!strict).
+__device__ __forceinline__ int count_run(const int32_t* a, int n, int32_t x, bool strict) {
+  int lo = 0, hi = n;
+  while (lo < hi) {
+    const int mid = (lo + hi) >> 1;
+    const bool left = strict ? a[mid] < x : a[mid] <= x;
+    if (left)
+      lo = mid + 1;
+    else
+      hi = mid;
+  }
+  return lo;
+}
+
+__device__ void merge_row(const MergeArgs& a, int r, int64_t soff, MergeSmem& s) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int K = a.K, tp = a.tp;
+  const int c0 = tid * PER;
+  const int64_t row_off = (int64_t)r * 2 * K;  // floats
+
+  // ---- 1. keys of this thread's columns
+  uint32_t key[MAX_TP][PER];
+  uint32_t vmask = 0;  // bit 4*s + e: column exists
+#pragma unroll
+  for (int sh = 0; sh < MAX_TP; ++sh) {
+#pragma unroll
+    for (int e = 0; e < PER; ++e) key[sh][e] = 0;
+    if (sh < tp && c0 < K) {
+      const float* v = reinterpret_cast<const float*>(a.base[sh] + soff + (int64_t)sh * a.shard_stride) + row_off + c0;
+      float f[PER];
+      if (a.vec) {
+        const float4 q = a.p2p ? ld_sys_f4(v) : __ldg(reinterpret_cast<const float4*>(v));
+        f[0] = q.x;
+        f[1] = q.y;
+        f[2] = q.z;
+        f[3] = q.w;
+      } else {
+#pragma unroll
+        for (int e = 0; e < PER; ++e) f[e] = c0 + e < K ? (a.p2p ? ld_sys_f32(v + e) : __ldg(v + e)) : 0.f;
+      }
+#pragma unroll
+      for (int e = 0; e < PER; ++e) {
+        if (c0 + e < K) {
+          key[sh][e] = monotone32(f[e]);
+          vmask |= 1u << (PER * sh + e);
         }
       }
+    }
+  }
+
+  // ---- 2. high keys: count, min, max
+  uint32_t nh = 0, kmin = 0xFFFFFFFFu, kmax = 0;
+#pragma unroll
+  for (int sh = 0; sh < MAX_TP; ++sh)
+#pragma unroll
+    for (int e = 0; e < PER; ++e)
+      if ((vmask >> (PER * sh + e)) & 1u) {
+        const uint32_t k = key[sh][e];
+        if (k > NEG_KEY) {
+          ++nh;
+          kmin = min(kmin, k);
+          kmax = max(kmax, k);
+        }
+      }
+  nh = __reduce_add_sync(0xffffffffu, nh);
+  kmin = __reduce_min_sync(0xffffffffu, kmin);
+  kmax = __reduce_max_sync(0xffffffffu, kmax);
+  if (lane == 0) {
+    s.red[0][warp] = nh;
+    s.red[1][warp] = kmin;
+    s.red[2][warp] = kmax;
+  }
+  __syncthreads();
+  nh = 0;
+  kmin = 0xFFFFFFFFu;
+  kmax = 0;
+#pragma unroll
+  for (int w = 0; w < NW; ++w) {
+    nh += s.red[0][w];
+    kmin = min(kmin, s.red[1][w]);
+    kmax = max(kmax, s.red[2][w]);
+  }
+  __syncthreads();
+
+  // ---- 3. the selection rule: key >= thr, or (tie) key > thr plus the
+  // first need_eq keys == thr in column order
+  uint32_t thr = NEG_KEY + 1;
+  uint32_t need_eq = 0;
+  bool tie = false;
+  int n_neg = 0;
+  if (nh <= (uint32_t)K) {
+    n_neg = K - (int)nh;
+  } else {
+    uint32_t base = kmin, need = (uint32_t)K;
+    const uint32_t span = kmax - kmin;
+    int bits = span ? 32 - __clz(span) : 0;
+    bool first = true;
+    while (true) {
+      if (bits == 0) {  // every remaining key equals base
+        thr = base;
+        need_eq = need;
+        tie = true;
+        break;
+      }
+      const int shift = max(bits - DIGIT, 0);
+      const int nbins = 1 << (bits - shift);
+      for (int i = tid; i < nbins; i += MT) s.hist[i] = 0;
       __syncthreads();
+#pragma unroll
+      for (int sh = 0; sh < MAX_TP; ++sh)
+#pragma unroll
+        for (int e = 0; e < PER; ++e) {
+          const uint32_t k = key[sh][e];
+          if (!((vmask >> (PER * sh + e)) & 1u) || k <= NEG_KEY || k < base) continue;
+          const uint32_t d = k - base;
+          if (!first && (d >> bits) != 0) continue;
+          atomicAdd(&s.hist[d >> shift], 1u);
+        }
+      __syncthreads();
+      pick_bin(nbins, need, s);
+      const uint32_t b = s.bin, above = s.above, cnt = s.cnt;
+      __syncthreads();
+      need -= above;
+      base += b << shift;
+      bits = shift;
+      first = false;
+      if (cnt == need) {  // the whole bin is taken: every key >= base
+        thr = base;
+        break;
+      }
     }
   }
-  const int64_t dst = p.dst_base >= 0 ? (int64_t)p.dst_base + r : (int64_t)p.dst_rows[r];
-  for (int i = tid; i < K; i += MNT) p.out[dst * p.out_stride + i] = s_sel[i];
+
+  // ---- 4. which columns are selected (ties ranked in column order)
+  uint32_t selm = 0;  // bit 4*s + e
+  if (tie) {
+    unsigned long long lo = 0, hi = 0;
+#pragma unroll
+    for (int sh = 0; sh < MAX_TP; ++sh) {
+      uint32_t c = 0;
+#pragma unroll
+      for (int e = 0; e < PER; ++e) c += ((vmask >> (PER * sh + e)) & 1u) && key[sh][e] == thr;
+      if (sh < 4)
+        lo += (unsigned long long)c << (16 * sh);
+      else
+        hi += (unsigned long long)c << (16 * (sh - 4));
+    }
+    unsigned long long tl, th;
+    scan_packed(lo, hi, tl, th, s);
+    uint32_t before = 0;  // ties of the shards before this one
+#pragma unroll
+    for (int sh = 0; sh < MAX_TP; ++sh) {
+      uint32_t rank = before + field(lo, hi, sh);
+#pragma unroll
+      for (int e = 0; e < PER; ++e) {
+        if (!((vmask >> (PER * sh + e)) & 1u)) continue;
+        const uint32_t k = key[sh][e];
+        if (k > thr) {
+          selm |= 1u << (PER * sh + e);
+        } else if (k == thr) {
+          if (rank < need_eq) selm |= 1u << (PER * sh + e);
+          ++rank;
+        }
+      }
+      before += field(tl, th, sh);
+    }
+  } else {
+#pragma unroll
+    for (int sh = 0; sh < MAX_TP; ++sh)
+#pragma unroll
+      for (int e = 0; e < PER; ++e)
+        if (((vmask >> (PER * sh + e)) & 1u) && key[sh][e] >= thr && key[sh][e] > NEG_KEY)
+          selm |= 1u << (PER * sh + e);
+  }
+
+  // ---- 5. compact the selected positions per shard, in column order
+  {
+    unsigned long long lo = 0, hi = 0;
+#pragma unroll
+    for (int sh = 0; sh < MAX_TP; ++sh) {
+      const uint32_t c = __popc((selm >> (PER * sh)) & 0xFu);
+      if (sh < 4)
+        lo += (unsigned long long)c << (16 * sh);
+      else
+        hi += (unsigned long long)c << (16 * (sh - 4));
+    }
+    unsigned long long tl, th;
+    scan_packed(lo, hi, tl, th, s);
+    if (tid == 0) {
+      int acc = 0;
+      for (int sh = 0; sh < MAX_TP; ++sh) {
+        s.seg[sh] = acc;
+        acc += sh < tp ? (int)field(tl, th, sh) : 0;
+      }
+      s.seg[MAX_TP] = acc;
+    }
+    uint32_t run0 = 0;
+#pragma unroll
+    for (int sh = 0; sh < MAX_TP; ++sh) {
+      const uint32_t m = (selm >> (PER * sh)) & 0xFu;
+      if (m) {
+        const float* pv =
+            reinterpret_cast<const float*>(a.base[sh] + soff + (int64_t)sh * a.shard_stride) + row_off + K + c0;
+        int32_t pp[PER];
+        if (a.vec) {
+          const float4 q = a.p2p ? ld_sys_f4(pv) : __ldg(reinterpret_cast<const float4*>(pv));
+          pp[0] = __float_as_int(q.x);
+          pp[1] = __float_as_int(q.y);
+          pp[2] = __float_as_int(q.z);
+          pp[3] = __float_as_int(q.w);
+        } else {
+#pragma unroll
+          for (int e = 0; e < PER; ++e)
+            pp[e] = ((m >> e) & 1u) ? __float_as_int(a.p2p ? ld_sys_f32(pv + e) : __ldg(pv + e)) : 0;
+        }
+        uint32_t slot = run0 + field(lo, hi, sh);
+#pragma unroll
+        for (int e = 0; e < PER; ++e)
+          if ((m >> e) & 1u) {
+            if (slot < (uint32_t)MAX_K) s.pos[slot] = pp[e];
+            ++slot;
+          }
+      }
+      run0 += field(tl, th, sh);
+    }
+  }
+  __syncthreads();
+
+  // ---- 6. ascending output: -1s first, then the merged runs
+  const int n_sel = min(s.seg[MAX_TP], K - n_neg);  // == K - n_neg by construction
+  int32_t* out = a.out + (a.dst_base >= 0 ? (int64_t)a.dst_base + r : (int64_t)a.dst_rows[r]) * a.out_stride;
+  for (int i = tid; i < n_neg; i += MT) out[i] = -1;
+  bool unsorted = false;
+  for (int i = tid; i + 1 < n_sel; i += MT) {
+    int sh = 0;
+    while (s.seg[sh + 1] <= i) ++sh;
+    if (i + 1 < s.seg[sh + 1] && s.pos[i] > s.pos[i + 1]) unsorted = true;
+  }
+  if (!__syncthreads_or(unsorted)) {
+    for (int i = tid; i < n_sel; i += MT) {
+      const int32_t p = s.pos[i];
+      int own = 0;
+      while (s.seg[own + 1] <= i) ++own;
+      int rank = i - s.seg[own];
+      for (int sh = 0; sh < tp; ++sh) {
+        const int lo = s.seg[sh], n = s.seg[sh + 1] - lo;
+        if (sh == own || n == 0) continue;
+        const bool strict = sh > own;  // equal positions: the lower shard goes first
+        const int32_t f = s.pos[lo], l = s.pos[lo + n - 1];
+        if (strict ? l < p : l <= p)
+          rank += n;
+        else if (strict ? f < p : f <= p)
+          rank += count_run(s.pos + lo, n, p, strict);
+      }
+      out[n_neg + rank] = p;
+    }
+  } else {
+    // runs in arbitrary order: rank = #smaller + #equal at a lower slot
+    int32_t mine[PER];
+    int rk[PER];
+#pragma unroll
+    for (int k = 0; k < PER; ++k) {
+      const int i = tid + k * MT;
+      mine[k] = i < n_sel ? s.pos[i] : 0;
+      rk[k] = 0;
+    }
+    for (int j = 0; j < n_sel; ++j) {
+      const int32_t v = s.pos[j];
+#pragma unroll
+      for (int k = 0; k < PER; ++k) rk[k] += v < mine[k] || (v == mine[k] && j < tid + k * MT);
+    }
+#pragma unroll
+    for (int k = 0; k < PER; ++k)
+      if (tid + k * MT < n_sel) out[n_neg + rk[k]] = mine[k];
+  }
 }
 
-__global__ void ipc_flag_set_kernel(int* flag, int seq) {
+// Exchange mode: the last CTA to finish publishes merged = seq and advances
+// the rank's sequence counter (every CTA arrives, even after an error).
+__device__ void finish_exchange(const MergeArgs& a, int seq) {
+  __syncthreads();
+  if (threadIdx.x != 0) return;
   __threadfence_system();
-  st_release_sys(flag, seq);
+  if (atomicAdd(a.ctl + 2, 1) == (int)gridDim.x - 1) {
+    a.ctl[2] = 0;
+    __threadfence_system();
+    if (read_err_word(a.err) == 0) st_release_sys_s32(a.my_flags + 1, seq);
+    a.ctl[0] = seq;
+  }
+}
+
+__global__ void __launch_bounds__(MT, 2) shard_merge_kernel(const MergeArgs a) {
+  __shared__ MergeSmem s;
+  const int r = blockIdx.x;
+  int seq = a.seq;
+  int64_t soff = a.slot_off;
+  if (a.ctl) {
+    seq = *reinterpret_cast<const volatile int*>(a.ctl) + 1;
+    soff = (int64_t)(seq & 1) * a.slot_bytes;
+  }
+  bool ok = true;
+  if (a.p2p) {
+    if (threadIdx.x == 0) s.ok = read_err_word(a.err) == 0;
+    __syncthreads();
+    if (s.ok && (int)threadIdx.x < a.tp && !wait_flag_geq(a.staged[threadIdx.x], seq, a.timeout_ns, a.err)) s.ok = 0;
+    __syncthreads();
+    ok = s.ok != 0;
+  }
+  if (ok && r < a.R) merge_row(a, r, soff, s);
+  if (a.ctl) finish_exchange(a, seq);
+}
+
+__global__ void ipc_flag_set_kernel(int* flag, int seq, const int32_t* err) {
+  if (read_err_word(err) != 0) return;  // a failed wait before this point: publish nothing
+  __threadfence_system();
+  st_release_sys_s32(flag, seq);
 }
 
 struct FlagPtrs {
@@ -236,6 +504,20 @@ __global__ void ipc_slot_wait_kernel(FlagPtrs f, int tp, int min_seq, int64_t ti
   __threadfence_system();
 }
 
+// Stages [R, K] values and [R, K] positions as the [R, 2K] f32 payload;
+// returns at once when the error word is set (a slot wait before it failed,
+// so a peer may still be reading the slot).
+__global__ void shard_stage_kernel(float* slot, const float* vals, int64_t vals_stride, const int32_t* idx,
+                                   int64_t idx_stride, int K, const int32_t* err) {
+  if (read_err_word(err) != 0) return;
+  const int r = blockIdx.x;
+  float* dst = slot + (int64_t)r * 2 * K;
+  for (int c = threadIdx.x; c < K; c += blockDim.x) {
+    dst[c] = vals[(int64_t)r * vals_stride + c];
+    dst[K + c] = __int_as_float(idx[(int64_t)r * idx_stride + c]);
+  }
+}
+
 int check_merge_args(int tp, int R, int K, int dst_base, const int32_t* dst_rows, const int32_t* out) {
   DSA_REQUIRE(tp >= 1 && tp <= MAX_TP, DSA_ERR_UNSUPPORTED, "shard_merge: tp must be in [1, %d] (got %d)",
               MAX_TP, tp);
@@ -245,6 +527,8 @@ int check_merge_args(int tp, int R, int K, int dst_base, const int32_t* dst_rows
   DSA_REQUIRE(out != nullptr, DSA_ERR_INVALID, "shard_merge: null out");
   return DSA_OK;
 }
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
 }  // namespace
 }  // namespace dsa
@@ -259,17 +543,18 @@ extern "C" int dsa_indexer_shard_merge(int32_t* out, int64_t out_stride, const f
   if (st != DSA_OK) return st;
   if (R == 0) return DSA_OK;
   DSA_REQUIRE(allf != nullptr && out_stride >= K, DSA_ERR_INVALID, "shard_merge: null allf or short out rows");
-  MergeParams p{};
-  for (int s = 0; s < MAX_TP; ++s) p.src.base[s] = reinterpret_cast<const uint8_t*>(allf);
-  p.shard_stride = (int64_t)R * 2 * K * sizeof(float);
-  p.out = out;
-  p.dst_rows = dst_rows;
-  p.out_stride = out_stride;
-  p.R = R;
-  p.tp = tp;
-  p.K = K;
-  p.dst_base = dst_base;
-  shard_merge_kernel<<<R, MNT, 0, as_stream(stream)>>>(p);
+  MergeArgs a{};
+  for (int s = 0; s < MAX_TP; ++s) a.base[s] = reinterpret_cast<const uint8_t*>(allf);
+  a.shard_stride = (int64_t)R * 2 * K * sizeof(float);
+  a.out = out;
+  a.dst_rows = dst_rows;
+  a.out_stride = out_stride;
+  a.R = R;
+  a.tp = tp;
+  a.K = K;
+  a.dst_base = dst_base;
+  a.vec = (K % 4 == 0) && aligned16(allf);
+  shard_merge_kernel<<<R, MT, 0, as_stream(stream)>>>(a);
   return check_launch("shard_merge_kernel");
 }
 
@@ -283,25 +568,74 @@ extern "C" int dsa_indexer_shard_merge_p2p(int32_t* out, int64_t out_stride, con
   if (R == 0) return DSA_OK;
   DSA_REQUIRE(data_ptrs && flag_ptrs && out_stride >= K && timeout_ns > 0, DSA_ERR_INVALID,
               "shard_merge_p2p: null pointer arrays, short out rows or non-positive timeout");
-  MergeParams p{};
+  MergeArgs a{};
+  a.vec = K % 4 == 0 && slot_off % 16 == 0;
   for (int s = 0; s < tp; ++s) {
     DSA_REQUIRE(data_ptrs[s] != 0 && flag_ptrs[s] != 0, DSA_ERR_INVALID, "shard_merge_p2p: null peer pointer %d", s);
-    p.src.base[s] = reinterpret_cast<const uint8_t*>(data_ptrs[s]) + slot_off;
-    p.src.staged[s] = reinterpret_cast<const int*>(flag_ptrs[s]);
+    a.base[s] = reinterpret_cast<const uint8_t*>(data_ptrs[s]);
+    a.staged[s] = reinterpret_cast<const int*>(flag_ptrs[s]);
+    a.vec = a.vec && aligned16(a.base[s]);
   }
-  p.out = out;
-  p.dst_rows = dst_rows;
-  p.err = err_flag;
-  p.out_stride = out_stride;
-  p.timeout_ns = timeout_ns;
-  p.R = R;
-  p.tp = tp;
-  p.K = K;
-  p.dst_base = dst_base;
-  p.seq = seq;
-  p.p2p = 1;
-  shard_merge_kernel<<<R, MNT, 0, as_stream(stream)>>>(p);
+  a.slot_off = slot_off;
+  a.out = out;
+  a.dst_rows = dst_rows;
+  a.err = err_flag;
+  a.out_stride = out_stride;
+  a.timeout_ns = timeout_ns;
+  a.R = R;
+  a.tp = tp;
+  a.K = K;
+  a.dst_base = dst_base;
+  a.seq = seq;
+  a.p2p = 1;
+  shard_merge_kernel<<<R, MT, 0, as_stream(stream)>>>(a);
   return check_launch("shard_merge_kernel(p2p)");
+}
+
+extern "C" int dsa_shard_exchange_merge(int32_t* out, int64_t out_stride, const uint64_t* data_ptrs,
+                                        const uint64_t* flag_ptrs, int tp, int rank, int R, int K,
+                                        int64_t slot_bytes, int32_t* ctl, int64_t timeout_ns, int32_t* err_flag,
+                                        void* stream) {
+  clear_error();
+  int st = check_merge_args(tp, R, K, 0, nullptr, out);
+  if (st != DSA_OK) return st;
+  DSA_REQUIRE(data_ptrs && flag_ptrs && ctl && err_flag && out_stride >= K && timeout_ns > 0 && rank >= 0 &&
+                  rank < tp && slot_bytes >= (int64_t)R * 2 * K * 4 && slot_bytes % 16 == 0,
+              DSA_ERR_INVALID, "shard_exchange_merge: bad arguments");
+  MergeArgs a{};
+  a.vec = K % 4 == 0;
+  for (int s = 0; s < tp; ++s) {
+    DSA_REQUIRE(data_ptrs[s] != 0 && flag_ptrs[s] != 0, DSA_ERR_INVALID,
+                "shard_exchange_merge: null peer pointer %d", s);
+    a.base[s] = reinterpret_cast<const uint8_t*>(data_ptrs[s]);
+    a.staged[s] = reinterpret_cast<const int*>(flag_ptrs[s]);
+    a.vec = a.vec && aligned16(a.base[s]);
+  }
+  a.my_flags = reinterpret_cast<int*>(flag_ptrs[rank]);
+  a.ctl = ctl;
+  a.slot_bytes = slot_bytes;
+  a.out = out;
+  a.err = err_flag;
+  a.out_stride = out_stride;
+  a.timeout_ns = timeout_ns;
+  a.R = R;
+  a.tp = tp;
+  a.K = K;
+  a.p2p = 1;
+  // at least one CTA, so the merged flag is published even for R == 0
+  shard_merge_kernel<<<R > 0 ? R : 1, MT, 0, as_stream(stream)>>>(a);
+  return check_launch("shard_merge_kernel(exchange)");
+}
+
+extern "C" int dsa_indexer_shard_stage(float* slot, const float* vals, int64_t vals_stride, const int32_t* idx,
+                                       int64_t idx_stride, int R, int K, const int32_t* err_flag, void* stream) {
+  clear_error();
+  DSA_REQUIRE(R >= 0 && K >= 1 && vals_stride >= K && idx_stride >= K, DSA_ERR_INVALID,
+              "shard_stage: bad sizes");
+  if (R == 0) return DSA_OK;
+  DSA_REQUIRE(slot && vals && idx, DSA_ERR_INVALID, "shard_stage: null pointer");
+  shard_stage_kernel<<<R, 256, 0, as_stream(stream)>>>(slot, vals, vals_stride, idx, idx_stride, K, err_flag);
+  return check_launch("shard_stage_kernel");
 }
 
 extern "C" int dsa_ipc_alloc(int64_t bytes, void** dev_ptr, uint8_t* handle_out) {
@@ -348,10 +682,10 @@ extern "C" int dsa_ipc_close(void* dev_ptr) {
   return DSA_OK;
 }
 
-extern "C" int dsa_ipc_flag_set(uint64_t flag_ptr, int which, int seq, void* stream) {
+extern "C" int dsa_ipc_flag_set(uint64_t flag_ptr, int which, int seq, const int32_t* err_flag, void* stream) {
   clear_error();
   DSA_REQUIRE(flag_ptr != 0 && (which == 0 || which == 1), DSA_ERR_INVALID, "ipc_flag_set: bad arguments");
-  ipc_flag_set_kernel<<<1, 1, 0, as_stream(stream)>>>(reinterpret_cast<int*>(flag_ptr) + which, seq);
+  ipc_flag_set_kernel<<<1, 1, 0, as_stream(stream)>>>(reinterpret_cast<int*>(flag_ptr) + which, seq, err_flag);
   return check_launch("ipc_flag_set_kernel");
 }
 

@@ -38,6 +38,8 @@ constexpr int CAP = 8192;  // candidates of the threshold bin kept in shared mem
 constexpr int KMAX = 4096;
 constexpr int SWEEP_U = 4;  // 128-position steps whose loads a warp issues together
 
+constexpr int MAX_TP = 8;
+
 struct TopkParams {
   int32_t* idx;
   const float* score;
@@ -47,6 +49,39 @@ struct TopkParams {
   int64_t score_stride;
   int max_kv;
   int K;
+  // payload mode (pay != null): row b is written to pay + b * pay_stride as
+  // K f32 values then K int32 positions + pos_off (bit-cast), -inf / -1 pads
+  float* pay;
+  int64_t pay_stride;
+  int pos_off;
+  int32_t* hist_clear;  // when set (== hist): each hist row is zeroed once read
+  // exchange staging (ctl != null): the payload goes to slot (seq & 1) of
+  // this rank's exchange buffer, seq = ctl[0] + 1, after every peer merged
+  // seq - 2; the last CTA publishes staged = seq on my_flags[0]
+  int* ctl;
+  int* my_flags;
+  const int* peer_merged[MAX_TP];
+  int tp;
+  int64_t slot_bytes;
+  int64_t timeout_ns;
+  int32_t* err;
+};
+
+// Where the selected positions of one row go.
+struct Emit {
+  int32_t* idx;        // index mode
+  float* val;          // payload mode: values ...
+  int32_t* pos;        // ... and shifted positions
+  const float* row;
+  int off;
+  __device__ __forceinline__ void operator()(int o, int P) const {
+    if (val) {
+      val[o] = P >= 0 ? row[P] : __int_as_float(0xff800000);
+      pos[o] = P >= 0 ? P + off : -1;
+    } else {
+      idx[o] = P;
+    }
+  }
 };
 
 struct TopkSmem {
@@ -59,6 +94,7 @@ struct TopkSmem {
   uint32_t warp_off[32];
   int T;
   uint32_t above, total;
+  int ok;
 };
 
 // Block-wide: find the largest bin T with count(bins >= T) >= need, scanning
@@ -176,7 +212,7 @@ __device__ __forceinline__ int count_below(const int32_t* a, int m, int32_t x) {
 // Rows whose threshold bin overflows the candidate buffer: two more radix
 // levels and an ordered compaction, all over global memory.
 template <int NT>
-__device__ void select_global(const float* row, int n, int K, uint32_t T1, uint32_t need2, int32_t* out,
+__device__ void select_global(const float* row, int n, int K, uint32_t T1, uint32_t need2, const Emit& out,
                               TopkSmem& s) {
   const int tid = threadIdx.x;
   for (int i = tid; i < NBIN1; i += NT) s.hist[i] = 0;
@@ -209,26 +245,24 @@ __device__ void select_global(const float* row, int n, int K, uint32_t T1, uint3
     const uint32_t n_eq = s.total;
     const bool sel = in && (key > kth || (eq && tie_rank < n_ties));
     const uint32_t pos = out_base + block_exclusive<NT>(sel ? 1u : 0u, s.warp, &s.total);
-    if (sel && pos < (uint32_t)K) out[pos] = i;
+    if (sel && pos < (uint32_t)K) out((int)pos, i);
     out_base += s.total;
     tie_base += n_eq;
   }
 }
 
 template <int NT>
-__global__ void __launch_bounds__(NT, 1024 / NT) topk_rows_kernel(const TopkParams p) {
+__device__ void topk_row(const TopkParams& p, int b, const Emit& out, TopkSmem& s) {
   constexpr int NWARP = NT / 32;
-  extern __shared__ __align__(16) unsigned char smem_raw[];
-  TopkSmem& s = *reinterpret_cast<TopkSmem*>(smem_raw);
-  const int b = blockIdx.x;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int K = p.K;
-  int32_t* out = p.idx + (int64_t)b * p.idx_stride;
-  const float* row = p.score + (int64_t)b * p.score_stride;
+  const float* row = out.row;
   const int n = max(0, min(p.lens[b], p.max_kv));
 
   if (n <= K) {  // everything valid is selected
-    for (int i = tid; i < K; i += NT) out[i] = i < n ? i : -1;
+    for (int i = tid; i < K; i += NT) out(i, i < n ? i : -1);
+    if (p.hist_clear)
+      for (int i = tid; i < NBIN1; i += NT) p.hist_clear[(int64_t)b * NBIN1 + i] = 0;
     return;
   }
   const bool vec = (reinterpret_cast<uintptr_t>(row) & 15) == 0;
@@ -238,7 +272,10 @@ __global__ void __launch_bounds__(NT, 1024 / NT) topk_rows_kernel(const TopkPara
 
   // ---- 1. level-1 histogram: bits 31..20
   if (p.hist) {
-    for (int i = tid; i < NBIN1; i += NT) s.hist[i] = (uint32_t)p.hist[(int64_t)b * NBIN1 + i];
+    for (int i = tid; i < NBIN1; i += NT) {
+      s.hist[i] = (uint32_t)p.hist[(int64_t)b * NBIN1 + i];
+      if (p.hist_clear) p.hist_clear[(int64_t)b * NBIN1 + i] = 0;
+    }
   } else {
     for (int i = tid; i < NBIN1; i += NT) s.hist[i] = 0;
     __syncthreads();
@@ -408,14 +445,59 @@ __global__ void __launch_bounds__(NT, 1024 / NT) topk_rows_kernel(const TopkPara
   for (int i = tid; i < (int)n_sure; i += NT) {
     const int32_t P = s.sure[i];
     const int o = i + count_below(s.sel, (int)n_sel, P);
-    if (o < K) out[o] = P;
+    if (o < K) out(o, P);
   }
   for (int i = tid; i < (int)n_sel; i += NT) {
     const int32_t P = s.sel[i];
     const int o = i + count_below(s.sure, (int)n_sure, P);
-    if (o < K) out[o] = P;
+    if (o < K) out(o, P);
   }
-  for (int i = (int)(n_sure + n_sel) + tid; i < K; i += NT) out[i] = -1;  // only for an inconsistent histogram
+  for (int i = (int)(n_sure + n_sel) + tid; i < K; i += NT) out(i, -1);  // only for an inconsistent histogram
+}
+
+template <int NT>
+__global__ void __launch_bounds__(NT, 1024 / NT) topk_rows_kernel(const TopkParams p) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  TopkSmem& s = *reinterpret_cast<TopkSmem*>(smem_raw);
+  const int b = blockIdx.x;
+  const int tid = threadIdx.x;
+  Emit e{};
+  e.row = p.score + (int64_t)b * p.score_stride;
+  float* pay = p.pay;
+  int seq = 0;
+  bool ok = true;
+  if (p.ctl) {  // exchange staging: wait until every peer is done with this slot
+    seq = *reinterpret_cast<const volatile int*>(p.ctl) + 1;
+    pay += (int64_t)(seq & 1) * (p.slot_bytes / 4);
+    if (tid == 0) s.ok = read_err_word(p.err) == 0;
+    __syncthreads();
+    if (seq > 2 && s.ok && tid < p.tp && !wait_flag_geq(p.peer_merged[tid], seq - 2, p.timeout_ns, p.err)) s.ok = 0;
+    __syncthreads();
+    ok = s.ok != 0;
+  }
+  if (pay) {
+    e.val = pay + (int64_t)b * p.pay_stride;
+    e.pos = reinterpret_cast<int32_t*>(e.val + p.K);
+    e.off = p.pos_off;
+  } else {
+    e.idx = p.idx + (int64_t)b * p.idx_stride;
+  }
+  if (ok) {
+    topk_row<NT>(p, b, e, s);
+  } else if (p.hist_clear) {
+    for (int i = tid; i < NBIN1; i += NT) p.hist_clear[(int64_t)b * NBIN1 + i] = 0;
+  }
+  if (p.ctl) {  // the last CTA publishes staged = seq (nothing after an error)
+    __syncthreads();
+    if (tid == 0) {
+      __threadfence_system();
+      if (atomicAdd(p.ctl + 1, 1) == (int)gridDim.x - 1) {
+        p.ctl[1] = 0;
+        __threadfence_system();
+        if (read_err_word(p.err) == 0) st_release_sys_s32(p.my_flags, seq);
+      }
+    }
+  }
 }
 
 std::once_flag g_once[kMaxDevices];
@@ -425,9 +507,9 @@ int run_topk(const TopkParams& p, int B, cudaStream_t s) {
   DSA_REQUIRE(B >= 0 && p.max_kv >= 0, DSA_ERR_INVALID, "topk: negative size");
   DSA_REQUIRE(p.K >= 1 && p.K <= KMAX, DSA_ERR_UNSUPPORTED, "topk: K must be in [1, %d] (got %d)", KMAX, p.K);
   if (B == 0) return DSA_OK;
-  DSA_REQUIRE(p.idx && p.lens && (p.score || p.max_kv == 0), DSA_ERR_INVALID, "topk: null pointer");
-  DSA_REQUIRE(p.idx_stride >= p.K && p.score_stride >= p.max_kv, DSA_ERR_INVALID,
-              "topk: row stride smaller than the row");
+  DSA_REQUIRE((p.idx || p.pay) && p.lens && (p.score || p.max_kv == 0), DSA_ERR_INVALID, "topk: null pointer");
+  DSA_REQUIRE((p.pay ? p.pay_stride >= 2 * (int64_t)p.K : p.idx_stride >= p.K) && p.score_stride >= p.max_kv,
+              DSA_ERR_INVALID, "topk: row stride smaller than the row");
   const int dev = current_device();
   DSA_REQUIRE(dev >= 0 && dev < kMaxDevices, DSA_ERR_UNSUPPORTED, "topk: device %d out of range", dev);
   std::call_once(g_once[dev], [dev] {
@@ -466,5 +548,58 @@ extern "C" int dsa_topk_rows(int32_t* idx, int64_t idx_stride, const float* scor
                              int max_kv, const int32_t* lens, int B, int K, void* stream) {
   clear_error();
   TopkParams p{idx, score, lens, nullptr, idx_stride, score_stride, max_kv, K};
+  return run_topk(p, B, as_stream(stream));
+}
+
+extern "C" int dsa_topk_rows_payload(float* pay, int64_t pay_stride, const float* score, int64_t score_stride,
+                                     int max_kv, const int32_t* lens, int32_t* hist, int B, int K, int pos_off,
+                                     void* stream) {
+  clear_error();
+  TopkParams p{};
+  p.score = score;
+  p.lens = lens;
+  p.hist = hist;
+  p.hist_clear = hist;
+  p.score_stride = score_stride;
+  p.max_kv = max_kv;
+  p.K = K;
+  p.pay = pay;
+  p.pay_stride = pay_stride;
+  p.pos_off = pos_off;
+  return run_topk(p, B, as_stream(stream));
+}
+
+extern "C" int dsa_shard_exchange_topk(const float* score, int64_t score_stride, int max_kv, const int32_t* lens,
+                                       int32_t* hist, int B, int K, int pos_off, void* slot_base,
+                                       int64_t slot_bytes, const uint64_t* flag_ptrs, int tp, int rank,
+                                       int32_t* ctl, int64_t timeout_ns, int32_t* err_flag, void* stream) {
+  clear_error();
+  DSA_REQUIRE(tp >= 1 && tp <= MAX_TP && rank >= 0 && rank < tp, DSA_ERR_UNSUPPORTED,
+              "shard_exchange_topk: tp must be in [1, %d] and rank < tp", MAX_TP);
+  DSA_REQUIRE(K >= 1 && K <= 2048, DSA_ERR_UNSUPPORTED, "shard_exchange_topk: K must be in [1, 2048]");
+  DSA_REQUIRE(B >= 1 && slot_base && flag_ptrs && ctl && err_flag && timeout_ns > 0 &&
+                  slot_bytes >= (int64_t)B * 2 * K * 4 && slot_bytes % 16 == 0,
+              DSA_ERR_INVALID, "shard_exchange_topk: bad arguments");
+  TopkParams p{};
+  p.score = score;
+  p.lens = lens;
+  p.hist = hist;
+  p.hist_clear = hist;
+  p.score_stride = score_stride;
+  p.max_kv = max_kv;
+  p.K = K;
+  p.pay = reinterpret_cast<float*>(slot_base);
+  p.pay_stride = 2 * (int64_t)K;
+  p.pos_off = pos_off;
+  p.ctl = ctl;
+  p.tp = tp;
+  p.slot_bytes = slot_bytes;
+  p.timeout_ns = timeout_ns;
+  p.err = err_flag;
+  for (int s = 0; s < tp; ++s) {
+    DSA_REQUIRE(flag_ptrs[s] != 0, DSA_ERR_INVALID, "shard_exchange_topk: null flag pointer %d", s);
+    p.peer_merged[s] = reinterpret_cast<const int*>(flag_ptrs[s]) + 1;
+  }
+  p.my_flags = reinterpret_cast<int*>(flag_ptrs[rank]);
   return run_topk(p, B, as_stream(stream));
 }

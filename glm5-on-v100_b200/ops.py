@@ -245,6 +245,77 @@ def check_p2p_status(device) -> None:
         raise RuntimeError(f"P2P shard exchange wait failed on {device}: status {L.STATUS_NAMES.get(v, v)}")
 
 
+def p2p_failed(device) -> bool:
+    """True (and the error word cleared) if a bounded P2P wait on `device`
+    expired since the last check; synchronises with the device."""
+    f = p2p_error_flag(device)
+    v = int(f.item())
+    if v != 0:
+        f.zero_()
+    return v != 0
+
+
+def shard_stage(slot_rows, vals, idx) -> None:
+    """slot_rows f32 [R, 2K] <- [vals | idx bits]; skipped on the device when
+    an earlier P2P wait failed (the slot may still be read by a peer)."""
+    R, K = vals.shape
+    _check(slot_rows.dtype == torch.float32 and slot_rows.is_contiguous() and tuple(slot_rows.shape) == (R, 2 * K),
+           "slot_rows must be contiguous f32 [R, 2K]")
+    _check(vals.dtype == torch.float32 and idx.dtype == torch.int32 and vals.stride(1) == 1 and idx.stride(1) == 1,
+           "vals f32 / idx int32 with unit inner stride")
+    with torch.cuda.device(slot_rows.device):
+        L.call("dsa_indexer_shard_stage", _vp(slot_rows), _vp(vals), vals.stride(0), _vp(idx), idx.stride(0), R, K,
+               _vp(p2p_error_flag(slot_rows.device)), _stream(slot_rows.device))
+
+
+def topk_rows_payload(pay, score, lens, hist, k: int, pos_off: int) -> None:
+    """Local top-k of a key shard written as payload rows pay[:, :k] = values,
+    pay[:, k:2k] = positions + pos_off (f32 bits); hist (or None) is consumed
+    and zeroed."""
+    _check(score.dtype == torch.float32 and pay.dtype == torch.float32, "score and pay must be fp32")
+    _rowmajor(score, "score")
+    _rowmajor(pay, "pay")
+    _int32(lens, "lengths")
+    B = score.size(0)
+    _check(pay.size(0) >= B and pay.size(1) >= 2 * k, "pay must be [B, >= 2k]")
+    hp = None
+    if hist is not None:
+        _check(hist.dtype == torch.int32 and hist.is_contiguous() and tuple(hist.shape) == (B, 4096),
+               "hist must be contiguous int32 [B, 4096]")
+        hp = _vp(hist)
+    with torch.cuda.device(score.device):
+        L.call("dsa_topk_rows_payload", _vp(pay), pay.stride(0), _vp(score), score.stride(0), score.size(1),
+               _vp(lens.reshape(-1).contiguous()), hp, B, int(k), int(pos_off), _stream(score.device))
+
+
+def shard_exchange_topk(ex, score, lens, hist, k: int, pos_off: int) -> None:
+    """Decode exchange, stage half: this rank's local top-k rows into slot
+    (seq & 1) of ex.buf, then staged = seq (no host sequencing; see
+    dsa_shard_exchange_topk)."""
+    _check(score.dtype == torch.float32, "score must be fp32")
+    _rowmajor(score, "score")
+    B = score.size(0)
+    hp = None
+    if hist is not None:
+        _check(hist.dtype == torch.int32 and hist.is_contiguous() and tuple(hist.shape) == (B, 4096),
+               "hist must be contiguous int32 [B, 4096]")
+        hp = _vp(hist)
+    with torch.cuda.device(score.device):
+        L.call("dsa_shard_exchange_topk", _vp(score), score.stride(0), score.size(1), _vp(lens), hp, B, int(k),
+               int(pos_off), ctypes.c_void_p(ex.buf.data_ptr()), ex.slot_bytes, ex.flag_arr, ex.tp, ex.rank,
+               _vp(ex.ctl), P2P_TIMEOUT_NS, _vp(p2p_error_flag(score.device)), _stream(score.device))
+
+
+def shard_exchange_merge(ex, out, R: int) -> None:
+    """Decode exchange, merge half: the global top-k of rows 0..R-1 from every
+    rank's slot into out[0:R] (ascending, -1 first), then merged = seq."""
+    _check(out.dtype == torch.int32 and out.dim() == 2 and out.stride(1) == 1, "out must be int32 2-D")
+    with torch.cuda.device(out.device):
+        L.call("dsa_shard_exchange_merge", _vp(out), out.stride(0), ex.data_arr, ex.flag_arr, ex.tp, ex.rank, int(R),
+               ex.K, ex.slot_bytes, _vp(ex.ctl), P2P_TIMEOUT_NS, _vp(p2p_error_flag(out.device)),
+               _stream(out.device))
+
+
 def _u64_array(t, tp):
     _check(t.device.type == "cpu" and t.dtype == torch.int64 and t.numel() >= tp, "pointer tensors must be CPU int64")
     arr = (ctypes.c_uint64 * tp)(*[int(x) for x in t.reshape(-1)[:tp].tolist()])
@@ -297,8 +368,8 @@ def _ipc_open_impl(handle):
 
 
 def _ipc_flag_set_impl(flag_ptr, which, seq):
-    L.call("dsa_ipc_flag_set", int(flag_ptr), int(which), int(seq),
-           _stream(torch.device("cuda", torch.cuda.current_device())))
+    dev = torch.device("cuda", torch.cuda.current_device())
+    L.call("dsa_ipc_flag_set", int(flag_ptr), int(which), int(seq), _vp(p2p_error_flag(dev)), _stream(dev))
 
 
 def _ipc_slot_wait_impl(flag_ptrs, tp, min_seq):

@@ -14,12 +14,16 @@ Differences from the reference, by design:
     128 rows (results are per row, so identical);
   * shard merges take any tp in [1, 8] and any K <= 2048 (the reference's
     fused kernels: tp in [2, 4], K == 2048);
-  * device waits of the P2P exchange are bounded and raise on timeout; the
-    state then falls back to the all-gather path permanently, as the
-    reference does on an init failure (sai.py:100-105).
+  * device waits of the P2P exchange are bounded; after one expires on any
+    rank, every rank (agreeing over the host) redoes the step through the
+    all-gather path and stays on it (the reference falls back only when its
+    init fails, sai.py:100-105);
+  * decode rows can be key-sharded too (ShardConfig.decode), with an
+    exchange whose sequence number lives on the device.
 """
 from __future__ import annotations
 
+import ctypes
 import logging
 from dataclasses import dataclass, field
 from typing import Callable, List, Optional
@@ -61,14 +65,23 @@ class IndexerMeta:
 
 @dataclass
 class ShardConfig:
-    """Key sharding of prefill scoring across tp ranks (sai.py:726-880)."""
+    """Key sharding of indexer scoring across tp ranks (prefill: sai.py:726-880;
+    decode rows too when `decode` is set) and the state of its merge."""
     tp: int = 1
     rank: int = 0
     min_ctx: int = 16384               # VLLM_SM70_IDXER_TP_SHARD_MIN_CTX default
     group: object = None               # torch.distributed group for the all-gather
-    cpu_group: object = None           # group for the IPC handle exchange
+    cpu_group: object = None           # gloo group: IPC handle exchange and the ranks' agreement
     merge: str = "fused"               # "p2p" | "fused" | "torch"
     rows_cap: int = 1024               # P2P slot capacity (max_num_batched_tokens)
+    decode: bool = False               # also split every decode row's keys across the ranks
+    backend: object = None             # ops module (or a stand-in with its IPC/merge functions)
+    agree: Optional[Callable] = None   # AND over the ranks (default: all_reduce MIN on cpu_group)
+    gather: Optional[Callable] = None  # [R, 2K] -> [tp*R, 2K] (default: NCCL all_gather_into_tensor)
+    p2p: object = None                 # P2PExchange, built on the first merge
+    decode_exchange: object = None     # DecodeExchange, built on the first sharded decode step
+    p2p_init_failed: bool = False
+    p2p_failed: bool = False           # set on every rank together: P2P is off from then on
 
 
 # Per-chunk (tok_lo, n_q, ke) entries handed to the sparse prefill attention
@@ -142,12 +155,9 @@ def torch_merge_epilogue(allf: torch.Tensor, K: int):
 
 
 # ------------------------------------------------------------- P2P state
-class P2PExchange:
-    """Double-buffered shard slots in CUDA IPC memory plus {staged, merged}
-    flags per rank (sai.py:44-106, :885-952). Per merge with sequence seq:
-    slot = seq & 1; wait until every peer merged seq-2 (slot reuse), stage my
-    payload, publish staged = seq, merge reading all peers' slots, publish
-    merged = seq. All device waits are bounded (ops.P2P_TIMEOUT_NS)."""
+class _IpcSlots:
+    """Two payload slots and a {staged, merged} flag pair in CUDA IPC memory,
+    opened on every rank of the shard group (sai.py:44-106)."""
 
     def __init__(self, device, tp: int, rank: int, K: int, rows_cap: int, cpu_group=None,
                  all_gather_object: Optional[Callable] = None, backend=ops):
@@ -156,7 +166,7 @@ class P2PExchange:
         self.backend = backend
         self.device = device
         self.tp, self.rank, self.K, self.rows_cap = tp, rank, K, rows_cap
-        self.slot_bytes = rows_cap * 2 * K * 4
+        self.slot_bytes = (rows_cap * 2 * K * 4 + 15) // 16 * 16
         self.buf, handle = backend.sm70_ipc_alloc(2 * self.slot_bytes)
         self.fbuf, fhandle = backend.sm70_ipc_alloc(64)
         payload = (handle.numpy().tobytes(), fhandle.numpy().tobytes())
@@ -172,72 +182,123 @@ class P2PExchange:
                 flag_ptrs.append(backend.sm70_ipc_open(torch.frombuffer(bytearray(fh), dtype=torch.uint8)))
         self.data_ptrs_t = torch.tensor(data_ptrs, dtype=torch.int64)
         self.flag_ptrs_t = torch.tensor(flag_ptrs, dtype=torch.int64)
+        self.data_arr = (ctypes.c_uint64 * tp)(*data_ptrs)
+        self.flag_arr = (ctypes.c_uint64 * tp)(*flag_ptrs)
         self.my_flag_ptr = self.fbuf.data_ptr()
+
+
+class P2PExchange(_IpcSlots):
+    """Host-sequenced exchange of the prefill merge (sai.py:885-952). Per merge
+    with sequence seq: slot = seq & 1; wait until every peer merged seq-2
+    (slot reuse), stage my payload, publish staged = seq, merge reading all
+    peers' slots, publish merged = seq. Every device wait is bounded
+    (ops.P2P_TIMEOUT_NS); after one expires the rank's error word is set, the
+    stage and both flag stores of that merge do nothing, and the merge kernel
+    returns at once, so no peer reads a half-written slot. The caller learns
+    of it from backend.p2p_failed()."""
+
+    def __init__(self, *args, **kwargs):
+        super().__init__(*args, **kwargs)
         self.seq = 0
 
     def merge(self, pending, out: torch.Tensor) -> None:
-        K = self.K
+        K, be = self.K, self.backend
         R = sum(p[1] for p in pending)
         self.seq += 1
         seq = self.seq
         soff = (seq & 1) * self.slot_bytes
         if seq > 2:
-            self.backend.sm70_ipc_slot_wait(self.flag_ptrs_t, self.tp, seq - 2)
+            be.sm70_ipc_slot_wait(self.flag_ptrs_t, self.tp, seq - 2)
         slot_view = self.buf[soff:soff + R * 2 * K * 4].view(torch.float32).view(R, 2 * K)
         ro = 0
         for _, n_r, lv, gi in pending:
-            slot_view[ro:ro + n_r, :K] = lv
-            slot_view[ro:ro + n_r, K:] = gi.view(torch.float32)
+            be.shard_stage(slot_view[ro:ro + n_r], lv, gi)
             ro += n_r
-        self.backend.sm70_ipc_flag_set(self.my_flag_ptr, 0, seq)
+        be.sm70_ipc_flag_set(self.my_flag_ptr, 0, seq)
         dst, base = destination(pending, out.device)
-        self.backend.sm70_indexer_shard_merge_p2p(out, self.data_ptrs_t, self.flag_ptrs_t, dst, base, K, self.tp,
-                                                  R, seq, soff)
-        self.backend.sm70_ipc_flag_set(self.my_flag_ptr, 1, seq)
+        be.sm70_indexer_shard_merge_p2p(out, self.data_ptrs_t, self.flag_ptrs_t, dst, base, K, self.tp, R, seq, soff)
+        be.sm70_ipc_flag_set(self.my_flag_ptr, 1, seq)
 
 
-_P2P_STATE: Optional[P2PExchange] = None
-_P2P_FAILED = False
+class DecodeExchange(_IpcSlots):
+    """Device-sequenced exchange of the key-sharded decode indexer: the
+    sequence number lives in a device control block (ctl[0]) that the merge
+    kernel advances, so a decode step (logits -> local top-k into my slot ->
+    merge over peer slots) is stream-ordered device work a CUDA graph can
+    replay (dsa_shard_exchange_topk / dsa_shard_exchange_merge). No
+    reference counterpart: the reference shards prefill only."""
+
+    def __init__(self, *args, **kwargs):
+        super().__init__(*args, **kwargs)
+        self.ctl = torch.zeros(4, dtype=torch.int32, device=self.buf.device)
+
+    def topk_stage(self, score, lens, hist, pos_off: int) -> None:
+        self.backend.shard_exchange_topk(self, score, lens, hist, self.K, pos_off)
+
+    def merge(self, out: torch.Tensor, R: int) -> None:
+        self.backend.shard_exchange_merge(self, out, R)
 
 
-def _p2p_state(device, shard: ShardConfig, K: int):
-    global _P2P_STATE, _P2P_FAILED
-    if _P2P_FAILED:
-        return None
-    if _P2P_STATE is None:
+def all_ranks_ok(ok: bool, shard: "ShardConfig") -> bool:
+    """AND of `ok` over the shard group, on the host (gloo cpu_group), so that
+    every rank takes the same merge path in the same step."""
+    if shard.tp <= 1:
+        return ok
+    if shard.agree is not None:
+        return bool(shard.agree(ok))
+    import torch.distributed as dist
+
+    t = torch.tensor([1 if ok else 0], dtype=torch.int32)
+    dist.all_reduce(t, op=dist.ReduceOp.MIN, group=shard.cpu_group)
+    return bool(t.item())
+
+
+def _p2p_state(device, shard: ShardConfig, K: int) -> Optional[P2PExchange]:
+    if shard.p2p is None and not shard.p2p_init_failed:
         try:
-            _P2P_STATE = P2PExchange(device, shard.tp, shard.rank, K, shard.rows_cap, shard.cpu_group)
+            shard.p2p = P2PExchange(device, shard.tp, shard.rank, K, shard.rows_cap, shard.cpu_group,
+                                    backend=shard.backend or ops)
             logger.info("P2P shard merge initialised (tp=%d, rows_cap=%d)", shard.tp, shard.rows_cap)
         except Exception:
-            logger.exception("P2P shard merge init failed; using the all-gather path")
-            _P2P_FAILED = True
-            return None
-    return _P2P_STATE
+            logger.exception("P2P shard merge init failed on this rank")
+            shard.p2p_init_failed = True
+    return shard.p2p
 
 
 def merge_shards(pending, topk_indices_buffer: torch.Tensor, K: int, shard: ShardConfig) -> None:
     """Exact global top-K of the rows in `pending` from every rank's local
-    candidates, written to topk_indices_buffer (sai.py:881-1030)."""
-    global _P2P_FAILED
+    candidates, written to topk_indices_buffer (sai.py:881-1030).
+
+    merge="p2p": every rank first agrees (host AND over the group) that its
+    exchange exists; after the merge every rank reports whether one of its
+    bounded waits expired, and if any did, ALL ranks redo this step through
+    the all-gather path and stay on it (the reference falls back only when
+    init fails, sai.py:100-105). Ranks therefore never run different
+    collectives."""
     if not pending:
         return
     device = topk_indices_buffer.device
     R = sum(p[1] for p in pending)
-    if shard.merge == "p2p":
+    if shard.merge == "p2p" and not shard.p2p_failed:
         st = _p2p_state(device, shard, K)
-        if st is not None and R <= st.rows_cap:
-            try:
-                st.merge(pending, topk_indices_buffer)
-                ops.check_p2p_status(device)
+        if not all_ranks_ok(st is not None, shard):
+            shard.p2p_failed = True
+            logger.warning("P2P shard merge unavailable on some rank; every rank uses the all-gather path")
+        elif R <= st.rows_cap:  # R is the same on every rank: all take this branch together
+            st.merge(pending, topk_indices_buffer)
+            if all_ranks_ok(not st.backend.p2p_failed(device), shard):
                 return
-            except RuntimeError:
-                logger.exception("P2P shard merge failed; switching to the all-gather path")
-                _P2P_FAILED = True
-    import torch.distributed as dist
-
+            shard.p2p_failed = True
+            logger.warning("P2P shard merge wait expired on some rank; every rank redoes the step through the "
+                           "all-gather path and stays on it")
     fused = pack_payload(pending, K, device)
-    allf = torch.empty((shard.tp * R, 2 * K), dtype=torch.float32, device=device)
-    dist.all_gather_into_tensor(allf, fused, group=shard.group)
+    if shard.gather is not None:
+        allf = shard.gather(fused)
+    else:
+        import torch.distributed as dist
+
+        allf = torch.empty((shard.tp * R, 2 * K), dtype=torch.float32, device=device)
+        dist.all_gather_into_tensor(allf, fused, group=shard.group)
     allf = allf.view(shard.tp, R, 2 * K)
     if shard.merge == "torch":
         mi = torch_merge_epilogue(allf, K)
@@ -247,7 +308,56 @@ def merge_shards(pending, topk_indices_buffer: torch.Tensor, K: int, shard: Shar
             ro += n_r
         return
     dst, base = destination(pending, device)
-    ops.sm70_indexer_shard_merge(topk_indices_buffer, allf, dst, base, K)
+    (shard.backend or ops).sm70_indexer_shard_merge(topk_indices_buffer, allf.contiguous(), dst, base, K)
+
+
+def decode_span(max_kv: int, shard: ShardConfig, page: int):
+    """(off, span, pg_lo, pg_hi) of this rank's contiguous key span of every
+    decode row (the prefill split of sai.py:797-806 over the block-table
+    width, so the span is fixed per rank and a captured step needs no host
+    sync)."""
+    off, span = shard_span(max_kv, shard.tp, shard.rank, page)
+    pg_lo = min(off // page, max(max_kv // page - 1, 0))
+    pg_hi = max(min(max_kv // page, (off + span + page - 1) // page), pg_lo + 1)
+    return off, (pg_hi - pg_lo) * page, pg_lo, pg_hi
+
+
+def decode_indexer_sharded(q, kv_cache, weights, block_table, seq_lens, topk_tokens, out_idx, shard: ShardConfig,
+                           bufs: Optional[dict] = None) -> None:
+    """Key-sharded decode indexer: this rank scores keys [off, off+span) of
+    every row (with the fused histogram), selects its local top-K straight
+    into payload rows, and the exact merge over all ranks writes the global
+    top-K of every row to out_idx on every rank.
+
+    merge="p2p" runs the device-sequenced DecodeExchange (no host sync; the
+    caller checks ops.p2p_failed at a point of its choosing); otherwise the
+    payload goes through the NCCL all-gather and the fused merge kernel."""
+    nd = q.shape[0]
+    page = kv_cache.shape[1]
+    max_kv = block_table.shape[1] * page
+    off, span, pg_lo, pg_hi = decode_span(max_kv, shard, page)
+    bufs = {} if bufs is None else bufs
+    if bufs.get("shape") != (nd, span, topk_tokens):
+        dev = q.device
+        bufs.update(shape=(nd, span, topk_tokens), score=torch.empty((nd, span), dtype=torch.float32, device=dev),
+                    hist=torch.zeros((nd, 4096), dtype=torch.int32, device=dev),
+                    pay=torch.empty((nd, 2 * topk_tokens), dtype=torch.float32, device=dev))
+    seg_bt = block_table[:, pg_lo:pg_hi]
+    sl = (seq_lens.to(torch.int32) - off).clamp_(0, span)
+    ops.sm70_indexer_logits(bufs["score"], q, kv_cache, weights, seg_bt, sl, bufs["hist"])
+    if shard.merge == "p2p":
+        ex = shard.decode_exchange
+        if ex is None:
+            ex = DecodeExchange(q.device, shard.tp, shard.rank, topk_tokens, shard.rows_cap, shard.cpu_group,
+                                backend=shard.backend or ops)
+            shard.decode_exchange = ex
+        ex.topk_stage(bufs["score"], sl, bufs["hist"], off)
+        ex.merge(out_idx, nd)
+        return
+    pay = bufs["pay"]
+    ops.topk_rows_payload(pay, bufs["score"], sl, bufs["hist"], topk_tokens, off)
+    pend = [(0, nd, pay[:, :topk_tokens], pay[:, topk_tokens:].contiguous().view(torch.int32))]
+    merge_shards(pend, out_idx, topk_tokens, shard)
 
 
 # ------------------------------------------------------------ main entry
@@ -280,7 +390,10 @@ def sparse_indexer(meta: IndexerMeta, kv_cache: torch.Tensor, q: torch.Tensor, k
         max_kv = bt.shape[1] * page
         score = torch.empty((nd, max_kv), dtype=torch.float32, device=q.device)
         topk_idx = topk_indices_buffer[:nd, :topk_tokens]
-        if fused_decode_topk:
+        if shard.tp > 1 and shard.decode:
+            decode_indexer_sharded(q[:nd].contiguous(), kv_cache, weights[:nd].contiguous(), bt, seq, topk_tokens,
+                                   topk_idx, shard)
+        elif fused_decode_topk:
             hist = torch.zeros((nd, 4096), dtype=torch.int32, device=q.device)
             ops.sm70_indexer_logits(score, q[:nd].contiguous(), kv_cache, weights[:nd].contiguous(), bt, seq, hist)
             ops.sm70_decode_topk(topk_idx, score, seq, hist, topk_tokens)

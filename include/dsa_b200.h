@@ -197,6 +197,17 @@ int dsa_topk_rows(int32_t* idx, int64_t idx_stride, const float* score,
                   int64_t score_stride, int max_kv, const int32_t* lens,
                   int B, int K, void* stream);
 
+/* The same selection written as shard payload rows: pay[b, 0:K] = the
+ * selected scores, pay[b, K:2K] = their positions + pos_off bit-cast to f32
+ * (-inf / -1 for pads), row stride pay_stride floats (>= 2K). This is the
+ * local top-K, the value gather and the global-id shift of a key-sharded
+ * rank (sai.py:841-856) in one launch. hist (may be NULL) is consumed and
+ * zeroed. */
+int dsa_topk_rows_payload(float* pay, int64_t pay_stride, const float* score,
+                          int64_t score_stride, int max_kv,
+                          const int32_t* lens, int32_t* hist, int B, int K,
+                          int pos_off, void* stream);
+
 /* =====================================================================
  * Indexer-K cache scatter.
  * Replaces sm70_indexer_k_store (dsa.cu:2910-2939, kernels :662-706; schema
@@ -262,13 +273,65 @@ int dsa_ipc_free(void* dev_ptr);
 int dsa_ipc_open(const uint8_t* handle, void** dev_ptr);
 int dsa_ipc_close(void* dev_ptr);
 /* Stream-ordered release store: ((int*)flag_ptr)[which] = seq after a
- * system-scope fence. */
-int dsa_ipc_flag_set(uint64_t flag_ptr, int which, int seq, void* stream);
+ * system-scope fence. When err_flag (device int, may be NULL) is non-zero at
+ * that point, nothing is published: a wait before this call failed, and a
+ * peer must not read this rank's slot. */
+int dsa_ipc_flag_set(uint64_t flag_ptr, int which, int seq,
+                     const int32_t* err_flag, void* stream);
 /* Stream-ordered bounded wait until every ((int*)flag_ptrs[s])[1] >=
  * min_seq (s < tp). On expiry (timeout_ns of device time) sets *err_flag
  * to DSA_ERR_TIMEOUT and returns on the device; the host reads err_flag. */
 int dsa_ipc_slot_wait(const uint64_t* flag_ptrs, int tp, int min_seq,
                       int64_t timeout_ns, int32_t* err_flag, void* stream);
+
+/* Stages a shard payload: slot row r = [vals[r, 0:K] | idx[r, 0:K] as f32
+ * bits], r < R (the staging the reference does with two tensor copies,
+ * sai.py:905-913). Returns on the device without writing when *err_flag is
+ * set (a slot wait before it failed, so a peer may still read the slot);
+ * err_flag may be NULL. */
+int dsa_indexer_shard_stage(float* slot, const float* vals,
+                            int64_t vals_stride, const int32_t* idx,
+                            int64_t idx_stride, int R, int K,
+                            const int32_t* err_flag, void* stream);
+
+/* =====================================================================
+ * Key-sharded decode indexer exchange with a device-side sequence counter.
+ * No reference counterpart: the reference shards only prefill scoring and
+ * sequences its exchange from the host (sai.py:885-952); here the decode
+ * step of every rank is stream-ordered device work that a CUDA graph can
+ * replay. Per rank: an IPC buffer of two slots (slot_bytes each, [R, 2K] f32
+ * payload rows), the IPC flag pair {staged, merged} of every rank (flag_ptrs,
+ * HOST array of tp device addresses, this rank's at index rank) and a local
+ * control block ctl (device int32[4], zeroed once: [0] last completed
+ * sequence number, [1] and [2] CTA arrival counters).
+ *
+ * Step seq = ctl[0] + 1:
+ *   dsa_shard_exchange_topk: every peer's merged flag >= seq - 2 (slot
+ *     reuse, bounded wait), then the exact top-K of each score row (as
+ *     dsa_decode_topk; hist, if given, is consumed and zeroed for the next
+ *     step) is written as a payload row of slot (seq & 1) of slot_base: K
+ *     values then K positions + pos_off (-inf / -1 pads); the last CTA
+ *     publishes staged = seq.
+ *   dsa_shard_exchange_merge: every peer's staged flag >= seq (bounded), the
+ *     merge of dsa_indexer_shard_merge over the tp peer slots (plain
+ *     relaxed system-scope peer loads) into out rows 0..R-1; the last CTA
+ *     publishes merged = seq and sets ctl[0] = seq.
+ * A wait that expires sets *err_flag = DSA_ERR_TIMEOUT; later calls then
+ * publish nothing and the host must rebuild the exchange.
+ * ===================================================================== */
+int dsa_shard_exchange_topk(const float* score, int64_t score_stride,
+                            int max_kv, const int32_t* lens, int32_t* hist,
+                            int B, int K, int pos_off, void* slot_base,
+                            int64_t slot_bytes, const uint64_t* flag_ptrs,
+                            int tp, int rank, int32_t* ctl,
+                            int64_t timeout_ns, int32_t* err_flag,
+                            void* stream);
+int dsa_shard_exchange_merge(int32_t* out, int64_t out_stride,
+                             const uint64_t* data_ptrs,
+                             const uint64_t* flag_ptrs, int tp, int rank,
+                             int R, int K, int64_t slot_bytes, int32_t* ctl,
+                             int64_t timeout_ns, int32_t* err_flag,
+                             void* stream);
 
 #ifdef __cplusplus
 }

@@ -27,7 +27,7 @@ def run_ref(*args):
 # --workload name -> the config's workload name
 NAMES = {"decode": "sparse_mla_decode", "indexer_prefill": "indexer_prefill", "sparse_prefill": "sparse_prefill",
          "indexer_decode": "indexer_decode", "shard_merge": "shard_merge", "decode_layer": "decode_layer",
-         "shard_merge_p2p": "shard_merge_p2p"}
+         "shard_merge_p2p": "shard_merge_p2p", "dsa_layer": "dsa_decode_layer"}
 
 
 @pytest.mark.parametrize("workload,extra,unit", [
@@ -35,6 +35,7 @@ NAMES = {"decode": "sparse_mla_decode", "indexer_prefill": "indexer_prefill", "s
     ("indexer_decode", ["--ctx", "4096", "--cpu-rows", "1"], "tok/s"),
     ("shard_merge", ["--cpu-rows", "16"], "rows/s"),
     ("decode_layer", ["--ctx", "4096", "--cpu-rows", "1"], "tok/s"),
+    ("dsa_layer", ["--ctx", "4096", "--cpu-rows", "1"], "tok/s"),
 ])
 def test_reference_arm_json_line(workload, extra, unit):
     d = run_ref("--workload", workload, *extra)

@@ -629,6 +629,127 @@ def test_shard_merge_p2p_local_slots_and_timeout(dsa):
     assert float(x.sum()) == 8.0
 
 
+def sharded_payload(rng, tp, R, K, span, overlap=False, ties=False):
+    """Candidates shaped like the key-sharded pipeline's: shard s holds its
+    local top-K as ascending positions of its own key span (shifted by s *
+    span, or all in one span when overlap is set), -1 / -inf pads at the end
+    of short rows."""
+    vals = rng.standard_normal((tp, R, K)).astype(np.float32)
+    if ties:
+        vals = np.round(vals).astype(np.float32)  # few distinct values: long runs of equal keys
+    pos = np.empty((tp, R, K), np.int32)
+    for s in range(tp):
+        for r in range(R):
+            pos[s, r] = np.sort(rng.choice(span, K, replace=False)) + (0 if overlap else s * span)
+    n_short = min(K, 3)
+    vals[tp - 1, 0, K - n_short:] = -np.inf  # a shard with fewer than K keys in row 0
+    pos[tp - 1, 0, K - n_short:] = -1
+    if R > 2:
+        vals[:, 2, :] = -np.inf  # a row no shard reaches
+        pos[:, 2, :] = -1
+    return np.concatenate([vals, pos.view(np.float32)], axis=2)
+
+
+@pytest.mark.parametrize("tp,K,overlap,ties", [(2, 2048, False, False), (8, 2048, False, False),
+                                               (4, 2048, True, False), (8, 2048, False, True),
+                                               (3, 512, True, True), (5, 6, False, False)])
+def test_shard_merge_sorted_runs(dsa, tp, K, overlap, ties):
+    """The merge's ordered path (every shard's run ascending): disjoint key
+    spans, overlapping spans (binary-searched ranks) and long runs of equal
+    values (column-order tie ranks); bit-exact against the oracle."""
+    rng = np.random.default_rng(tp * 7 + K + 3 * overlap + ties)
+    R = 6
+    allf = sharded_payload(rng, tp, R, K, span=max(4 * K, 64), overlap=overlap, ties=ties)
+    out = torch.full((R, K), -9, dtype=torch.int32, device=DEV)
+    dsa.sm70_indexer_shard_merge(out, to_dev(allf), torch.empty(0, dtype=torch.int32, device=DEV), 0, K)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(out.cpu().numpy(), O.shard_merge(allf, K))
+
+
+def test_shard_merge_all_equal_values(dsa):
+    """Every candidate has the same value: the lower columns win (the first K
+    columns of shard 0), whatever their positions."""
+    tp, R, K = 4, 3, 2048
+    rng = np.random.default_rng(5)
+    vals = np.full((tp, R, K), 1.5, np.float32)
+    pos = rng.permutation(tp * R * K).reshape(tp, R, K).astype(np.int32)
+    allf = np.concatenate([vals, pos.view(np.float32)], axis=2)
+    out = torch.empty(R, K, dtype=torch.int32, device=DEV)
+    dsa.sm70_indexer_shard_merge(out, to_dev(allf), torch.empty(0, dtype=torch.int32, device=DEV), 0, K)
+    torch.cuda.synchronize()
+    exp = O.shard_merge(allf, K)
+    np.testing.assert_array_equal(exp, np.sort(pos[0], axis=1))
+    np.testing.assert_array_equal(out.cpu().numpy(), exp)
+
+
+def test_topk_rows_payload_matches_topk(dsa):
+    """The payload top-k (local top-K + value gather + global-id shift in one
+    launch) against the index top-k on the same scores; its hist is zeroed."""
+    from importlib import import_module
+
+    ops = import_module("glm5-on-v100_b200.ops")
+    rng = np.random.default_rng(12)
+    B, S, K, off = 5, 9000, 2048, 40960
+    s = rng.standard_normal((B, S)).astype(np.float32)
+    lens = np.array([9000, 5000, 2048, 100, 0], np.int32)
+    for b in range(B):
+        s[b, lens[b]:] = -np.inf
+    score, dl = to_dev(s), to_dev(lens)
+    hist = to_dev(O.level1_hist(s, lens))
+    pay = torch.full((B, 2 * K), 7.0, device=DEV)
+    ops.topk_rows_payload(pay, score, dl, hist, K, off)
+    torch.cuda.synchronize()
+    exp = O.topk_rows(s, lens, K)
+    p = pay.cpu().numpy()
+    got_pos = p[:, K:].copy().view(np.int32)
+    np.testing.assert_array_equal(got_pos, np.where(exp >= 0, exp + off, -1))
+    exp_val = np.where(exp >= 0, np.take_along_axis(s, np.maximum(exp, 0), axis=1), -np.inf)
+    np.testing.assert_array_equal(p[:, :K], exp_val)
+    assert int(hist.abs().sum()) == 0
+
+
+def test_decode_exchange_single_rank_steps_and_timeout(dsa):
+    """The device-sequenced decode exchange with one rank (its own slots):
+    five steps in a row (slots alternate, ctl[0] advances, staged/merged
+    flags follow), each exact against the oracle; then a slot-reuse wait that
+    runs out (merged flag forced behind): TIMEOUT is reported, nothing is
+    published, and the context stays usable."""
+    from importlib import import_module
+
+    ops = import_module("glm5-on-v100_b200.ops")
+    sai = import_module("glm5-on-v100_b200.sparse_attn_indexer")
+    rng = np.random.default_rng(21)
+    B, S, K = 6, 12000, 2048
+    ex = sai.DecodeExchange(torch.device(DEV), 1, 0, K, 8, all_gather_object=lambda o, p: o.__setitem__(0, p))
+    lens = np.array([12000, 11000, 3000, 2048, 17, 0], np.int32)
+    dl = to_dev(lens)
+    for step in range(5):
+        s = rng.standard_normal((B, S)).astype(np.float32)
+        score = to_dev(s)
+        out = torch.full((B, K), -9, dtype=torch.int32, device=DEV)
+        ex.topk_stage(score, dl, None, 0)
+        ex.merge(out, B)
+        torch.cuda.synchronize()
+        assert not ops.p2p_failed(DEV)
+        exp = np.sort(O.topk_rows(s, lens, K), axis=1)
+        np.testing.assert_array_equal(out.cpu().numpy(), exp)
+        assert int(ex.ctl[0]) == step + 1
+        assert ex.fbuf.view(torch.int32)[:2].tolist() == [step + 1, step + 1]
+    old = ops.P2P_TIMEOUT_NS
+    ops.P2P_TIMEOUT_NS = 50_000_000  # 50 ms
+    try:
+        ex.fbuf.view(torch.int32)[1] = 0  # merged flag behind: the step-6 slot wait (merged >= 4) cannot finish
+        ex.topk_stage(to_dev(rng.standard_normal((B, S)).astype(np.float32)), dl, None, 0)
+        ex.merge(torch.empty(B, K, dtype=torch.int32, device=DEV), B)
+        torch.cuda.synchronize()
+        assert ops.p2p_failed(DEV)
+        assert ex.fbuf.view(torch.int32)[:2].tolist() == [5, 0]  # neither flag published
+    finally:
+        ops.P2P_TIMEOUT_NS = old
+    x = torch.ones(4, device=DEV) * 2
+    assert float(x.sum()) == 8.0
+
+
 def test_ipc_alloc_handle(dsa):
     buf, handle = dsa.sm70_ipc_alloc(4096)
     assert buf.is_cuda and buf.numel() == 4096 and handle.numel() == 64

@@ -115,13 +115,18 @@ def test_per_token_metadata():
 # ------------------------------------------- P2P exchange, fake IPC backend
 class FakeIPC:
     """CPU stand-in for the IPC ops of ops.py: buffers in a shared registry,
-    device waits as bounded host polls, the merge by the oracle."""
+    device waits as bounded host polls that set an error word on expiry (as
+    the device waits do), the merges by the oracle. A rank built with
+    stall_staged=True never publishes its staged flag (a stuck peer)."""
 
     registry: dict = {}
     lock = threading.Lock()
 
-    def __init__(self, rank, timeout_s=5.0):
+    def __init__(self, rank, timeout_s=5.0, stage_delay_s=0.0):
         self.rank, self.n_alloc, self.timeout_s = rank, 0, timeout_s
+        self.stage_delay_s = stage_delay_s
+        self.err = 0
+        self.merges_p2p = 0
 
     @staticmethod
     def key(rank, i):
@@ -145,27 +150,78 @@ class FakeIPC:
     def _flags(self, ptr):
         return self._buf(ptr).view(torch.int32)
 
-    def _poll(self, cond, what):
+    def _poll(self, cond):
         t0 = time.monotonic()
         while not cond():
-            if time.monotonic() - t0 > self.timeout_s:
-                raise RuntimeError(f"fake IPC wait timed out: {what}")
+            if self.err or time.monotonic() - t0 > self.timeout_s:
+                self.err = 3  # DSA_ERR_TIMEOUT
+                return False
             time.sleep(0.001)
+        return True
 
     def sm70_ipc_flag_set(self, flag_ptr, which, seq):
+        if which == 0 and self.stage_delay_s:
+            time.sleep(self.stage_delay_s)
+        if self.err:
+            return
         self._flags(flag_ptr)[which] = seq
 
     def sm70_ipc_slot_wait(self, flag_ptrs, tp, min_seq):
-        self._poll(lambda: all(int(self._flags(p)[1]) >= min_seq for p in flag_ptrs[:tp].tolist()), "slot")
+        self._poll(lambda: all(int(self._flags(p)[1]) >= min_seq for p in flag_ptrs[:tp].tolist()))
+
+    def shard_stage(self, slot_rows, vals, idx):
+        if self.err:
+            return
+        K = vals.shape[1]
+        slot_rows[:, :K] = vals
+        slot_rows[:, K:] = idx.view(torch.float32)
 
     def sm70_indexer_shard_merge_p2p(self, out, data_ptrs, flag_ptrs, dst_rows, dst_base, topk, tp, R, seq, slot_off):
-        self._poll(lambda: all(int(self._flags(p)[0]) >= seq for p in flag_ptrs[:tp].tolist()), "staged")
+        if self.err or not self._poll(lambda: all(int(self._flags(p)[0]) >= seq for p in flag_ptrs[:tp].tolist())):
+            return
+        self.merges_p2p += 1
         allf = np.stack([self._buf(p)[slot_off:slot_off + R * 2 * topk * 4].view(torch.float32).view(R, 2 * topk)
                          .numpy() for p in data_ptrs[:tp].tolist()])
-        merged = torch.from_numpy(O.shard_merge(allf, topk))
+        self._write(out, O.shard_merge(allf, topk), dst_rows, dst_base, R, topk)
+
+    def sm70_indexer_shard_merge(self, out, allf, dst_rows, dst_base, topk):
+        self._write(out, O.shard_merge(allf.numpy(), topk), dst_rows, dst_base, allf.shape[1], topk)
+
+    @staticmethod
+    def _write(out, merged, dst_rows, dst_base, R, topk):
         rows = dst_rows.tolist() if dst_base < 0 else list(range(dst_base, dst_base + R))
         for i, r in enumerate(rows):
-            out[r, :topk] = merged[i]
+            out[r, :topk] = torch.from_numpy(merged[i])
+
+    def p2p_failed(self, device):
+        failed, self.err = self.err != 0, 0
+        return failed
+
+
+class HostGroup:
+    """Ranks as threads: the host AND and the all-gather of merge_shards."""
+
+    def __init__(self, n):
+        self.n = n
+        self.barrier = threading.Barrier(n, timeout=30)
+        self.slots = [None] * n
+
+    def _exchange(self, rank, v):
+        self.slots[rank] = v
+        self.barrier.wait()
+        got = list(self.slots)
+        self.barrier.wait()
+        return got
+
+    def agree(self, rank, ok):
+        return all(self._exchange(rank, bool(ok)))
+
+    def gather(self, rank, t):
+        return torch.cat(self._exchange(rank, t.clone()), dim=0)
+
+
+def _handles(tp):
+    return [[FakeIPC.key(r, 0).to_bytes(64, "little"), FakeIPC.key(r, 1).to_bytes(64, "little")] for r in range(tp)]
 
 
 def _payloads(seed, tp, R, K, rounds):
@@ -178,12 +234,29 @@ def _payloads(seed, tp, R, K, rounds):
     return out
 
 
+def _run_ranks(tp, fn):
+    errors = []
+
+    def run(r):
+        try:
+            fn(r)
+        except Exception as e:  # surfaced below
+            errors.append(e)
+
+    threads = [threading.Thread(target=run, args=(r,)) for r in range(tp)]
+    for t in threads:
+        t.start()
+    for t in threads:
+        t.join(60)
+    assert not errors, errors
+
+
 def test_p2p_exchange_protocol_two_ranks():
     """Two ranks (threads) merge three times: the slots alternate (seq & 1)
     and the third merge waits until every rank merged the first."""
     tp, R, K, rounds = 2, 6, 8, 3
     FakeIPC.registry.clear()
-    handles = [[FakeIPC.key(r, 0).to_bytes(64, "little"), FakeIPC.key(r, 1).to_bytes(64, "little")] for r in range(tp)]
+    handles = _handles(tp)
 
     def gather(objs, payload):
         objs[:] = [tuple(h) for h in handles]
@@ -192,22 +265,14 @@ def test_p2p_exchange_protocol_two_ranks():
           for r in range(tp)]
     data = _payloads(11, tp, R, K, rounds)
     outs = [[torch.full((R, K), -9, dtype=torch.int32) for _ in range(rounds)] for _ in range(tp)]
-    errors = []
 
     def run(r):
-        try:
-            for i, (vals, pos) in enumerate(data):
-                pend = [(0, R, torch.from_numpy(vals[r]), torch.from_numpy(pos[r]))]
-                ex[r].merge(pend, outs[r][i])
-        except Exception as e:  # surfaced below
-            errors.append(e)
+        for i, (vals, pos) in enumerate(data):
+            pend = [(0, R, torch.from_numpy(vals[r]), torch.from_numpy(pos[r]))]
+            ex[r].merge(pend, outs[r][i])
+            assert not ex[r].backend.p2p_failed("cpu")
 
-    threads = [threading.Thread(target=run, args=(r,)) for r in range(tp)]
-    for t in threads:
-        t.start()
-    for t in threads:
-        t.join(30)
-    assert not errors, errors
+    _run_ranks(tp, run)
     for i, (vals, pos) in enumerate(data):
         allf = np.concatenate([vals, pos.view(np.float32)], axis=2)
         exp = O.shard_merge(allf, K)
@@ -216,16 +281,52 @@ def test_p2p_exchange_protocol_two_ranks():
     assert [e.seq for e in ex] == [rounds, rounds]
 
 
-def test_p2p_exchange_times_out_when_a_peer_never_stages():
+def test_p2p_exchange_wait_expires_without_staging():
+    """A peer that never stages: the merge wait expires, the error word is
+    set, and nothing after it runs (no merged flag, no output write)."""
     tp, R, K = 2, 2, 4
     FakeIPC.registry.clear()
-    handles = [[FakeIPC.key(r, 0).to_bytes(64, "little"), FakeIPC.key(r, 1).to_bytes(64, "little")] for r in range(tp)]
+    handles = _handles(tp)
     ex = [sai.P2PExchange("cpu", tp, r, K, rows_cap=4, all_gather_object=lambda o, p: o.__setitem__(
         slice(None), [tuple(h) for h in handles]), backend=FakeIPC(r, timeout_s=0.2)) for r in range(tp)]
-    vals = torch.zeros(R, K)
-    pos = torch.zeros(R, K, dtype=torch.int32)
-    with pytest.raises(RuntimeError, match="timed out"):
-        ex[0].merge([(0, R, vals, pos)], torch.empty(R, K, dtype=torch.int32))
+    out = torch.full((R, K), -9, dtype=torch.int32)
+    ex[0].merge([(0, R, torch.zeros(R, K), torch.zeros(R, K, dtype=torch.int32))], out)
+    assert ex[0].backend.p2p_failed("cpu")
+    assert int(ex[0].fbuf.view(torch.int32)[1]) == 0  # merged flag never published
+    assert (out == -9).all()
+
+
+def test_p2p_failure_on_one_rank_moves_every_rank_to_the_all_gather_path():
+    """Rank 1 publishes its staged flag late, so rank 0's merge wait expires
+    while rank 1's merge succeeds. The ranks agree over the host: BOTH redo
+    the step through the all-gather path (same collectives on every rank),
+    both results are exact, and both stay off P2P for the next step."""
+    tp, R, K = 2, 5, 16
+    FakeIPC.registry.clear()
+    handles = _handles(tp)
+    group = HostGroup(tp)
+    backends = [FakeIPC(0, timeout_s=0.3), FakeIPC(1, timeout_s=5.0, stage_delay_s=0.8)]
+    shards = [sai.ShardConfig(tp=tp, rank=r, merge="p2p", rows_cap=8, backend=backends[r],
+                              agree=lambda ok, r=r: group.agree(r, ok), gather=lambda t, r=r: group.gather(r, t))
+              for r in range(tp)]
+    for r in range(tp):  # exchanges built up front (stand-in IPC handle exchange)
+        shards[r].p2p = sai.P2PExchange("cpu", tp, r, K, rows_cap=8, all_gather_object=lambda o, p: o.__setitem__(
+            slice(None), [tuple(h) for h in handles]), backend=backends[r])
+    data = _payloads(5, tp, R, K, 2)
+    outs = [[torch.full((R, K), -9, dtype=torch.int32) for _ in range(2)] for _ in range(tp)]
+
+    def run(r):
+        for i, (vals, pos) in enumerate(data):
+            pend = [(0, R, torch.from_numpy(vals[r]), torch.from_numpy(pos[r]))]
+            sai.merge_shards(pend, outs[r][i], K, shards[r])
+
+    _run_ranks(tp, run)
+    assert [s.p2p_failed for s in shards] == [True, True]
+    assert backends[0].merges_p2p == 0 and backends[1].merges_p2p == 1  # step 2 never tried P2P
+    for i, (vals, pos) in enumerate(data):
+        exp = O.shard_merge(np.concatenate([vals, pos.view(np.float32)], axis=2), K)
+        for r in range(tp):
+            np.testing.assert_array_equal(outs[r][i].numpy(), exp)
 
 
 # ------------------------------------------------ key-sharded merge, gloo
