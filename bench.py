@@ -964,10 +964,12 @@ class ShardedLayerWorkload(DecodeLayerWorkload):
         return self.B * (self.span * (132 + 4) + self.HI * 128 * 2 + self.HI * 4)
 
     def roofline_part(self):
-        """The indexer logits over this rank's key span (the O(S) scan)."""
+        """The indexer logits with the fused histogram over this rank's key
+        span (the O(S) scan), the kernel the layer step launches."""
+        hist = torch.zeros(self.B, 4096, dtype=torch.int32, device=self.bt.device)
         if self.tp == 1:
             def fn(dsa):
-                dsa.sm70_indexer_logits(self.score, self.qi[0], self.k_cache, self.w, self.bt, self.seq, None)
+                dsa.sm70_indexer_logits(self.score, self.qi[0], self.k_cache, self.w, self.bt, self.seq, hist)
         else:
             off, span, lo, hi = self._sai.decode_span(self.bt.shape[1] * self.PAGE, self.shard, self.PAGE)
             score = torch.empty(self.B, span, dtype=torch.float32, device=self.bt.device)
@@ -975,7 +977,7 @@ class ShardedLayerWorkload(DecodeLayerWorkload):
             sl = (self.seq - off).clamp(0, span)
 
             def fn(dsa):
-                dsa.sm70_indexer_logits(score, self.qi[0], self.k_cache, self.w, seg, sl, None)
+                dsa.sm70_indexer_logits(score, self.qi[0], self.k_cache, self.w, seg, sl, hist)
         return fn, self.indexer_bytes()
 
     def roofline_note(self, kind):
