@@ -6,7 +6,8 @@
 // monotone32(score) >> 20). Same function as the reference's decode kernel
 // (csrc/attention/sm70_mla_decode.cu:150-329, histogram :309-319).
 //
-// One CTA = one query row x 4096 positions, in sub-tiles of 128 keys (two
+// One CTA = one query row x up to 4096 positions (fewer when the rows x keys
+// would not fill whole waves of the GPU), in sub-tiles of 128 keys (two
 // pages), 8 warps, two CTAs per SM:
 //   * a page is 64 x 132 = 8,448 contiguous bytes, so each arrives with one
 //     bulk copy (cp.async.bulk, completing on an mbarrier), DSTAGES sub-tiles
@@ -22,6 +23,8 @@
 // memory and added to the global one once per CTA. Every wait is bounded by
 // device time; on expiry the CTA records DSA_ERR_TIMEOUT in the sticky status
 // word, drains its own MMAs, frees TMEM and returns.
+#include <algorithm>
+
 #include "indexer_tc.cuh"
 #include "sparse_mla.cuh"
 #include "tc_common.cuh"
@@ -38,7 +41,7 @@ constexpr int DP = 64;                        // page size served
 constexpr int DP_BYTES = DP * IDXK_ROW;       // 8,448
 constexpr int DSUB = 128;                     // keys per sub-tile (MMA M)
 constexpr int DSTAGES = 3;                    // staged sub-tiles
-constexpr int DCTA_KEYS = 4096;               // positions per CTA
+constexpr int DCTA_KEYS = 4096;               // most positions per CTA
 constexpr int DNT = 256;                      // 8 warps
 constexpr uint32_t KT_REGION = DSUB * 128;    // one 64-dim region of the key tile: 16 KB
 constexpr uint64_t kWaitTimeoutNs = 2000000000ull;
@@ -108,10 +111,10 @@ __global__ void __launch_bounds__(DNT, 2) indexer_decode_tc_kernel(const Indexer
   const uint32_t mb_done = mb_mma + 8u;            // drain on abort
 
   const int b = blockIdx.x;
-  const int p0 = blockIdx.y * DCTA_KEYS;
+  const int p0 = blockIdx.y * a.cta_keys;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   float* score_row = a.score + (int64_t)b * a.score_stride;
-  const int p_end = min(p0 + DCTA_KEYS, a.max_kv);
+  const int p_end = min(p0 + a.cta_keys, a.max_kv);
   const int valid_len = min(a.seq_lens[b], a.max_kv);
   const int v_end = min(p_end, valid_len);  // positions [p0, v_end) are scored
   for (int i = max(p0, v_end) + tid; i < p_end; i += DNT) score_row[i] = -INFINITY;
@@ -337,13 +340,23 @@ int launch_indexer_decode_tc(const IndexerDecodeTcArgs& a, cudaStream_t s) {
   int32_t* err = nullptr;
   st = tc_error_word(dev, &err);
   if (st != DSA_OK) return st;
-  const dim3 grid(a.B, (a.max_kv + DCTA_KEYS - 1) / DCTA_KEYS);
+  // Positions per CTA: whole waves of the resident CTAs (two per SM), at
+  // most DCTA_KEYS each, so few rows or short key spans (a key-sharded rank)
+  // still spread over every SM.
+  IndexerDecodeTcArgs b = a;
+  const int64_t resident = 2LL * sm_count(dev);
+  const int64_t keys = (int64_t)a.B * a.max_kv;
+  const int64_t waves = (keys + resident * DCTA_KEYS - 1) / (resident * DCTA_KEYS);
+  int64_t per = (keys + waves * resident - 1) / std::max<int64_t>(waves * resident, 1);
+  per = (per + DSUB - 1) / DSUB * DSUB;
+  b.cta_keys = (int)std::min<int64_t>(std::max<int64_t>(per, 2 * DSUB), DCTA_KEYS);
+  const dim3 grid(a.B, (a.max_kv + b.cta_keys - 1) / b.cta_keys);
   if (a.n_ihead <= 16)
-    indexer_decode_tc_kernel<16><<<grid, DNT, DecodeTcLayout<16>::BYTES, s>>>(a, err);
+    indexer_decode_tc_kernel<16><<<grid, DNT, DecodeTcLayout<16>::BYTES, s>>>(b, err);
   else if (a.n_ihead <= 32)
-    indexer_decode_tc_kernel<32><<<grid, DNT, DecodeTcLayout<32>::BYTES, s>>>(a, err);
+    indexer_decode_tc_kernel<32><<<grid, DNT, DecodeTcLayout<32>::BYTES, s>>>(b, err);
   else
-    indexer_decode_tc_kernel<64><<<grid, DNT, DecodeTcLayout<64>::BYTES, s>>>(a, err);
+    indexer_decode_tc_kernel<64><<<grid, DNT, DecodeTcLayout<64>::BYTES, s>>>(b, err);
   return check_launch("indexer_decode_tc_kernel");
 }
 

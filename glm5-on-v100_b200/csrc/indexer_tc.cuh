@@ -49,6 +49,7 @@ struct IndexerDecodeTcArgs {
   int max_blocks;
   const int32_t* seq_lens;
   int32_t* hist;       // [B, 4096] or null
+  int cta_keys;        // positions per CTA (set by the launcher)
 };
 
 bool indexer_decode_tc_eligible(int k_format, int page_size, int n_ihead, int packed);
