@@ -920,7 +920,6 @@ int tc_cluster_size(int n_splits) {
 int tc_choose_splits(int B, int head_tiles, int topk, int nsm) {
   const int ntiles = (topk + TM - 1) / TM;
   if (ntiles <= 1) return 1;
-  if (const char* f = getenv("DSA_XP_SPLITS")) return atoi(f);  // EXPERIMENT ONLY
   const double units = (double)B * head_tiles;
   int best = 1;
   double best_cost = 1e300;
