@@ -3,7 +3,11 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
                     [--workload decode|indexer_prefill|sparse_prefill]
 
-Default workload (BASELINE config 2 at 128k context): sparse MLA decode, batch
+Default workload: the DSA decode layer at 180k context, batch 8 (indexer
+logits + top-2048 + sparse MLA decode; on N GPUs the keys of every row are
+split N ways with a P2P top-k merge and the 64 heads N ways); at N = 1 the
+line also carries named sub-records for the rest of the headline metric.
+Sub-record "sparse_mla_decode_b64_ctx128k": sparse MLA decode, batch
 64, 64 heads, q 576-d bf16, fp8_ds_mla paged latent cache (64-token blocks,
 random block permutation), seq_len 131,072, top-k 2,048 sorted uniform
 positions per row, bf16 output. A step is one decode call over the batch.
@@ -13,7 +17,7 @@ sets, so consecutive steps read different cache rows: inputs larger than L2).
 `e2e` times the same call through the public op with the step's q and idx
 copied from pinned host memory and o / lse copied back, every step.
 
-Other workloads (BASELINE configs 3 and 4; same JSON contract, value in
+Other workloads (same JSON contract, value in
 TFLOP/s of the algorithmic FLOPs):
   indexer_prefill  one causal chunk of 65,536 queries x 65,536 keys, 32
                    indexer heads x 128, bf16 q and keys, logits then top-2048
@@ -24,9 +28,11 @@ TFLOP/s of the algorithmic FLOPs):
 
 --impl reference times the reference's own CPU torch path (a port of
 TritonMLAImpl._forward_mqa_torch and of the indexer math, oracle/ref_port.py)
-on the host cores. Multi-GPU (torchrun): each rank runs its own copy of the
-workload (independent rows, no data-path collective; weak scaling); timing is
-the max over ranks.
+on the host cores. Multi-GPU (torchrun, one rank per GPU): the default
+dsa_layer workload splits the fixed batch-8 layer across the ranks (strong
+scaling: keys and heads sharded, P2P exchange of the local top-k lists);
+the other workloads run a copy per rank (weak scaling). Timing is the max
+over ranks.
 """
 from __future__ import annotations
 
@@ -306,7 +312,7 @@ class DecodeWorkload(Workload):
 
 
 class IndexerPrefillWorkload(Workload):
-    """one causal chunk, logits then top-K per row."""
+    """Indexer prefill: one causal chunk of 65,536 queries, logits then top-K per row."""
 
     metric = "indexer prefill TFLOPS (causal QK FLOPs, logits + top-2048)"
     unit = "TFLOP/s"
@@ -408,7 +414,7 @@ class IndexerPrefillWorkload(Workload):
 
 
 class SparsePrefillWorkload(Workload):
-    """sparse prefill attention + indexer-K scatter."""
+    """Sparse prefill attention (16,384 tokens over a 180k cache) + indexer-K scatter."""
 
     metric = "sparse prefill attention TFLOPS (top-2048, 64 heads)"
     unit = "TFLOP/s"
@@ -518,7 +524,7 @@ class SparsePrefillWorkload(Workload):
 
 class IndexerDecodeWorkload(Workload):
     cpu_rows_default = 1
-    """The indexer half of a BASELINE config 2 decode step: per row, logits
+    """The indexer half of a batch-64 decode step: per row, logits
     with the fused level-1 histogram over its 128k keys in the fp8 indexer-K
     cache, then the exact top-2048 from that histogram."""
 
@@ -619,7 +625,7 @@ class IndexerDecodeWorkload(Workload):
 
 class ShardMergeWorkload(Workload):
     cpu_rows_default = 512
-    """The exact merge of the key-sharded indexer (BASELINE config 5's
+    """The exact merge of the key-sharded indexer (the 8-way key split's
     8-way key split) on one GPU: for each of R query rows, the global top-2048
     of 8 shards' local top-2048 (value, position) lists, lowest position first
     on ties, positions ascending."""
@@ -707,7 +713,7 @@ class DecodeLayerWorkload(Workload):
     histogram over the row's keys in the fp8 indexer-K cache, exact top-2048)
     and sparse MLA decode attention over the selected rows of the
     fp8_ds_mla latent cache; both caches share the block table, as the
-    reference's layer does. At B = 8 and 180k keys this is BASELINE config 5's
+    reference's layer does. At B = 8 and 180k keys this is the sharded layer's
     layer on one GPU."""
 
     metric = "DSA decode layer tok/s @128k ctx (indexer + top-2048 + sparse MLA)"

@@ -31,5 +31,7 @@ from .ops import (  # noqa: F401
     sm70_ipc_slot_wait,
     sm70_sparse_mla_decode,
 )
+from . import sparse_attn_indexer  # noqa: F401  (registers the sm70_sparse_indexer op)
+from .sparse_attn_indexer import sm70_sparse_indexer  # noqa: F401
 
 _sys.modules.setdefault("glm5_on_v100_b200", _sys.modules[__name__])

@@ -90,6 +90,38 @@ __device__ __forceinline__ uint4 bf16x8_to_half8(uint4 v) {
                     bf16x2_to_half2_bits(v.z), bf16x2_to_half2_bits(v.w));
 }
 
+// Largest |x| of eight bf16 values, as its 15-bit magnitude pattern (the
+// unsigned order of these patterns is the order of |x|).
+__device__ __forceinline__ uint32_t bf16x8_max_abs_bits(uint4 v) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+  uint32_t m = 0;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) m = max(m, max(w[i] & 0x7FFFu, (w[i] >> 16) & 0x7FFFu));
+  return m;
+}
+
+// Power-of-two shift qe such that x * 2^-qe puts the largest magnitude
+// (pattern `bits`) in [2^14, 2^15): inside fp16's normal range with room to
+// spare, whatever the bf16 exponent (small values are scaled up, so they do
+// not fall into fp16 subnormals). Clamped so 2^+-qe stays a normal float.
+__device__ __forceinline__ int bf16_fp16_shift(uint32_t bits) {
+  return min(114, max(-100, (int)((bits >> 7) & 0xFFu) - 141));
+}
+
+// bf16 pair x 2^-qe -> half2 bits (exact while the scaled values stay in the
+// half normal range; qe = 0 is a plain conversion).
+__device__ __forceinline__ uint32_t bf16x2_to_half2_scaled(uint32_t v, float mul) {
+  __nv_bfloat162 b = *reinterpret_cast<__nv_bfloat162*>(&v);
+  float2 f = __bfloat1622float2(b);
+  return pack_half2(f.x * mul, f.y * mul);
+}
+
+__device__ __forceinline__ uint4 bf16x8_to_half8_scaled(uint4 v, int qe) {
+  const float mul = __int_as_float((127 - qe) << 23);  // 2^-qe, exact
+  return make_uint4(bf16x2_to_half2_scaled(v.x, mul), bf16x2_to_half2_scaled(v.y, mul),
+                    bf16x2_to_half2_scaled(v.z, mul), bf16x2_to_half2_scaled(v.w, mul));
+}
+
 // --------------------------------------------------------- shared memory
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));

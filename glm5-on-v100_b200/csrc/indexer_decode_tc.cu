@@ -106,6 +106,7 @@ __global__ void __launch_bounds__(DNT, 2) indexer_decode_tc_kernel(const Indexer
   int64_t* sBase = reinterpret_cast<int64_t*>(sm + Lay::OFF_BASE);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + Lay::OFF_SLOT);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + Lay::OFF_SLOT + 4);
+  uint32_t* q_bits = reinterpret_cast<uint32_t*>(sm + Lay::OFF_SLOT + 8);  // largest |q| bf16 pattern
   const uint32_t mb0 = base + Lay::OFF_MBAR;        // copies of stage s at mb0 + 8 s
   const uint32_t mb_mma = mb0 + 8u * DSTAGES;      // MMAs of a sub-tile done
   const uint32_t mb_done = mb_mma + 8u;            // drain on abort
@@ -171,6 +172,22 @@ __global__ void __launch_bounds__(DNT, 2) indexer_decode_tc_kernel(const Indexer
     tmem_alloc(smem_u32(tmem_slot), Lay::TMEM_COLS);
   }
   for (int i = tid; i < NBIN; i += DNT) sHist[i] = 0;
+  // bf16 q beyond fp16's range: the row's q is scaled by 2^-qe for the MMA
+  // and every score by 2^qe after it (both exact; relu commutes with them)
+  int qe = 0;
+  if (a.q_bf16) {
+    if (tid == 0) *q_bits = 0;
+    __syncthreads();
+    uint32_t bits = 0;
+    for (int i = tid; i < a.n_ihead * 16; i += DNT)
+      bits = max(bits, bf16x8_max_abs_bits(*reinterpret_cast<const uint4*>(
+                           reinterpret_cast<const uint8_t*>(a.q) + ((int64_t)b * a.n_ihead * HD + 8 * i) * 2)));
+    bits = __reduce_max_sync(0xffffffffu, bits);
+    if (lane == 0) atomicMax(q_bits, bits);
+    __syncthreads();
+    qe = bf16_fp16_shift(*q_bits);
+  }
+  const float qmul = __int_as_float((127 + qe) << 23);  // 2^qe
   // q as the MMA's B operand: NQ rows (heads, zero past n_ihead) x 128 dims,
   // two 64-dim regions of 128-byte swizzled rows
   for (int i = tid; i < NQ * 16; i += DNT) {
@@ -179,7 +196,7 @@ __global__ void __launch_bounds__(DNT, 2) indexer_decode_tc_kernel(const Indexer
     if (h < a.n_ihead) {
       v = *reinterpret_cast<const uint4*>(reinterpret_cast<const uint8_t*>(a.q) +
                                           (((int64_t)b * a.n_ihead + h) * HD + 8 * c) * 2);
-      if (a.q_bf16) v = bf16x8_to_half8(v);
+      if (a.q_bf16) v = bf16x8_to_half8_scaled(v, qe);
     }
     *reinterpret_cast<uint4*>(sm + Lay::OFF_Q + (c >> 3) * Lay::Q_REGION + sw128_off(h, c & 7)) = v;
   }
@@ -277,7 +294,7 @@ __global__ void __launch_bounds__(DNT, 2) indexer_decode_tc_kernel(const Indexer
     if (half == 0) {
       const int pos = k0 + key;
       if (pos < v_end) {
-        const float v = (s + sPart[key]) * sScale[key];
+        const float v = (s + sPart[key]) * sScale[key] * qmul;
         atomicAdd(&sHist[monotone32(v) >> 20], 1u);
         score_row[pos] = v;
       }

@@ -293,11 +293,12 @@ __global__ void __launch_bounds__(NTHREADS, 1) sparse_mla_decode_tc_kernel(const
   int* table = reinterpret_cast<int*>(sm + SM_TABLE);
   uint8_t* misc = sm + SM_MISC;
   // misc: [0, 80) 10 mbarriers | 80 TMEM base | 84 abort | 88 any_rescale |
-  // [96, 160) ovf | [160, 288) s_valid | [288, 1824) per-head floats
+  // 92 q_bits | [96, 160) ovf | [160, 288) s_valid | [288, 1824) per-head floats
   uint64_t* mbar = reinterpret_cast<uint64_t*>(misc);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(misc + 80);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(misc + 84);
   int* any_rescale = reinterpret_cast<int*>(misc + 88);
+  uint32_t* q_bits = reinterpret_cast<uint32_t*>(misc + 92);  // largest |q| bf16 bit pattern of this CTA
   int* ovf = reinterpret_cast<int*>(misc + 96);           // [2 parities][8 softmax warps] overflow votes
   uint8_t* s_valid = misc + 160;                          // [2 buffers][64 rows] row counted
   float* m_ref = reinterpret_cast<float*>(misc + 288);    // [64] running max (log2 units)
@@ -367,12 +368,27 @@ __global__ void __launch_bounds__(NTHREADS, 1) sparse_mla_decode_tc_kernel(const
     for (int i = tid; i < nheads * 72; i += kQThreads) cp_async16(smem_u32(qraw + 16 * i), qg + 16 * i);
     cp_async_commit();
     cp_async_wait<0>();
+    // bf16 q may exceed the fp16 range of the MMA operand: this CTA's Q is
+    // then scaled by 2^-qe and the softmax scale by 2^qe (both exact), so
+    // every score * scale is unchanged
+    int qe = 0;
+    if (p.q_bf16) {
+      uint32_t bits = 0;
+      for (int i = tid; i < nheads * 72; i += kQThreads)
+        bits = max(bits, bf16x8_max_abs_bits(*reinterpret_cast<const uint4*>(qraw + 16 * i)));
+      bits = __reduce_max_sync(0xffffffffu, bits);
+      if (tid == 0) *q_bits = 0;
+      named_bar(3, kQThreads);
+      if (lane == 0) atomicMax(q_bits, bits);
+      named_bar(3, kQThreads);
+      qe = bf16_fp16_shift(*q_bits);
+    }
     for (int i = tid; i < NH * 72; i += kQThreads) {
       const int h = i / 72, c = i % 72;
       uint4 v = make_uint4(0, 0, 0, 0);
       if (h < nheads) {
         v = *reinterpret_cast<const uint4*>(qraw + 16 * i);
-        if (p.q_bf16) v = bf16x8_to_half8(v);
+        if (p.q_bf16) v = bf16x8_to_half8_scaled(v, qe);
       }
       *reinterpret_cast<uint4*>(sm + SM_Q + (c >> 3) * Q_REGION + sw128_off(h, c & 7)) = v;
     }
@@ -386,6 +402,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) sparse_mla_decode_tc_kernel(const
   __syncthreads();
   fence_after_sync();
   const uint32_t tmem = *tmem_slot;
+  // softmax scale in log2 units, times 2^qe when this CTA's bf16 Q was scaled down
+  const float scale_log2 = p.q_bf16 ? p.scale_log2 * exp2f((float)bf16_fp16_shift(*q_bits)) : p.scale_log2;
   // Base descriptors; a start-address advance of X bytes adds X >> 4.
   const uint64_t desc_kv = sw128_desc(base + SM_KV, 16, 1024);                       // tile buffer 0, K-major
   const uint64_t desc_q = sw128_desc(base + SM_Q, 16, 1024);                         // Q, K-major
@@ -550,7 +568,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) sparse_mla_decode_tc_kernel(const
       bool over = false;
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
-        const float v = (vrow ? __uint_as_float(s[i]) * p.scale_log2 : -INFINITY) - m_ref[hbase + 2 * i];
+        const float v = (vrow ? __uint_as_float(s[i]) * scale_log2 : -INFINITY) - m_ref[hbase + 2 * i];
         s[i] = __float_as_uint(v);
         over |= v > kRescaleThreshold;
       }
@@ -569,7 +587,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) sparse_mla_decode_tc_kernel(const
         }
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-          const float v = vrow ? __uint_as_float(s[i]) * p.scale_log2 : -INFINITY;
+          const float v = vrow ? __uint_as_float(s[i]) * scale_log2 : -INFINITY;
           s[i] = __float_as_uint(v);
           uint32_t m = monotone32(v);
           m = max(m, __shfl_xor_sync(0xffffffffu, m, 1));

@@ -23,6 +23,7 @@ Differences from the reference, by design:
 """
 from __future__ import annotations
 
+import contextlib
 import ctypes
 import logging
 from dataclasses import dataclass, field
@@ -460,3 +461,61 @@ def _prefill_chunk(chunk: PrefillChunk, kv_cache, q, weights, topk_tokens, topk_
     if pending:
         merge_shards(pending, topk_indices_buffer, topk_tokens, shard)
     return (tok_lo, n_q, ke)
+
+
+# -------------------------------------------------- the layer's custom op
+# vLLM's forward context stand-in: the per-step indexer metadata of every
+# layer, keyed by the layer's k-cache prefix, plus the layer group's key
+# sharding (the reference reads get_forward_context().attn_metadata,
+# sai.py:541-546).
+_FORWARD: dict = {"attn_metadata": None, "shard": None}
+
+
+@contextlib.contextmanager
+def forward_context(attn_metadata: Optional[dict], shard: Optional[ShardConfig] = None):
+    """Makes `attn_metadata` ({k_cache_prefix: IndexerMeta}) and `shard` the
+    state that ``sm70_sparse_indexer`` reads for the duration of a step."""
+    old = dict(_FORWARD)
+    _FORWARD.update(attn_metadata=attn_metadata, shard=shard)
+    try:
+        yield
+    finally:
+        _FORWARD.update(old)
+
+
+def _sm70_sparse_indexer_impl(k_cache_prefix: str, kv_cache: torch.Tensor, q: torch.Tensor, k: torch.Tensor,
+                              weights: torch.Tensor, topk_tokens: int, head_dim: int, max_model_len: int,
+                              topk_indices_buffer: torch.Tensor) -> torch.Tensor:
+    """Body of the vllm::sm70_sparse_indexer custom op (sai.py:528-1071): a
+    profiling / dummy run without metadata returns the buffer untouched
+    (sai.py:543-544); otherwise the layer's metadata drives sparse_indexer."""
+    md = _FORWARD["attn_metadata"]
+    if not isinstance(md, dict):
+        return topk_indices_buffer
+    if k.shape[-1] != head_dim:
+        raise RuntimeError(f"sm70_sparse_indexer: k head dim {k.shape[-1]} != head_dim {head_dim}")
+    sparse_indexer(md[k_cache_prefix], kv_cache, q, k, weights, topk_tokens, topk_indices_buffer,
+                   shard=_FORWARD["shard"])
+    return topk_indices_buffer
+
+
+def _sm70_sparse_indexer_fake(k_cache_prefix, kv_cache, q, k, weights, topk_tokens, head_dim, max_model_len,
+                              topk_indices_buffer):
+    return topk_indices_buffer
+
+
+# schema of the reference's registration (direct_register_custom_op with
+# mutates_args=["topk_indices_buffer"], sai.py:1089-1095)
+ops._lib_def.define("sm70_sparse_indexer(str k_cache_prefix, Tensor kv_cache, Tensor q, Tensor k, Tensor weights, "
+                    "int topk_tokens, int head_dim, int max_model_len, Tensor(a!) topk_indices_buffer) -> Tensor(a!)")
+ops._lib_def.impl("sm70_sparse_indexer", _sm70_sparse_indexer_impl, "CUDA")
+torch.library.register_fake(f"{ops.NAMESPACE}::sm70_sparse_indexer")(_sm70_sparse_indexer_fake)
+
+
+def sm70_sparse_indexer(k_cache_prefix: str, kv_cache: torch.Tensor, q: torch.Tensor, k: torch.Tensor,
+                        weights: torch.Tensor, topk_tokens: int, head_dim: int, max_model_len: int,
+                        topk_indices_buffer: torch.Tensor) -> torch.Tensor:
+    """The reference's Python entry (sai.py:1098-1119), dispatching through
+    the registered op."""
+    return getattr(torch.ops, ops.NAMESPACE).sm70_sparse_indexer(k_cache_prefix, kv_cache, q, k, weights, topk_tokens,
+                                                                 head_dim, max_model_len, topk_indices_buffer)

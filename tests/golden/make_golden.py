@@ -15,7 +15,7 @@ digest of the regenerated inputs and the reference outputs:
   * varlen_prefill.npz — _varlen_attention (vllm/v1/attention/backends/mla/
     prefill/sm70_triton.py:54-187), dense causal prefill; the sparse kernel with
     every causal position selected must equal it (the reference's own gate,
-    docs/INTEGRATION.md:124-128).
+    the reference's docs/INTEGRATION.md:124-128).
   * shard_merge.npz — the torch.topk shard-merge epilogue
     (reference/sparse_attn_indexer.py:1007-1030), executed from the reference
     source text on a seeded all-gather payload with ties and -inf entries.
@@ -138,7 +138,7 @@ def main():
     tmla = _load("ref_triton_mla", os.path.join(ref, "reference/triton_mla.py"))
     st = _load("ref_sm70_triton",
                os.path.join(ref, "vllm/v1/attention/backends/mla/prefill/sm70_triton.py"))
-    # B=1, 16 heads, 2,048 cached tokens, top-k 512, scale 1/sqrt(192)
+    # the CPU-runnable decode case: B=1, 16 heads, 2,048 cached tokens, top-k 512, scale 1/sqrt(192)
     mqa_decode_fixture(tmla, "config1", seed=1, B=1, H=16, page=64,
                        seq_lens=[2048], topk=512, bps=32, scale=1.0 / np.sqrt(192.0))
     # ragged batch: short rows (seq_len < topk, -1 padding), long rows, odd head count

@@ -106,3 +106,20 @@ def test_torch_ops_registered_with_reference_schemas(dsa):
                  "sm70_indexer_shard_merge_p2p", "sm70_ipc_alloc", "sm70_ipc_open", "sm70_ipc_flag_set",
                  "sm70_ipc_slot_wait", "persistent_topk"]:
         assert hasattr(ns, name), name
+    # the layer op: reference signature with topk_indices_buffer mutated (sai.py:1089-1119)
+    assert args(ns.sm70_sparse_indexer) == [("k_cache_prefix", False), ("kv_cache", False), ("q", False),
+                                            ("k", False), ("weights", False), ("topk_tokens", False),
+                                            ("head_dim", False), ("max_model_len", False),
+                                            ("topk_indices_buffer", True)]
+
+
+def test_sparse_indexer_op_without_metadata_returns_buffer(dsa):
+    """A profiling / dummy run (no forward-context metadata) leaves the buffer
+    untouched and returns it, as the reference does (sai.py:543-544)."""
+    import torch
+
+    sai = dsa.sparse_attn_indexer
+    buf = torch.full((3, 4), 5, dtype=torch.int32)
+    out = sai._sm70_sparse_indexer_impl("layers.0.k_cache", torch.empty(0), torch.empty(0), torch.empty(3, 128),
+                                        torch.empty(0), 4, 128, 1024, buf)
+    assert out is buf and int(buf.sum()) == 60
