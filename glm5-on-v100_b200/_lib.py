@@ -66,6 +66,9 @@ SIGNATURES = {
     "dsa_topk_rows_payload": (_i, [_p, _i64, _p, _i64, _i, _p, _p, _i, _i, _i, _p]),
     "dsa_shard_exchange_topk": (_i, [_p, _i64, _i, _p, _p, _i, _i, _i, _p, _i64, _p, _i, _i, _p, _i64, _p, _p]),
     "dsa_shard_exchange_merge": (_i, [_p, _i64, _p, _p, _i, _i, _i, _i, _i64, _p, _i64, _p, _p]),
+    "dsa_concat_and_cache_ds_mla": (_i, [_p, _i64, _p, _i64, _p, _i64, _i, _p, _i, _p, _p, _i64, _i, _p]),
+    "dsa_indexer_qk_store": (_i, [_p, _i, _p, _i, _p, _i, _i64, _p, _i64, _p, _i64, _i, _p, _p, ctypes.c_float, _p,
+                                  _p, _i64, _i, ctypes.c_float, _p, _i, _i, _p]),
 }
 
 

@@ -378,6 +378,63 @@ def _ipc_slot_wait_impl(flag_ptrs, tp, min_seq):
            _vp(p2p_error_flag(dev)), _stream(dev))
 
 
+def _rope_args(positions, cos_sin_cache):
+    if positions is None:
+        return None, None, 0
+    _check(positions.dtype == torch.int64 and positions.is_contiguous(), "positions must be contiguous int64")
+    _check(cos_sin_cache is not None and cos_sin_cache.dtype == torch.float32 and cos_sin_cache.is_contiguous() and
+           cos_sin_cache.dim() == 2 and cos_sin_cache.size(1) == 64,
+           "cos_sin_cache must be contiguous f32 [max_pos, 64] (32 cos | 32 sin)")
+    return _vp(positions), _vp(cos_sin_cache), cos_sin_cache.size(0)
+
+
+def _concat_and_cache_ds_mla_impl(kv_c, k_pe, kv_cache, slot_mapping, positions, cos_sin_cache, is_neox):
+    _check(kv_c.dtype in (torch.float16, torch.bfloat16) and k_pe.dtype == kv_c.dtype,
+           "kv_c and k_pe must be fp16 or bf16, the same dtype")
+    _check(kv_c.dim() == 2 and kv_c.size(1) == 512 and kv_c.stride(1) == 1, "kv_c must be [T, 512], unit inner stride")
+    k_pe = k_pe.reshape(k_pe.size(0), -1)
+    _check(k_pe.size(1) == 64 and k_pe.stride(1) == 1, "k_pe must be [T, 64] (or [T, 1, 64])")
+    _check(kv_cache.dtype == torch.uint8 and kv_cache.size(-1) == DSMLA_ROW_BYTES and kv_cache.is_contiguous(),
+           "kv_cache must be contiguous uint8 fp8_ds_mla [n_blocks, page, 656]")
+    _int32(slot_mapping, "slot_mapping")
+    n = kv_c.size(0)
+    if n == 0:
+        return
+    pp, cp, max_pos = _rope_args(positions, cos_sin_cache)
+    with torch.cuda.device(kv_c.device):
+        L.call("dsa_concat_and_cache_ds_mla", _vp(kv_cache), kv_cache.numel() // DSMLA_ROW_BYTES, _vp(kv_c),
+               kv_c.stride(0), _vp(k_pe), k_pe.stride(0), _DTYPE[kv_c.dtype], _vp(slot_mapping.contiguous()), n, pp, cp,
+               max_pos, int(bool(is_neox)), _stream(kv_c.device))
+
+
+def _indexer_qk_store_impl(q_out, weights_out, kv_cache, q, kw, slot_mapping, ln_weight, ln_bias, ln_eps, positions,
+                           cos_sin_cache, is_neox, weight_scale):
+    _check(q.dtype in (torch.float16, torch.bfloat16) and kw.dtype == q.dtype, "q and kw must be fp16 or bf16, same dtype")
+    _check(q.dim() == 3 and q.size(2) == 128 and q.stride(2) == 1 and q.stride(1) == 128,
+           "q must be [T, n_head, 128] with contiguous heads")
+    T, H = q.size(0), q.size(1)
+    _check(kw.dim() == 2 and kw.size(0) == T and kw.size(1) == 128 + H and kw.stride(1) == 1,
+           "kw must be [T, 128 + n_head] (k then weight logits)")
+    _check(q_out.dtype in (torch.float16, torch.bfloat16) and q_out.is_contiguous() and tuple(q_out.shape) == (T, H, 128),
+           "q_out must be contiguous fp16/bf16 [T, n_head, 128]")
+    _check(weights_out.dtype in _DTYPE and weights_out.is_contiguous() and tuple(weights_out.shape) == (T, H),
+           "weights_out must be contiguous [T, n_head]")
+    fmt, row = _k_cache_format(kv_cache)
+    _check(kv_cache.is_contiguous(), "kv_cache must be contiguous")
+    _int32(slot_mapping, "slot_mapping")
+    for t, name in ((ln_weight, "ln_weight"), (ln_bias, "ln_bias")):
+        _check(t is None or (t.dtype == torch.float32 and t.is_contiguous() and t.numel() == 128),
+               f"{name} must be f32 [128]")
+    if T == 0:
+        return
+    pp, cp, max_pos = _rope_args(positions, cos_sin_cache)
+    with torch.cuda.device(q.device):
+        L.call("dsa_indexer_qk_store", _vp(q_out), _DTYPE[q_out.dtype], _vp(weights_out), _DTYPE[weights_out.dtype],
+               _vp(kv_cache), fmt, kv_cache.numel() // row, _vp(q), q.stride(0), _vp(kw), kw.stride(0),
+               _DTYPE[q.dtype], _vp(ln_weight), _vp(ln_bias), float(ln_eps), pp, cp, max_pos, int(bool(is_neox)),
+               float(weight_scale), _vp(slot_mapping.contiguous()), T, H, _stream(q.device))
+
+
 # ------------------------------------------------------ torch registration
 _lib_def = torch.library.Library(NAMESPACE, "DEF")
 _SCHEMAS = {
@@ -405,6 +462,15 @@ _SCHEMAS = {
     "sm70_ipc_flag_set": ("(int flag_ptr, int which, int seq) -> ()", _ipc_flag_set_impl,
                           "CompositeExplicitAutograd"),
     "sm70_ipc_slot_wait": ("(Tensor flag_ptrs, int tp, int min_seq) -> ()", _ipc_slot_wait_impl, "CPU"),
+    # cache writers (no SM70 op in the reference: the upstream writer and the
+    # indexer's torch producer, with the rotary embedding fused in)
+    "concat_and_cache_ds_mla": ("(Tensor kv_c, Tensor k_pe, Tensor! kv_cache, Tensor slot_mapping, "
+                                "Tensor? positions, Tensor? cos_sin_cache, bool is_neox) -> ()",
+                                _concat_and_cache_ds_mla_impl, "CUDA"),
+    "indexer_qk_store": ("(Tensor! q_out, Tensor! weights_out, Tensor! kv_cache, Tensor q, Tensor kw, "
+                         "Tensor slot_mapping, Tensor? ln_weight, Tensor? ln_bias, float ln_eps, Tensor? positions, "
+                         "Tensor? cos_sin_cache, bool is_neox, float weight_scale) -> ()",
+                         _indexer_qk_store_impl, "CUDA"),
 }
 for _name, (_schema, _fn, _key) in _SCHEMAS.items():
     _lib_def.define(_name + _schema)
@@ -417,7 +483,7 @@ def _noop_fake(*args, **kwargs):
 
 for _name in ("sm70_sparse_mla_decode", "sm70_indexer_logits", "sm70_indexer_logits_packed", "sm70_decode_topk",
               "persistent_topk", "sm70_indexer_k_store", "sm70_indexer_shard_merge",
-              "sm70_indexer_shard_merge_p2p"):
+              "sm70_indexer_shard_merge_p2p", "concat_and_cache_ds_mla", "indexer_qk_store"):
     torch.library.register_fake(f"{NAMESPACE}::{_name}")(_noop_fake)
 
 
@@ -480,3 +546,23 @@ def sm70_ipc_flag_set(flag_ptr: int, which: int, seq: int) -> None:
 
 def sm70_ipc_slot_wait(flag_ptrs, tp: int, min_seq: int) -> None:
     _op("sm70_ipc_slot_wait")(flag_ptrs, tp, min_seq)
+
+
+def concat_and_cache_mla(kv_c, k_pe, kv_cache, slot_mapping, kv_cache_dtype: str = "fp8_ds_mla", scale=None,
+                         positions=None, cos_sin_cache=None, is_neox: bool = False) -> None:
+    """Latent-cache writer with the upstream signature (concat_and_cache_mla,
+    kv_cache_dtype "fp8_ds_mla"; scale is unused by that format). Given
+    positions and a cos/sin table, the rotary embedding of k_pe is applied
+    on the way in (k_pe is then the un-rotated key)."""
+    _check(kv_cache_dtype == "fp8_ds_mla", f"only the fp8_ds_mla cache is written here (got {kv_cache_dtype})")
+    _op("concat_and_cache_ds_mla")(kv_c, k_pe, kv_cache, slot_mapping, positions, cos_sin_cache, is_neox)
+
+
+def indexer_qk_store(q_out, weights_out, kv_cache, q, kw, slot_mapping, ln_weight=None, ln_bias=None,
+                     ln_eps: float = 1e-6, positions=None, cos_sin_cache=None, is_neox: bool = False,
+                     weight_scale: float = 1.0) -> None:
+    """The indexer's q / k / weights producer fused into the K store: k =
+    LayerNorm(kw[:, :128]) + rotary into the cache rows, q_out = rotary(q),
+    weights_out = kw[:, 128:] * weight_scale."""
+    _op("indexer_qk_store")(q_out, weights_out, kv_cache, q, kw, slot_mapping, ln_weight, ln_bias, float(ln_eps),
+                            positions, cos_sin_cache, is_neox, float(weight_scale))

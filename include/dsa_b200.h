@@ -226,6 +226,57 @@ int dsa_indexer_k_store(void* kv_cache, int cache_format, int64_t n_rows,
                         const int32_t* slot, int n_tok, void* stream);
 
 /* =====================================================================
+ * Cache writers.
+ *
+ * dsa_concat_and_cache_ds_mla: the fp8_ds_mla latent-cache writer, the
+ * upstream concat_and_cache_mla with kv_cache_dtype "fp8_ds_mla" that the
+ * reference patches (full.patch:3183-3242; row layout dsa.cu:74-100), with
+ * the rotary embedding of k_pe fused in. For t < n_tok with
+ * 0 <= slot[t] < n_rows, cache row slot[t] (656 B) =
+ *   e4m3(kv_c[t, 128j + i] / s_j)  for the four 128-wide tiles j
+ *     (round to nearest even, saturating), s_j = max(amax_j / 448, FLT_MIN)
+ *   | s_0..s_3 as f32
+ *   | fp16 of rope(k_pe[t], positions[t]) (64 values).
+ * Rows with slot < 0 or >= n_rows are skipped. kv_c [n_tok, >= 512] and
+ * k_pe [n_tok, >= 64] in in_dtype (f16 or bf16), row strides in elements;
+ * kv_c rows 16-byte aligned. positions (int64, may be NULL for no rotation)
+ * index cos_sin [max_pos, 64] f32 = 32 cos | 32 sin (vLLM's cos_sin_cache);
+ * rope_neox selects pairs (i, i + 32) instead of (2i, 2i + 1). The
+ * rotation is computed in f32 without fused multiply-adds.
+ * ===================================================================== */
+int dsa_concat_and_cache_ds_mla(void* kv_cache, int64_t n_rows,
+                                const void* kv_c, int64_t kv_c_stride,
+                                const void* k_pe, int64_t k_pe_stride,
+                                int in_dtype, const int32_t* slot, int n_tok,
+                                const int64_t* positions, const float* cos_sin,
+                                int64_t max_pos, int rope_neox, void* stream);
+
+/* dsa_indexer_qk_store: the lightning indexer's q / k / weights producer
+ * (the post-GEMM part of Indexer.forward's SM70 branch,
+ * full.patch:6404-6425) fused into the indexer-K store (dsa.cu:662-706).
+ * Per token t (kw = [k | weight logits], [n_tok, 128 + n_head]):
+ *   k = LayerNorm(kw[t, :128]; ln_weight, ln_bias, ln_eps) (NULL weight /
+ *       bias = 1 / 0), rotated on dims [0, 64), written to cache row slot[t]
+ *       as cache_format (f16, bf16, or DSA_FP8_IDXK with the K store's
+ *       quantisation) unless slot[t] < 0 or >= n_rows;
+ *   q_out[t, h] = q[t, h] rotated on dims [0, 64) (q [n_tok, n_head, 128],
+ *       token stride q_stride elements), in q_out_dtype (f16 / bf16);
+ *   w_out[t, h] = kw[t, 128 + h] * w_scale (the reference's
+ *       softmax_scale * n_head^-0.5), in w_out_dtype (f16 / bf16 / f32).
+ * Rotary pairs and cos_sin as for dsa_concat_and_cache_ds_mla. All
+ * arithmetic in f32, each output rounded once. n_head in [1, 256].
+ * ===================================================================== */
+int dsa_indexer_qk_store(void* q_out, int q_out_dtype, void* w_out,
+                         int w_out_dtype, void* k_cache, int cache_format,
+                         int64_t n_rows, const void* q, int64_t q_stride,
+                         const void* kw, int64_t kw_stride, int in_dtype,
+                         const float* ln_weight, const float* ln_bias,
+                         float ln_eps, const int64_t* positions,
+                         const float* cos_sin, int64_t max_pos, int rope_neox,
+                         float w_scale, const int32_t* slot, int n_tok,
+                         int n_head, void* stream);
+
+/* =====================================================================
  * Exact shard merge of key-sharded indexer top-k candidates.
  * Replaces sm70_indexer_shard_merge (dsa.cu:2411-2434, kernel :2054-2182;
  * schema binds "sm70_indexer_shard_merge(Tensor! out, Tensor allf, Tensor

@@ -393,3 +393,68 @@ def sharded_local_candidates(score_full: np.ndarray, lens: np.ndarray, K: int,
     vals[neg] = -np.inf
     gidx = np.where(neg, loc_idx, loc_idx + off).astype(np.int32)
     return vals.astype(np.float32), gidx
+
+
+# ---------------------------------------------------------------------------
+# Cache writers: the fp8_ds_mla latent writer (upstream concat_and_cache_mla,
+# amax fix full.patch:3209-3230, row dsa.cu:74-100) and the indexer's
+# q / k / weights producer (full.patch:6404-6425) with the K store.
+# ---------------------------------------------------------------------------
+def rope_f32(x: np.ndarray, pos: np.ndarray, cos_sin: np.ndarray, neox: bool) -> np.ndarray:
+    """Rotary embedding of the first 64 dims of x [n, >=64] at positions pos,
+    cos_sin [max_pos, 64] = 32 cos | 32 sin (vLLM's RotaryEmbedding: NeoX
+    pairs (i, i+32) or GPT-J pairs (2i, 2i+1)); every product and sum is
+    rounded in f32, as the writer kernels compute it."""
+    x = np.array(x, dtype=np.float32, copy=True)
+    p = np.clip(np.asarray(pos, dtype=np.int64), 0, cos_sin.shape[0] - 1)
+    c = cos_sin[p, :32].astype(np.float32)
+    s = cos_sin[p, 32:64].astype(np.float32)
+    i1, i2 = (np.arange(32), np.arange(32) + 32) if neox else (np.arange(0, 64, 2), np.arange(1, 64, 2))
+    x1, x2 = x[:, i1], x[:, i2]
+    x[:, i1] = (x1 * c).astype(np.float32) - (x2 * s).astype(np.float32)
+    x[:, i2] = (x2 * c).astype(np.float32) + (x1 * s).astype(np.float32)
+    return x
+
+
+def dsmla_write_rows(kv_c, k_pe, pos=None, cos_sin=None, neox=False) -> np.ndarray:
+    """Rows the latent writer stores for kv_c [n, 512] and k_pe [n, 64]
+    (rotated first when pos is given): the per-tile encoding of
+    dsmla_encode_rows over [kv_c | rope(k_pe)]."""
+    kv = np.asarray(kv_c, dtype=np.float32)
+    kp = np.asarray(k_pe, dtype=np.float32).reshape(kv.shape[0], 64)
+    if pos is not None:
+        kp = rope_f32(kp, pos, cos_sin, neox)
+    return dsmla_encode_rows(np.concatenate([kv, kp], axis=1))
+
+
+def indexer_qk_produce(q, kw, ln_w, ln_b, eps, pos, cos_sin, neox, w_scale):
+    """(q_out [T, H, 128], k [T, 128], weights [T, H]) of the indexer's producer
+    in float64: k = LayerNorm(kw[:, :128]) (biased variance, eps inside the
+    root), rotary on dims [0, 64) of k and of every q head, weights =
+    kw[:, 128:] * w_scale (full.patch:6406-6425)."""
+    q = np.asarray(q, dtype=np.float64)
+    kw = np.asarray(kw, dtype=np.float64)
+    T, H, _ = q.shape
+    k = kw[:, :128]
+    mu = k.mean(axis=1, keepdims=True)
+    var = ((k - mu) ** 2).mean(axis=1, keepdims=True)
+    k = (k - mu) / np.sqrt(var + eps)
+    if ln_w is not None:
+        k = k * np.asarray(ln_w, dtype=np.float64)
+    if ln_b is not None:
+        k = k + np.asarray(ln_b, dtype=np.float64)
+    qo = q.copy()
+    if pos is not None:
+        p = np.clip(np.asarray(pos, dtype=np.int64), 0, cos_sin.shape[0] - 1)
+        c = np.asarray(cos_sin, dtype=np.float64)[p, :32]
+        s = np.asarray(cos_sin, dtype=np.float64)[p, 32:64]
+        i1, i2 = (np.arange(32), np.arange(32) + 32) if neox else (np.arange(0, 64, 2), np.arange(1, 64, 2))
+
+        def rot(x, c, s):
+            x1, x2 = x[..., i1].copy(), x[..., i2].copy()
+            x[..., i1] = x1 * c - x2 * s
+            x[..., i2] = x2 * c + x1 * s
+
+        rot(k, c, s)
+        rot(qo, c[:, None, :], s[:, None, :])
+    return qo, k, kw[:, 128:] * w_scale

@@ -126,3 +126,25 @@ def test_global_topk_subset_of_shard_union():
         payload.append(np.concatenate([v, g.view(np.float32)], axis=1))
     merged = O.shard_merge(np.stack(payload), K)
     np.testing.assert_array_equal(np.sort(full, axis=1), merged)
+
+
+def test_rope_oracle_matches_vllm_rotary_embedding():
+    """The writers' rotary embedding (oracle.rope_f32) equals vLLM's own
+    PyTorch implementation (RotaryEmbedding.forward_static, the rotary the
+    reference's model code calls) bit for bit in f32, in both pair orders."""
+    import torch
+
+    try:
+        from vllm.model_executor.layers.rotary_embedding.base import RotaryEmbedding
+    except Exception as e:  # pragma: no cover - vLLM is part of this image
+        pytest.skip(f"vLLM rotary embedding not importable: {e}")
+    rng = np.random.default_rng(4)
+    inv = 1.0 / 10000.0 ** (np.arange(0, 64, 2, dtype=np.float64) / 64)
+    f = np.outer(np.arange(1024, dtype=np.float64), inv)
+    cs = np.concatenate([np.cos(f), np.sin(f)], axis=1).astype(np.float32)
+    x = rng.standard_normal((17, 64)).astype(np.float32)
+    pos = rng.integers(0, 1024, size=17)
+    for neox in (True, False):
+        _, k = RotaryEmbedding.forward_static(torch.from_numpy(pos), torch.zeros(17, 64),
+                                              torch.from_numpy(x.copy()), 64, 64, torch.from_numpy(cs), neox)
+        np.testing.assert_array_equal(O.rope_f32(x, pos, cs, neox), k.numpy())
