@@ -62,6 +62,21 @@ __device__ __forceinline__ void e4m3x4_to_half2x2(uint32_t v, __half2& lo, __hal
   hi = *reinterpret_cast<__half2*>(&r1);
 }
 
+// Four e4m3 bytes -> two half2 words holding value / 256 each, exactly, with
+// integer operations only (no conversion-pipe instructions): each byte goes to
+// a 16-bit lane with its sign replicated above it (prmt sign-extension
+// selectors), and a shift puts exponent + mantissa in fp16 bits 7..13 and the
+// sign on bit 15 (bit 14 cleared). e4m3's exponent bias (7) vs fp16's (15) is
+// the 2^-8 factor; e4m3 subnormals become fp16 subnormals. lo holds bytes 0, 1
+// and hi bytes 2, 3.
+__device__ __forceinline__ void e4m3x4_to_half2x2_div256(uint32_t w, uint32_t& lo, uint32_t& hi) {
+  uint32_t a, b;
+  asm("prmt.b32 %0, %1, 0, 0x9180;" : "=r"(a) : "r"(w));
+  asm("prmt.b32 %0, %1, 0, 0xB3A2;" : "=r"(b) : "r"(w));
+  lo = (a << 7) & 0xBF80BF80u;
+  hi = (b << 7) & 0xBF80BF80u;
+}
+
 // Two floats -> two e4m3 bytes (round-to-nearest-even, saturating to +-448).
 __device__ __forceinline__ uint16_t f32x2_to_e4m3x2(float a, float b) {
   return (uint16_t)__nv_cvt_float2_to_fp8x2(make_float2(a, b), __NV_SATFINITE, __NV_E4M3);

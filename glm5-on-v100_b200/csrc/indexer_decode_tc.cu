@@ -70,11 +70,6 @@ __device__ __forceinline__ float load_weight(const IndexerDecodeTcArgs& a, int64
   return __half2float(reinterpret_cast<const __half*>(a.w)[i]);
 }
 
-__device__ __forceinline__ uint32_t e4m3x2_to_half2(uint32_t two_bytes) {
-  const __half2_raw r = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)two_bytes, __NV_E4M3);
-  return *reinterpret_cast<const uint32_t*>(&r);
-}
-
 // NQ/2 consecutive TMEM columns of this thread's lane.
 template <int N>
 __device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, uint32_t (&r)[N]) {
@@ -250,14 +245,13 @@ __global__ void __launch_bounds__(DNT, 2) indexer_decode_tc_kernel(const Indexer
       uint32_t hv[8];
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        hv[2 * e] = e4m3x2_to_half2(w[e] & 0xFFFFu);
-        hv[2 * e + 1] = e4m3x2_to_half2(w[e] >> 16);
+        e4m3x4_to_half2x2_div256(w[e], hv[2 * e], hv[2 * e + 1]);  // keys / 256, exact
       }
       uint8_t* region = ktile + (c16 >> 2) * KT_REGION;
       *reinterpret_cast<uint4*>(region + sw128_off(key, 2 * (c16 & 3))) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
       *reinterpret_cast<uint4*>(region + sw128_off(key, 2 * (c16 & 3) + 1)) =
           make_uint4(hv[4], hv[5], hv[6], hv[7]);
-      if (c16 == 0) sScale[key] = sc;
+      if (c16 == 0) sScale[key] = sc * 256.0f;  // the keys' 1/256 undone with their scale
     }
     fence_proxy_async();
     fence_before_sync();

@@ -24,7 +24,11 @@
 //      order, and the two ascending lists merged into the output.
 // When bin T1 holds more keys than the candidate buffer, the row is resolved
 // by radix levels over global memory and an ordered block-wide compaction.
+#include <cooperative_groups.h>
+
 #include "common.cuh"
+
+namespace cg = cooperative_groups;
 
 namespace dsa {
 namespace {
@@ -95,6 +99,8 @@ struct TopkSmem {
   int T;
   uint32_t above, total;
   int ok;
+  uint32_t cl_cnt[8];  // cluster mode: every CTA's (sure | candidates << 16) counts
+  uint32_t cl_nsel;    // cluster mode (rank 0): selected candidates
 };
 
 // Block-wide: find the largest bin T with count(bins >= T) >= need, scanning
@@ -251,6 +257,59 @@ __device__ void select_global(const float* row, int n, int K, uint32_t T1, uint3
   }
 }
 
+// The K-th key among the n_cand candidates of level-1 bin T1 (held in
+// position order in s.cand_key / s.cand_pos): two more radix levels (12 + 8
+// bits), then the selected candidates (key > kth, or == kth among the first
+// such keys) compacted in position order into s.sel. Returns their count.
+template <int NT>
+__device__ uint32_t resolve_candidates(TopkSmem& s, uint32_t n_cand, uint32_t need2, uint32_t T1) {
+  const int tid = threadIdx.x;
+  for (int i = tid; i < NBIN1; i += NT) s.hist[i] = 0;
+  __syncthreads();
+  for (int i = tid; i < (int)n_cand; i += NT) atomicAdd(&s.hist[(s.cand_key[i] >> 8) & 0xFFFu], 1u);
+  __syncthreads();
+  find_threshold<NT>(s.hist, NBIN1, need2, s.warp, &s.T, &s.above);
+  const uint32_t T2 = (uint32_t)s.T;
+  const uint32_t need3 = need2 - s.above;
+  __syncthreads();
+  for (int i = tid; i < 256; i += NT) s.hist[i] = 0;
+  __syncthreads();
+  for (int i = tid; i < (int)n_cand; i += NT) {
+    const uint32_t key = s.cand_key[i];
+    if (((key >> 8) & 0xFFFu) == T2) atomicAdd(&s.hist[key & 0xFFu], 1u);
+  }
+  __syncthreads();
+  find_threshold<NT>(s.hist, 256, need3, s.warp, &s.T, &s.above);
+  const uint32_t kth = (T1 << 20) | (T2 << 8) | (uint32_t)s.T;
+  const uint32_t n_ties = need3 - s.above;
+  __syncthreads();
+
+  const int per = (int)((n_cand + NT - 1) / NT);
+  const int c0 = min((int)n_cand, tid * per), c1 = min((int)n_cand, c0 + per);
+  uint32_t my_eq = 0;
+  for (int i = c0; i < c1; ++i) my_eq += s.cand_key[i] == kth;
+  uint32_t tie = block_exclusive<NT>(my_eq, s.warp, &s.total);
+  uint32_t my_sel = 0;
+  for (int i = c0; i < c1; ++i) {
+    const uint32_t key = s.cand_key[i];
+    if (key > kth || (key == kth && tie < n_ties)) ++my_sel;
+    tie += key == kth;
+  }
+  uint32_t sp = block_exclusive<NT>(my_sel, s.warp, &s.total);
+  const uint32_t n_sel = min(s.total, (uint32_t)KMAX);
+  tie -= my_eq;
+  for (int i = c0; i < c1; ++i) {
+    const uint32_t key = s.cand_key[i];
+    if (key > kth || (key == kth && tie < n_ties)) {
+      if (sp < (uint32_t)KMAX) s.sel[sp] = s.cand_pos[i];
+      ++sp;
+    }
+    tie += key == kth;
+  }
+  __syncthreads();
+  return n_sel;
+}
+
 template <int NT>
 __device__ void topk_row(const TopkParams& p, int b, const Emit& out, TopkSmem& s) {
   constexpr int NWARP = NT / 32;
@@ -395,51 +454,7 @@ __device__ void topk_row(const TopkParams& p, int b, const Emit& out, TopkSmem& 
   __syncthreads();
 
   // ---- 3. resolve the low 20 bits among the candidates
-  for (int i = tid; i < NBIN1; i += NT) s.hist[i] = 0;
-  __syncthreads();
-  for (int i = tid; i < (int)n_cand; i += NT) atomicAdd(&s.hist[(s.cand_key[i] >> 8) & 0xFFFu], 1u);
-  __syncthreads();
-  find_threshold<NT>(s.hist, NBIN1, need2, s.warp, &s.T, &s.above);
-  const uint32_t T2 = (uint32_t)s.T;
-  const uint32_t need3 = need2 - s.above;
-  __syncthreads();
-  for (int i = tid; i < 256; i += NT) s.hist[i] = 0;
-  __syncthreads();
-  for (int i = tid; i < (int)n_cand; i += NT) {
-    const uint32_t key = s.cand_key[i];
-    if (((key >> 8) & 0xFFFu) == T2) atomicAdd(&s.hist[key & 0xFFu], 1u);
-  }
-  __syncthreads();
-  find_threshold<NT>(s.hist, 256, need3, s.warp, &s.T, &s.above);
-  const uint32_t kth = (T1 << 20) | (T2 << 8) | (uint32_t)s.T;
-  const uint32_t n_ties = need3 - s.above;
-  __syncthreads();
-
-  // selected candidates, in position order: key > kth, or key == kth among
-  // the first n_ties such keys
-  const int per = (int)((n_cand + NT - 1) / NT);
-  const int c0 = min((int)n_cand, tid * per), c1 = min((int)n_cand, c0 + per);
-  uint32_t my_eq = 0;
-  for (int i = c0; i < c1; ++i) my_eq += s.cand_key[i] == kth;
-  uint32_t tie = block_exclusive<NT>(my_eq, s.warp, &s.total);
-  uint32_t my_sel = 0;
-  for (int i = c0; i < c1; ++i) {
-    const uint32_t key = s.cand_key[i];
-    if (key > kth || (key == kth && tie < n_ties)) ++my_sel;
-    tie += key == kth;
-  }
-  uint32_t sp = block_exclusive<NT>(my_sel, s.warp, &s.total);
-  const uint32_t n_sel = min(s.total, (uint32_t)KMAX);
-  tie -= my_eq;
-  for (int i = c0; i < c1; ++i) {
-    const uint32_t key = s.cand_key[i];
-    if (key > kth || (key == kth && tie < n_ties)) {
-      if (sp < (uint32_t)KMAX) s.sel[sp] = s.cand_pos[i];
-      ++sp;
-    }
-    tie += key == kth;
-  }
-  __syncthreads();
+  const uint32_t n_sel = resolve_candidates<NT>(s, n_cand, need2, T1);
 
   // ---- merge the two ascending lists
   for (int i = tid; i < (int)n_sure; i += NT) {
@@ -500,8 +515,248 @@ __global__ void __launch_bounds__(NT, 1024 / NT) topk_rows_kernel(const TopkPara
   }
 }
 
+// ---------------------------------------------------------- cluster mode
+// Few long rows (decode batches with the logits kernel's histogram): the CL
+// CTAs of one thread-block cluster share a row, each sweeping a contiguous
+// CL-th of it, so a batch of 8 rows keeps 64 SMs busy instead of 8. Every CTA
+// derives the same threshold bin T1 from the row's histogram; after a count
+// pass the CTAs exchange their counts through distributed shared memory,
+// write their "sure" positions to their own shared memory and their
+// candidates (bin T1) into rank 0's candidate lists at their prefix offsets,
+// in position order. Rank 0 resolves the K-th key among the candidates;
+// every CTA then emits its own sure positions and the selected candidates
+// that fall in its range, ranked against rank 0's selected list and its own
+// sure list. Rows whose bin T1 overflows the candidate buffer are done by
+// rank 0 alone with the one-CTA path.
+constexpr int CL = 8;
+constexpr int NT_CL = 512;
+
+template <int NT>
+__device__ void topk_row_cluster(const TopkParams& p, int b, const Emit& out, TopkSmem& s,
+                                 cg::cluster_group& cl, int rank) {
+  constexpr int NWARP = NT / 32;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int K = p.K;
+  const float* row = out.row;
+  const int n = max(0, min(p.lens[b], p.max_kv));
+  if (n <= K) {  // uniform over the cluster: rank 0 emits the row
+    if (rank == 0) {
+      for (int i = tid; i < K; i += NT) out(i, i < n ? i : -1);
+      if (p.hist_clear)
+        for (int i = tid; i < NBIN1; i += NT) p.hist_clear[(int64_t)b * NBIN1 + i] = 0;
+    }
+    return;
+  }
+  for (int i = tid; i < NBIN1; i += NT) s.hist[i] = (uint32_t)p.hist[(int64_t)b * NBIN1 + i];
+  __syncthreads();
+  find_threshold<NT>(s.hist, NBIN1, (uint32_t)K, s.warp, &s.T, &s.above);
+  const uint32_t T1 = (uint32_t)s.T;
+  const uint32_t need2 = (uint32_t)K - s.above;
+  const uint32_t cnt1 = s.hist[T1];
+  const bool overflow = cnt1 > (uint32_t)CAP || s.above > (uint32_t)KMAX;
+  __syncthreads();
+  if (overflow) {  // the same decision in every CTA (same histogram)
+    cl.sync();     // every CTA has read the histogram before rank 0 may clear it
+    if (rank == 0) topk_row<NT>(p, b, out, s);
+    return;
+  }
+  const bool vec = (reinterpret_cast<uintptr_t>(row) & 15) == 0;
+  const int per = ((n + CL * 128 - 1) / (CL * 128)) * 128;  // positions per CTA, 128-aligned
+  const int r0 = min(n, rank * per), r1 = min(n, r0 + per);
+  const int run = ((r1 - r0 + NWARP * 128 - 1) / (NWARP * 128)) * 128;
+  const int w0 = r0 + warp * run, w1 = min(r1, w0 + run);
+
+  // count pass
+  uint32_t ns = 0, nc = 0;
+  for (int i0 = w0; i0 < w1; i0 += 128 * SWEEP_U) {
+    uint32_t kq[SWEEP_U][4];
+#pragma unroll
+    for (int u = 0; u < SWEEP_U; ++u) load4(row, i0 + 128 * u + 4 * lane, w1, vec, kq[u]);
+#pragma unroll
+    for (int u = 0; u < SWEEP_U; ++u) {
+      const int i = i0 + 128 * u + 4 * lane;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        if (i + e >= w1) continue;
+        const uint32_t bin = kq[u][e] >> 20;
+        ns += bin > T1;
+        nc += bin == T1;
+      }
+    }
+  }
+  uint32_t packed = ns | (nc << 16);
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) packed += __shfl_xor_sync(0xffffffffu, packed, off);
+  if (lane == 0) s.warp_off[warp] = packed;
+  __syncthreads();
+  if (warp == 0) {
+    const uint32_t v = lane < NWARP ? s.warp_off[lane] : 0u;
+    uint32_t inc_s = v & 0xFFFFu, inc_c = v >> 16;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const uint32_t us = __shfl_up_sync(0xffffffffu, inc_s, off);
+      const uint32_t uc = __shfl_up_sync(0xffffffffu, inc_c, off);
+      if (lane >= off) {
+        inc_s += us;
+        inc_c += uc;
+      }
+    }
+    if (lane < NWARP) s.warp[lane] = (inc_s - (v & 0xFFFFu)) | ((inc_c - (v >> 16)) << 16);
+    if (lane == NWARP - 1) {
+      const uint32_t tot = inc_s | (inc_c << 16);
+      for (int r = 0; r < CL; ++r) *cl.map_shared_rank(&s.cl_cnt[rank], r) = tot;
+    }
+  }
+  cl.sync();  // counts exchanged; every CTA has read the histogram
+  if (rank == 0 && p.hist_clear)
+    for (int i = tid; i < NBIN1; i += NT) p.hist_clear[(int64_t)b * NBIN1 + i] = 0;
+  uint32_t sure_base = 0, cand_base = 0, n_cand = 0;
+#pragma unroll
+  for (int r = 0; r < CL; ++r) {
+    const uint32_t c = s.cl_cnt[r];
+    if (r < rank) {
+      sure_base += c & 0xFFFFu;
+      cand_base += c >> 16;
+    }
+    n_cand += c >> 16;
+  }
+  const uint32_t my_sure = s.cl_cnt[rank] & 0xFFFFu;
+  n_cand = min(n_cand, (uint32_t)CAP);
+  uint32_t* key0 = cl.map_shared_rank(s.cand_key, 0);
+  int32_t* pos0 = cl.map_shared_rank(s.cand_pos, 0);
+
+  // write pass: sure positions here, candidates into rank 0, in order
+  uint32_t off_s = s.warp[warp] & 0xFFFFu, off_c = cand_base + (s.warp[warp] >> 16);
+  for (int i0 = w0; i0 < w1; i0 += 128 * SWEEP_U) {
+    uint32_t kq[SWEEP_U][4];
+#pragma unroll
+    for (int u = 0; u < SWEEP_U; ++u) load4(row, i0 + 128 * u + 4 * lane, w1, vec, kq[u]);
+#pragma unroll
+    for (int u = 0; u < SWEEP_U; ++u) {
+      const int i = i0 + 128 * u + 4 * lane;
+      const uint32_t* k = kq[u];
+      uint32_t cs = 0, cc = 0;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        if (i + e >= w1) continue;
+        cs += (k[e] >> 20) > T1;
+        cc += (k[e] >> 20) == T1;
+      }
+      uint32_t inc = cs | (cc << 16);
+#pragma unroll
+      for (int off = 1; off < 32; off <<= 1) {
+        const uint32_t up = __shfl_up_sync(0xffffffffu, inc, off);
+        if (lane >= off) inc += up;
+      }
+      const uint32_t tot = __shfl_sync(0xffffffffu, inc, 31);
+      const uint32_t ex = inc - (cs | (cc << 16));
+      uint32_t ps = off_s + (ex & 0xFFFFu), pc = off_c + (ex >> 16);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        if (i + e >= w1) continue;
+        const uint32_t bin = k[e] >> 20;
+        if (bin > T1) {
+          if (ps < (uint32_t)KMAX) s.sure[ps] = i + e;
+          ++ps;
+        } else if (bin == T1) {
+          if (pc < (uint32_t)CAP) {
+            key0[pc] = k[e];
+            pos0[pc] = i + e;
+          }
+          ++pc;
+        }
+      }
+      off_s += tot & 0xFFFFu;
+      off_c += tot >> 16;
+    }
+  }
+  cl.sync();  // all candidates have landed in rank 0
+  if (rank == 0) {
+    const uint32_t n_sel = resolve_candidates<NT>(s, n_cand, need2, T1);
+    if (tid == 0) s.cl_nsel = n_sel;
+  }
+  cl.sync();  // rank 0's selected list is ready
+  const int32_t* sel0 = cl.map_shared_rank(s.sel, 0);
+  const int n_sel = (int)*cl.map_shared_rank(&s.cl_nsel, 0);
+  const int lo = count_below(sel0, n_sel, r0), hi = count_below(sel0, n_sel, r1);
+  // this CTA's selected candidates, copied next to its sure list
+  int32_t* mine = s.cand_pos;  // rank 0's candidates are consumed; other CTAs never used theirs
+  for (int j = tid; j < hi - lo; j += NT) mine[j] = sel0[lo + j];
+  __syncthreads();
+  const int nm = hi - lo;
+  const int n_my_sure = (int)min(my_sure, (uint32_t)KMAX);
+  for (int i = tid; i < n_my_sure; i += NT) {
+    const int32_t P = s.sure[i];
+    const int o = (int)sure_base + i + lo + count_below(mine, nm, P);
+    if (o < K) out(o, P);
+  }
+  for (int j = tid; j < nm; j += NT) {
+    const int32_t P = mine[j];
+    const int o = (int)sure_base + lo + j + count_below(s.sure, n_my_sure, P);
+    if (o < K) out(o, P);
+  }
+  if (rank == CL - 1) {  // only for an inconsistent histogram: pad the tail
+    int total = 0;
+    for (int r = 0; r < CL; ++r) total += (int)(s.cl_cnt[r] & 0xFFFFu);
+    for (int i = total + n_sel + tid; i < K; i += NT) out(i, -1);
+  }
+  cl.sync();  // no CTA leaves while another still reads rank 0's lists
+}
+
+__global__ void __launch_bounds__(NT_CL, 1) topk_cluster_kernel(const TopkParams p) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  TopkSmem& s = *reinterpret_cast<TopkSmem*>(smem_raw);
+  cg::cluster_group cl = cg::this_cluster();
+  const int rank = (int)cl.block_rank();
+  const int b = blockIdx.y;
+  const int tid = threadIdx.x;
+  Emit e{};
+  e.row = p.score + (int64_t)b * p.score_stride;
+  float* pay = p.pay;
+  int seq = 0;
+  bool ok = true;
+  if (p.ctl) {  // exchange staging: rank 0 waits for the slot, the cluster follows its verdict
+    seq = *reinterpret_cast<const volatile int*>(p.ctl) + 1;
+    pay += (int64_t)(seq & 1) * (p.slot_bytes / 4);
+    if (rank == 0) {
+      if (tid == 0) s.ok = read_err_word(p.err) == 0;
+      __syncthreads();
+      if (seq > 2 && s.ok && tid < p.tp && !wait_flag_geq(p.peer_merged[tid], seq - 2, p.timeout_ns, p.err))
+        s.ok = 0;
+      __syncthreads();
+    }
+    cl.sync();
+    ok = *cl.map_shared_rank(&s.ok, 0) != 0;
+    cl.sync();  // rank 0's verdict is read before its shared memory is reused
+  }
+  if (pay) {
+    e.val = pay + (int64_t)b * p.pay_stride;
+    e.pos = reinterpret_cast<int32_t*>(e.val + p.K);
+    e.off = p.pos_off;
+  } else {
+    e.idx = p.idx + (int64_t)b * p.idx_stride;
+  }
+  if (ok) {
+    topk_row_cluster<NT_CL>(p, b, e, s, cl, rank);
+  } else if (p.hist_clear && rank == 0) {
+    for (int i = tid; i < NBIN1; i += NT_CL) p.hist_clear[(int64_t)b * NBIN1 + i] = 0;
+  }
+  if (p.ctl) {  // the last CTA of the grid publishes staged = seq (nothing after an error)
+    __syncthreads();
+    if (tid == 0) {
+      __threadfence_system();
+      if (atomicAdd(p.ctl + 1, 1) == (int)(gridDim.x * gridDim.y) - 1) {
+        p.ctl[1] = 0;
+        __threadfence_system();
+        if (read_err_word(p.err) == 0) st_release_sys_s32(p.my_flags, seq);
+      }
+    }
+  }
+}
+
 std::once_flag g_once[kMaxDevices];
 int g_status[kMaxDevices];
+int g_cluster_ok[kMaxDevices];  // clusters of CL topk CTAs can be resident
 
 int run_topk(const TopkParams& p, int B, cudaStream_t s) {
   DSA_REQUIRE(B >= 0 && p.max_kv >= 0, DSA_ERR_INVALID, "topk: negative size");
@@ -518,11 +773,54 @@ int run_topk(const TopkParams& p, int B, cudaStream_t s) {
     if (e == cudaSuccess)
       e = cudaFuncSetAttribute(topk_rows_kernel<NT_LARGE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                (int)sizeof(TopkSmem));
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(topk_cluster_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               (int)sizeof(TopkSmem));
     g_status[dev] = (int)e;
+    if (e == cudaSuccess) {  // can clusters of CL such CTAs be resident at all?
+      cudaLaunchConfig_t cfg{};
+      cfg.gridDim = dim3(CL, 1, 1);
+      cfg.blockDim = dim3(NT_CL);
+      cfg.dynamicSmemBytes = sizeof(TopkSmem);
+      cudaLaunchAttribute attr{};
+      attr.id = cudaLaunchAttributeClusterDimension;
+      attr.val.clusterDim.x = CL;
+      attr.val.clusterDim.y = 1;
+      attr.val.clusterDim.z = 1;
+      cfg.attrs = &attr;
+      cfg.numAttrs = 1;
+      int nc = 0;
+      if (cudaOccupancyMaxActiveClusters(&nc, topk_cluster_kernel, &cfg) != cudaSuccess) {
+        cudaGetLastError();
+        nc = 0;
+      }
+      g_cluster_ok[dev] = nc > 0;
+    }
   });
   if (g_status[dev] != 0) {
     set_error("cudaFuncSetAttribute(topk): %s", cudaGetErrorString((cudaError_t)g_status[dev]));
     return DSA_ERR_CUDA;
+  }
+  // few long rows with the logits kernel's histogram: a cluster of CL CTAs per row
+  if (p.hist && g_cluster_ok[dev] && B < sm_count(dev) && p.max_kv >= CL * 1024 && p.K <= KMAX) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(CL, B, 1);
+    cfg.blockDim = dim3(NT_CL);
+    cfg.dynamicSmemBytes = sizeof(TopkSmem);
+    cfg.stream = s;
+    cudaLaunchAttribute attr{};
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = CL;
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, topk_cluster_kernel, p);
+    if (e != cudaSuccess) {
+      set_error("topk_cluster_kernel launch: %s", cudaGetErrorString(e));
+      return DSA_ERR_CUDA;
+    }
+    return DSA_OK;
   }
   if (2 * B < sm_count(dev))
     topk_rows_kernel<NT_LARGE><<<B, NT_LARGE, sizeof(TopkSmem), s>>>(p);

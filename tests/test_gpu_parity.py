@@ -607,6 +607,61 @@ def test_topk_long_decode_row(dsa):
     np.testing.assert_array_equal(out.cpu().numpy(), O.topk_rows(score, lens, K))
 
 
+def cluster_topk_rows(rng, S):
+    """Rows for the cluster top-k (few rows of >= 8192 keys with a histogram):
+    a long row, a short one (< K), one just above K, one with a long run of
+    values equal to the K-th, and one whose threshold bin holds more keys
+    than the candidate buffer (the one-CTA fallback inside the cluster)."""
+    B = 6
+    s = rng.standard_normal((B, S)).astype(np.float32)
+    s[3] = np.round(s[3] * 2) / 2             # few distinct values: huge ties at the K-th
+    n_eq = min(30000, S - 100)                # more equal keys than the candidate buffer holds
+    s[4, :n_eq] = 1.0
+    s[4, n_eq:] = rng.standard_normal(S - n_eq).astype(np.float32) - 5.0
+    s[5] = np.arange(S, dtype=np.float32)[::-1] * 1e-3  # strictly decreasing
+    lens = np.array([S, 1500, 2049, S, S, S - 7], np.int32)
+    for b in range(B):
+        s[b, lens[b]:] = -np.inf
+    return s, lens
+
+
+@pytest.mark.parametrize("S", [9000, 70000, 180224])
+def test_decode_topk_cluster_mode_exact(dsa, S):
+    """Few long rows with the fused histogram run as a cluster of CTAs per row;
+    exact (lowest-position ties, ascending, -1 padded) and the histogram is
+    left as given (sm70_decode_topk does not clear it)."""
+    rng = np.random.default_rng(S)
+    s, lens = cluster_topk_rows(rng, S)
+    K = 2048
+    hist = to_dev(O.level1_hist(s, lens))
+    out = torch.full((s.shape[0], K), -9, dtype=torch.int32, device=DEV)
+    dsa.sm70_decode_topk(out, to_dev(s), to_dev(lens), hist, K)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(out.cpu().numpy(), O.topk_rows(s, lens, K))
+    np.testing.assert_array_equal(hist.cpu().numpy(), O.level1_hist(s, lens))
+
+
+def test_topk_payload_cluster_mode_clears_hist(dsa):
+    """Payload mode in cluster mode: values, shifted positions, pads, and the
+    consumed histogram zeroed for the next step."""
+    from importlib import import_module
+
+    ops = import_module("glm5-on-v100_b200.ops")
+    rng = np.random.default_rng(33)
+    S, K, off = 40000, 2048, 90000
+    s, lens = cluster_topk_rows(rng, S)
+    hist = to_dev(O.level1_hist(s, lens))
+    pay = torch.full((s.shape[0], 2 * K), 7.0, device=DEV)
+    ops.topk_rows_payload(pay, to_dev(s), to_dev(lens), hist, K, off)
+    torch.cuda.synchronize()
+    exp = O.topk_rows(s, lens, K)
+    p = pay.cpu().numpy()
+    np.testing.assert_array_equal(p[:, K:].copy().view(np.int32), np.where(exp >= 0, exp + off, -1))
+    np.testing.assert_array_equal(p[:, :K], np.where(exp >= 0, np.take_along_axis(s, np.maximum(exp, 0), axis=1),
+                                                     -np.inf).astype(np.float32))
+    assert int(hist.abs().sum()) == 0
+
+
 # -------------------------------------------------------------- K scatter
 @pytest.mark.parametrize("k_dtype", [torch.float16, torch.bfloat16])
 @pytest.mark.parametrize("fmt", ["fp8", "f16", "bf16"])
@@ -812,7 +867,10 @@ def test_decode_exchange_single_rank_steps_and_timeout(dsa):
         s = rng.standard_normal((B, S)).astype(np.float32)
         score = to_dev(s)
         out = torch.full((B, K), -9, dtype=torch.int32, device=DEV)
-        ex.topk_stage(score, dl, None, 0)
+        # odd steps with the fused histogram (the cluster kernel, B < SMs and
+        # S >= 8192), even steps without it (one CTA per row)
+        hist = to_dev(O.level1_hist(s, lens)) if step % 2 else None
+        ex.topk_stage(score, dl, hist, 0)
         ex.merge(out, B)
         torch.cuda.synchronize()
         assert not ops.p2p_failed(DEV)
@@ -824,7 +882,8 @@ def test_decode_exchange_single_rank_steps_and_timeout(dsa):
     ops.P2P_TIMEOUT_NS = 50_000_000  # 50 ms
     try:
         ex.fbuf.view(torch.int32)[1] = 0  # merged flag behind: the step-6 slot wait (merged >= 4) cannot finish
-        ex.topk_stage(to_dev(rng.standard_normal((B, S)).astype(np.float32)), dl, None, 0)
+        s = rng.standard_normal((B, S)).astype(np.float32)
+        ex.topk_stage(to_dev(s), dl, to_dev(O.level1_hist(s, lens)), 0)
         ex.merge(torch.empty(B, K, dtype=torch.int32, device=DEV), B)
         torch.cuda.synchronize()
         assert ops.p2p_failed(DEV)
