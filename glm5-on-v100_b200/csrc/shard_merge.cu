@@ -34,7 +34,11 @@
 // relaxed system-scope loads (plain peer loads; no TMA, no multicast).
 #include <climits>
 
+#include <cooperative_groups.h>
+
 #include "common.cuh"
+
+namespace cg = cooperative_groups;
 
 namespace dsa {
 namespace {
@@ -459,7 +463,7 @@ __device__ void finish_exchange(const MergeArgs& a, int seq) {
   __syncthreads();
   if (threadIdx.x != 0) return;
   __threadfence_system();
-  if (atomicAdd(a.ctl + 2, 1) == (int)gridDim.x - 1) {
+  if (atomicAdd(a.ctl + 2, 1) == (int)(gridDim.x * gridDim.y) - 1) {
     a.ctl[2] = 0;
     __threadfence_system();
     if (read_err_word(a.err) == 0) st_release_sys_s32(a.my_flags + 1, seq);
@@ -485,6 +489,394 @@ __global__ void __launch_bounds__(MT, 2) shard_merge_kernel(const MergeArgs a) {
     ok = s.ok != 0;
   }
   if (ok && r < a.R) merge_row(a, r, soff, s);
+  if (a.ctl) finish_exchange(a, seq);
+}
+
+// ---------------------------------------------------------- cluster mode
+// Few rows (a decode batch): the tp CTAs of one thread-block cluster share a
+// row, CTA s owning shard s's K candidates (its peer's slot in P2P mode), so
+// 8 rows x 8 shards keep 64 SMs busy instead of 8. The same steps as
+// merge_row, with the block-wide reductions made cluster-wide through
+// distributed shared memory:
+//   * every CTA publishes (high count, min, max) to all CTAs;
+//   * a radix pass: local histogram, flushed into rank 0's (DSMEM atomics);
+//     rank 0 picks the bin and writes it to every CTA; two cluster barriers;
+//   * tie counts, run lengths and run bounds are exchanged per shard, which
+//     is also column order;
+//   * each CTA ranks the positions of its own run against the other runs
+//     (bounds first, a binary search over DSMEM otherwise) and writes them;
+//     runs that are not ascending are gathered into rank 0, which ranks all
+//     by counting.
+struct ClusterMergeSmem {
+  uint32_t hist[NBIN];
+  int32_t pos[MAX_K];        // this CTA's run; rank 0: all runs in the unsorted fallback
+  uint32_t red[3][NW];
+  unsigned long long scan[2][NW];
+  uint32_t x_nh[MAX_TP], x_min[MAX_TP], x_max[MAX_TP];  // per-CTA values, published to all
+  uint32_t x_eq[MAX_TP], x_len[MAX_TP];
+  int32_t x_first[MAX_TP], x_last[MAX_TP];
+  int x_sorted[MAX_TP], x_ok[MAX_TP];
+  uint32_t bin, above, cnt;  // rank 0 -> all: the chosen bin of a pass
+  uint32_t total;
+};
+
+__device__ __forceinline__ uint32_t block_sum_u32(uint32_t v, uint32_t* red) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  v = __reduce_add_sync(0xffffffffu, v);
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  uint32_t t = 0;
+#pragma unroll
+  for (int w = 0; w < NW; ++w) t += red[w];
+  __syncthreads();
+  return t;
+}
+
+// Block-wide exclusive prefix of v in thread order (one counter).
+__device__ __forceinline__ uint32_t block_excl_u32(uint32_t v, uint32_t* red) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  uint32_t inc = v;
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+    const uint32_t u = __shfl_up_sync(0xffffffffu, inc, d);
+    if (lane >= d) inc += u;
+  }
+  if (lane == 31) red[warp] = inc;
+  __syncthreads();
+  uint32_t pre = 0;
+#pragma unroll
+  for (int w = 0; w < NW; ++w)
+    if (w < warp) pre += red[w];
+  __syncthreads();
+  return pre + inc - v;
+}
+
+// The same pick as pick_bin, on the cluster smem layout.
+__device__ __forceinline__ void pick_bin_cl(int nbins, uint32_t need, ClusterMergeSmem& s) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  uint32_t h[4], c = 0;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int b = 4 * tid + j;
+    h[j] = b < nbins ? s.hist[b] : 0u;
+    c += h[j];
+  }
+  uint32_t suf = c;
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+    const uint32_t v = __shfl_down_sync(0xffffffffu, suf, d);
+    if (lane + d < 32) suf += v;
+  }
+  if (lane == 0) s.red[0][warp] = suf;
+  __syncthreads();
+  uint32_t later = 0;
+#pragma unroll
+  for (int w = 0; w < NW; ++w)
+    if (w > warp) later += s.red[0][w];
+  suf += later;
+  uint32_t above = suf - c;
+  if (above < need && suf >= need) {
+#pragma unroll
+    for (int j = 3; j >= 0; --j) {
+      if (above + h[j] >= need) {
+        s.bin = 4 * tid + j;
+        s.above = above;
+        s.cnt = h[j];
+        break;
+      }
+      above += h[j];
+    }
+  }
+  __syncthreads();
+}
+
+__device__ void merge_row_cluster(const MergeArgs& a, int r, int64_t soff, ClusterMergeSmem& s,
+                                  cg::cluster_group& cl, int rank) {
+  const int tid = threadIdx.x;
+  const int K = a.K, tp = a.tp;
+  const int c0 = tid * PER;
+  const int64_t row_off = (int64_t)r * 2 * K;
+  const float* slab = reinterpret_cast<const float*>(a.base[rank] + soff + (int64_t)rank * a.shard_stride) + row_off;
+  ClusterMergeSmem* s0 = cl.map_shared_rank(&s, 0);
+
+  // ---- 1. this shard's keys
+  uint32_t key[PER];
+  uint32_t vmask = 0;
+  if (c0 < K) {
+    float f[PER];
+    if (a.vec) {
+      const float4 q = a.p2p ? ld_sys_f4(slab + c0) : __ldg(reinterpret_cast<const float4*>(slab + c0));
+      f[0] = q.x;
+      f[1] = q.y;
+      f[2] = q.z;
+      f[3] = q.w;
+    } else {
+#pragma unroll
+      for (int e = 0; e < PER; ++e)
+        f[e] = c0 + e < K ? (a.p2p ? ld_sys_f32(slab + c0 + e) : __ldg(slab + c0 + e)) : 0.f;
+    }
+#pragma unroll
+    for (int e = 0; e < PER; ++e) {
+      key[e] = monotone32(f[e]);
+      if (c0 + e < K) vmask |= 1u << e;
+    }
+  }
+  uint32_t nh = 0, kmin = 0xFFFFFFFFu, kmax = 0;
+#pragma unroll
+  for (int e = 0; e < PER; ++e)
+    if (((vmask >> e) & 1u) && key[e] > NEG_KEY) {
+      ++nh;
+      kmin = min(kmin, key[e]);
+      kmax = max(kmax, key[e]);
+    }
+  nh = block_sum_u32(nh, s.red[0]);
+  {
+    const int lane = tid & 31, warp = tid >> 5;
+    const uint32_t wmin = __reduce_min_sync(0xffffffffu, kmin), wmax = __reduce_max_sync(0xffffffffu, kmax);
+    if (lane == 0) {
+      s.red[1][warp] = wmin;
+      s.red[2][warp] = wmax;
+    }
+    __syncthreads();
+    kmin = 0xFFFFFFFFu;
+    kmax = 0;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) {
+      kmin = min(kmin, s.red[1][w]);
+      kmax = max(kmax, s.red[2][w]);
+    }
+  }
+  if (tid < tp) {  // publish this CTA's values to every CTA
+    ClusterMergeSmem* d = cl.map_shared_rank(&s, tid);
+    d->x_nh[rank] = nh;
+    d->x_min[rank] = kmin;
+    d->x_max[rank] = kmax;
+  }
+  if (rank == 0)
+    for (int i = tid; i < NBIN; i += MT) s.hist[i] = 0;
+  cl.sync();
+  nh = 0;
+  kmin = 0xFFFFFFFFu;
+  kmax = 0;
+  for (int q = 0; q < tp; ++q) {
+    nh += s.x_nh[q];
+    kmin = min(kmin, s.x_min[q]);
+    kmax = max(kmax, s.x_max[q]);
+  }
+
+  // ---- 2. selection rule (cluster-wide radix select over the high keys)
+  uint32_t thr = NEG_KEY + 1, need_eq = 0;
+  bool tie = false;
+  int n_neg = 0;
+  if (nh <= (uint32_t)K) {
+    n_neg = K - (int)nh;
+  } else {
+    uint32_t base = kmin, need = (uint32_t)K;
+    const uint32_t span = kmax - kmin;
+    int bits = span ? 32 - __clz(span) : 0;
+    bool first = true;
+    while (true) {
+      if (bits == 0) {
+        thr = base;
+        need_eq = need;
+        tie = true;
+        break;
+      }
+      const int shift = max(bits - DIGIT, 0);
+      const int nbins = 1 << (bits - shift);
+      if (rank != 0)  // rank 0's histogram was cleared before the last cluster barrier
+        for (int i = tid; i < nbins; i += MT) s.hist[i] = 0;
+      __syncthreads();
+      // local counts (rank 0 counts straight into the row's histogram)
+#pragma unroll
+      for (int e = 0; e < PER; ++e) {
+        const uint32_t k = key[e];
+        if (!((vmask >> e) & 1u) || k <= NEG_KEY || k < base) continue;
+        const uint32_t d = k - base;
+        if (!first && (d >> bits) != 0) continue;
+        atomicAdd(&s.hist[d >> shift], 1u);
+      }
+      __syncthreads();
+      if (rank != 0)
+        for (int i = tid; i < nbins; i += MT) {
+          const uint32_t c = s.hist[i];
+          if (c) atomicAdd(&s0->hist[i], c);
+        }
+      cl.sync();  // rank 0 holds the row's histogram
+      if (rank == 0) {
+        pick_bin_cl(nbins, need, s);
+        for (int i = tid; i < nbins; i += MT) s.hist[i] = 0;  // cleared for the next pass
+        if (tid > 0 && tid < tp) {
+          ClusterMergeSmem* d = cl.map_shared_rank(&s, tid);
+          d->bin = s.bin;
+          d->above = s.above;
+          d->cnt = s.cnt;
+        }
+      }
+      cl.sync();  // every CTA has the pass's bin
+      const uint32_t b = s.bin, above = s.above, cnt = s.cnt;
+      need -= above;
+      base += b << shift;
+      bits = shift;
+      first = false;
+      if (cnt == need) {
+        thr = base;
+        break;
+      }
+    }
+  }
+
+  // ---- 3. selected columns of this shard (ties ranked in column order)
+  uint32_t selm = 0;
+  if (tie) {
+    uint32_t my_eq = 0;
+#pragma unroll
+    for (int e = 0; e < PER; ++e) my_eq += ((vmask >> e) & 1u) && key[e] == thr;
+    uint32_t rank_eq = block_excl_u32(my_eq, s.red[0]);
+    const uint32_t tot_eq = block_sum_u32(my_eq, s.red[1]);
+    if (tid < tp) cl.map_shared_rank(&s, tid)->x_eq[rank] = tot_eq;
+    cl.sync();
+    for (int q = 0; q < rank; ++q) rank_eq += s.x_eq[q];
+#pragma unroll
+    for (int e = 0; e < PER; ++e) {
+      if (!((vmask >> e) & 1u)) continue;
+      if (key[e] > thr) {
+        selm |= 1u << e;
+      } else if (key[e] == thr) {
+        if (rank_eq < need_eq) selm |= 1u << e;
+        ++rank_eq;
+      }
+    }
+  } else {
+#pragma unroll
+    for (int e = 0; e < PER; ++e)
+      if (((vmask >> e) & 1u) && key[e] >= thr && key[e] > NEG_KEY) selm |= 1u << e;
+  }
+
+  // ---- 4. this CTA's run of selected positions, in column order
+  const uint32_t my_n = __popc(selm);
+  uint32_t slot = block_excl_u32(my_n, s.red[0]);
+  const uint32_t run_len = block_sum_u32(my_n, s.red[1]);
+  if (selm) {
+    const float* pv = slab + K + c0;
+    int32_t pp[PER];
+    if (a.vec) {
+      const float4 q = a.p2p ? ld_sys_f4(pv) : __ldg(reinterpret_cast<const float4*>(pv));
+      pp[0] = __float_as_int(q.x);
+      pp[1] = __float_as_int(q.y);
+      pp[2] = __float_as_int(q.z);
+      pp[3] = __float_as_int(q.w);
+    } else {
+#pragma unroll
+      for (int e = 0; e < PER; ++e)
+        pp[e] = ((selm >> e) & 1u) ? __float_as_int(a.p2p ? ld_sys_f32(pv + e) : __ldg(pv + e)) : 0;
+    }
+#pragma unroll
+    for (int e = 0; e < PER; ++e)
+      if ((selm >> e) & 1u) {
+        if (slot < (uint32_t)MAX_K) s.pos[slot] = pp[e];
+        ++slot;
+      }
+  }
+  __syncthreads();
+  const int n_run = (int)min(run_len, (uint32_t)MAX_K);
+  bool unsorted = false;
+  for (int i = tid; i + 1 < n_run; i += MT)
+    if (s.pos[i] > s.pos[i + 1]) unsorted = true;
+  const int my_sorted = !__syncthreads_or(unsorted);
+  if (tid < tp) {
+    ClusterMergeSmem* d = cl.map_shared_rank(&s, tid);
+    d->x_len[rank] = (uint32_t)n_run;
+    d->x_first[rank] = n_run ? s.pos[0] : 0;
+    d->x_last[rank] = n_run ? s.pos[n_run - 1] : 0;
+    d->x_sorted[rank] = my_sorted;
+  }
+  cl.sync();
+  int all_sorted = 1, total = 0, seg0 = 0;
+  for (int q = 0; q < tp; ++q) {
+    all_sorted &= s.x_sorted[q];
+    if (q < rank) seg0 += (int)s.x_len[q];
+    total += (int)s.x_len[q];
+  }
+  total = min(total, K - n_neg);
+  int32_t* out = a.out + (a.dst_base >= 0 ? (int64_t)a.dst_base + r : (int64_t)a.dst_rows[r]) * a.out_stride;
+  if (rank == 0)
+    for (int i = tid; i < n_neg; i += MT) out[i] = -1;
+
+  // ---- 5. ascending output
+  if (all_sorted) {
+    for (int i = tid; i < n_run; i += MT) {
+      const int32_t p = s.pos[i];
+      int rk = i;
+      for (int q = 0; q < tp; ++q) {
+        const int n = (int)s.x_len[q];
+        if (q == rank || n == 0) continue;
+        const bool strict = q > rank;  // equal positions: the lower shard goes first
+        const int32_t f = s.x_first[q], l = s.x_last[q];
+        if (strict ? l < p : l <= p)
+          rk += n;
+        else if (strict ? f < p : f <= p)
+          rk += count_run(cl.map_shared_rank(s.pos, q), n, p, strict);
+      }
+      if (n_neg + rk < K) out[n_neg + rk] = p;
+    }
+  } else {
+    // gather every run into rank 0 (its own run moves to its segment too)
+    int32_t* pos0 = cl.map_shared_rank(s.pos, 0);
+    __syncthreads();
+    int32_t mine[PER];
+    int nm = 0;
+    for (int i = tid; i < n_run && nm < PER; i += MT) mine[nm++] = s.pos[i];
+    cl.sync();  // rank 0's own run is read by its threads before it is overwritten
+    for (int k = 0; k < nm; ++k) {
+      const int i = tid + k * MT;
+      if (seg0 + i < MAX_K) pos0[seg0 + i] = mine[k];
+    }
+    cl.sync();
+    if (rank == 0) {
+      int32_t v[PER];
+      int rk[PER];
+#pragma unroll
+      for (int k = 0; k < PER; ++k) {
+        const int i = tid + k * MT;
+        v[k] = i < total ? s.pos[i] : 0;
+        rk[k] = 0;
+      }
+      for (int j = 0; j < total; ++j) {
+        const int32_t u = s.pos[j];
+#pragma unroll
+        for (int k = 0; k < PER; ++k) rk[k] += u < v[k] || (u == v[k] && j < tid + k * MT);
+      }
+#pragma unroll
+      for (int k = 0; k < PER; ++k)
+        if (tid + k * MT < total && n_neg + rk[k] < K) out[n_neg + rk[k]] = v[k];
+    }
+  }
+  cl.sync();  // no CTA leaves while another reads its run
+}
+
+__global__ void __launch_bounds__(MT, 1) shard_merge_cluster_kernel(const MergeArgs a) {
+  __shared__ ClusterMergeSmem s;
+  cg::cluster_group cl = cg::this_cluster();
+  const int rank = (int)cl.block_rank();
+  const int r = blockIdx.y;
+  int seq = a.seq;
+  int64_t soff = a.slot_off;
+  if (a.ctl) {
+    seq = *reinterpret_cast<const volatile int*>(a.ctl) + 1;
+    soff = (int64_t)(seq & 1) * a.slot_bytes;
+  }
+  bool ok = true;
+  if (a.p2p) {  // each CTA waits for its own shard's peer, the cluster agrees
+    if (threadIdx.x == 0) {
+      int mine = read_err_word(a.err) == 0;
+      if (mine) mine = wait_flag_geq(a.staged[rank], seq, a.timeout_ns, a.err);
+      for (int q = 0; q < a.tp; ++q) cl.map_shared_rank(&s, q)->x_ok[rank] = mine;
+    }
+    cl.sync();
+    for (int q = 0; q < a.tp; ++q) ok = ok && s.x_ok[q] != 0;
+  }
+  if (ok && r < a.R) merge_row_cluster(a, r, soff, s, cl, rank);
   if (a.ctl) finish_exchange(a, seq);
 }
 
@@ -530,6 +922,58 @@ int check_merge_args(int tp, int R, int K, int dst_base, const int32_t* dst_rows
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
+std::once_flag g_cl_once[kMaxDevices];
+int g_cl_ok[kMaxDevices];  // clusters of 8 merge CTAs can be resident
+
+// One CTA per row, or, for few rows, a cluster of tp CTAs per row. rows = R
+// (at least one CTA runs, so the exchange mode always publishes its flag).
+int launch_merge(const MergeArgs& a, int rows, cudaStream_t s, const char* what) {
+  const int dev = current_device();
+  bool cluster = false;
+  if (a.tp >= 2 && a.R > 0 && a.R <= 32 && dev >= 0 && dev < kMaxDevices) {
+    std::call_once(g_cl_once[dev], [dev] {
+      cudaLaunchConfig_t cfg{};
+      cfg.gridDim = dim3(MAX_TP, 1, 1);
+      cfg.blockDim = dim3(MT);
+      cudaLaunchAttribute attr{};
+      attr.id = cudaLaunchAttributeClusterDimension;
+      attr.val.clusterDim.x = MAX_TP;
+      attr.val.clusterDim.y = 1;
+      attr.val.clusterDim.z = 1;
+      cfg.attrs = &attr;
+      cfg.numAttrs = 1;
+      int n = 0;
+      if (cudaOccupancyMaxActiveClusters(&n, shard_merge_cluster_kernel, &cfg) != cudaSuccess) {
+        cudaGetLastError();
+        n = 0;
+      }
+      g_cl_ok[dev] = n > 0;
+    });
+    cluster = g_cl_ok[dev] != 0;
+  }
+  if (!cluster) {
+    shard_merge_kernel<<<rows, MT, 0, s>>>(a);
+    return check_launch(what);
+  }
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(a.tp, a.R, 1);
+  cfg.blockDim = dim3(MT);
+  cfg.stream = s;
+  cudaLaunchAttribute attr{};
+  attr.id = cudaLaunchAttributeClusterDimension;
+  attr.val.clusterDim.x = a.tp;
+  attr.val.clusterDim.y = 1;
+  attr.val.clusterDim.z = 1;
+  cfg.attrs = &attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, shard_merge_cluster_kernel, a);
+  if (e != cudaSuccess) {
+    set_error("%s (cluster) launch: %s", what, cudaGetErrorString(e));
+    return DSA_ERR_CUDA;
+  }
+  return DSA_OK;
+}
+
 }  // namespace
 }  // namespace dsa
 
@@ -554,8 +998,7 @@ extern "C" int dsa_indexer_shard_merge(int32_t* out, int64_t out_stride, const f
   a.K = K;
   a.dst_base = dst_base;
   a.vec = (K % 4 == 0) && aligned16(allf);
-  shard_merge_kernel<<<R, MT, 0, as_stream(stream)>>>(a);
-  return check_launch("shard_merge_kernel");
+  return launch_merge(a, R, as_stream(stream), "shard_merge_kernel");
 }
 
 extern "C" int dsa_indexer_shard_merge_p2p(int32_t* out, int64_t out_stride, const uint64_t* data_ptrs,
@@ -588,8 +1031,7 @@ extern "C" int dsa_indexer_shard_merge_p2p(int32_t* out, int64_t out_stride, con
   a.dst_base = dst_base;
   a.seq = seq;
   a.p2p = 1;
-  shard_merge_kernel<<<R, MT, 0, as_stream(stream)>>>(a);
-  return check_launch("shard_merge_kernel(p2p)");
+  return launch_merge(a, R, as_stream(stream), "shard_merge_kernel(p2p)");
 }
 
 extern "C" int dsa_shard_exchange_merge(int32_t* out, int64_t out_stride, const uint64_t* data_ptrs,
@@ -623,8 +1065,7 @@ extern "C" int dsa_shard_exchange_merge(int32_t* out, int64_t out_stride, const 
   a.K = K;
   a.p2p = 1;
   // at least one CTA, so the merged flag is published even for R == 0
-  shard_merge_kernel<<<R > 0 ? R : 1, MT, 0, as_stream(stream)>>>(a);
-  return check_launch("shard_merge_kernel(exchange)");
+  return launch_merge(a, R > 0 ? R : 1, as_stream(stream), "shard_merge_kernel(exchange)");
 }
 
 extern "C" int dsa_indexer_shard_stage(float* slot, const float* vals, int64_t vals_stride, const int32_t* idx,

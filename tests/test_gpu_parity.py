@@ -703,14 +703,14 @@ def merge_payload(rng, tp, R, K, n_pos=10 ** 6):
     return np.concatenate([vals, pos.view(np.float32)], axis=2)
 
 
+@pytest.mark.parametrize("R", [5, 37])  # a cluster of tp CTAs per row / one CTA per row
 @pytest.mark.parametrize("tp,K", [(1, 64), (2, 2048), (3, 100), (4, 2048), (8, 2048), (8, 1)])
-def test_shard_merge_exact(dsa, tp, K):
-    rng = np.random.default_rng(tp * 31 + K)
-    R = 5
+def test_shard_merge_exact(dsa, tp, K, R):
+    rng = np.random.default_rng(tp * 31 + K + R)
     allf = merge_payload(rng, tp, R, K)
     out = torch.full((R + 3, K), -9, dtype=torch.int32, device=DEV)
     dsa.sm70_indexer_shard_merge(out, to_dev(allf), torch.empty(0, dtype=torch.int32, device=DEV), 2, K)
-    dst = np.array([7, 0, 3, 1, 6], np.int32)
+    dst = rng.permutation(R + 3)[:R].astype(np.int32)
     out2 = torch.full((R + 3, K), -9, dtype=torch.int32, device=DEV)
     dsa.sm70_indexer_shard_merge(out2, to_dev(allf), to_dev(dst), -1, K)
     torch.cuda.synchronize()
@@ -793,12 +793,12 @@ def sharded_payload(rng, tp, R, K, span, overlap=False, ties=False):
 @pytest.mark.parametrize("tp,K,overlap,ties", [(2, 2048, False, False), (8, 2048, False, False),
                                                (4, 2048, True, False), (8, 2048, False, True),
                                                (3, 512, True, True), (5, 6, False, False)])
-def test_shard_merge_sorted_runs(dsa, tp, K, overlap, ties):
+@pytest.mark.parametrize("R", [6, 33])  # a cluster of tp CTAs per row / one CTA per row
+def test_shard_merge_sorted_runs(dsa, tp, K, overlap, ties, R):
     """The merge's ordered path (every shard's run ascending): disjoint key
     spans, overlapping spans (binary-searched ranks) and long runs of equal
     values (column-order tie ranks); bit-exact against the oracle."""
-    rng = np.random.default_rng(tp * 7 + K + 3 * overlap + ties)
-    R = 6
+    rng = np.random.default_rng(tp * 7 + K + 3 * overlap + ties + R)
     allf = sharded_payload(rng, tp, R, K, span=max(4 * K, 64), overlap=overlap, ties=ties)
     out = torch.full((R, K), -9, dtype=torch.int32, device=DEV)
     dsa.sm70_indexer_shard_merge(out, to_dev(allf), torch.empty(0, dtype=torch.int32, device=DEV), 0, K)
