@@ -478,7 +478,8 @@ int run_logits(LogitsParams p, int k_format, int page_size, bool use_rows, cudaS
       launch_rows<K_F16, false>(p, mt, s);
     return check_launch("indexer_rows_kernel");
   }
-  if (!p.packed && indexer_tc_eligible(k_format, p.q_bf16, page_size, p.n_ihead, p.n_kv_rows, p.B, p.max_kv)) {
+  if ((!p.packed || p.n_ihead == 32) &&
+      indexer_tc_eligible(k_format, p.q_bf16, page_size, p.n_ihead, p.n_kv_rows, p.B, p.max_kv)) {
     IndexerTcArgs t{};
     t.score = p.score;
     t.score_stride = p.score_stride;
@@ -496,6 +497,7 @@ int run_logits(LogitsParams p, int k_format, int page_size, bool use_rows, cudaS
     t.bt_stride = p.bt_stride;
     t.max_blocks = p.max_blocks;
     t.seq_lens = p.seq_lens;
+    t.packed = p.packed;
     return launch_indexer_logits_tc(t, s);
   }
   if (k_format == DSA_FP8_IDXK)

@@ -140,8 +140,13 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   auto load_q = [&](int h) {  // thread 0
     const int s = h % QSTAGES;
     mbar_arrive_expect_tx(mb_q_full(s), QSTAGE_BYTES);
-    for (int rg = 0; rg < 2; ++rg)
-      tma_load_3d(sbase + OFF_Q + s * QSTAGE_BYTES + rg * (QSTAGE_BYTES / 2), tmq, 64 * rg, h, q0, mb_q_full(s));
+    if (a.packed) {  // one 32-byte-swizzled [128 rows x 16 dims] box per K-step (dims d, r, c, t, h)
+      for (int kk = 0; kk < HD / 16; ++kk)
+        tma_load_5d(sbase + OFF_Q + s * QSTAGE_BYTES + kk * (QM * 32), tmq, 0, 0, kk, q0 / 16, h, mb_q_full(s));
+    } else {
+      for (int rg = 0; rg < 2; ++rg)
+        tma_load_3d(sbase + OFF_Q + s * QSTAGE_BYTES + rg * (QSTAGE_BYTES / 2), tmq, 64 * rg, h, q0, mb_q_full(s));
+    }
   };
   auto issue_head = [&](int h) {  // thread 0: S_(h&1) = Q_h . K^T
     const uint32_t qa = sbase + OFF_Q + (h % QSTAGES) * QSTAGE_BYTES;
@@ -151,7 +156,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     for (int kk = 0; kk < HD / 16; ++kk) {
       const uint32_t off_a = (kk >> 2) * (QSTAGE_BYTES / 2) + (kk & 3) * 32;
       const uint32_t off_b = (kk >> 2) * (KTILE_BYTES / 2) + (kk & 3) * 32;
-      mma_f16_ss(d, sw128_desc(qa + off_a, 16, 1024), sw128_desc(kb + off_b, 16, 1024), IDESC, kk > 0 ? 1u : 0u);
+      const uint64_t da = a.packed ? sw32_desc(qa + kk * (QM * 32), 256) : sw128_desc(qa + off_a, 16, 1024);
+      mma_f16_ss(d, da, sw128_desc(kb + off_b, 16, 1024), IDESC, kk > 0 ? 1u : 0u);
     }
     mma_commit(mb_s_full(h & 1));
   };
@@ -318,12 +324,13 @@ int ensure_setup(int dev) {
 }
 
 int encode(CUtensorMap* m, const void* base, bool bf16, cuuint32_t rank, const cuuint64_t* dims,
-           const cuuint64_t* strides_bytes, const cuuint32_t* box, const char* what) {
-  const cuuint32_t elem_strides[3] = {1, 1, 1};
+           const cuuint64_t* strides_bytes, const cuuint32_t* box, const char* what,
+           CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
+  const cuuint32_t elem_strides[5] = {1, 1, 1, 1, 1};
   const CUresult r = g_encode(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, rank,
                               const_cast<void*>(base), dims, strides_bytes, box, elem_strides,
-                              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                              CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   DSA_REQUIRE(r == CUDA_SUCCESS, DSA_ERR_CUDA, "indexer_logits_tc: tensor map for %s failed (CUresult %d)", what,
               (int)r);
   return DSA_OK;
@@ -348,7 +355,16 @@ int launch_indexer_logits_tc(const IndexerTcArgs& a, cudaStream_t s) {
   if (st != DSA_OK) return st;
   const bool bf16 = a.q_bf16 != 0;
   CUtensorMap tq, tk;
-  {
+  if (a.packed) {
+    // packed q [32, nqt, 8, 16, 16]: element (h, t, c, r, d) = q[16t + r, h, 16c + d]; a box is one
+    // head's 16-dim chunk c of 128 rows (8 row groups t), 32 bytes per row
+    const cuuint64_t nqt = (cuuint64_t)((a.B + 15) / 16);
+    const cuuint64_t dims[5] = {16, 16, 8, nqt, (cuuint64_t)a.n_ihead};
+    const cuuint64_t strides[4] = {32, 16 * 32, 8 * 16 * 32, nqt * 8 * 16 * 32};
+    const cuuint32_t box[5] = {16, 16, 1, QM / 16, 1};
+    st = encode(&tq, a.q, bf16, 5, dims, strides, box, "q_packed", CU_TENSOR_MAP_SWIZZLE_32B);
+    if (st != DSA_OK) return st;
+  } else {
     const cuuint64_t dims[3] = {(cuuint64_t)HD, (cuuint64_t)a.n_ihead, (cuuint64_t)a.B};
     const cuuint64_t strides[2] = {(cuuint64_t)HD * 2, (cuuint64_t)a.n_ihead * HD * 2};
     const cuuint32_t box[3] = {64, 1, QM};

@@ -22,10 +22,12 @@ struct IndexerTcArgs {
   int64_t bt_stride;
   int max_blocks;
   const int32_t* seq_lens;
+  int packed;          // q is the packed layout [32, ceil(B/16), 8, 16, 16] (sai.py:131-148)
 };
 
 // True when the tcgen05 kernel serves this call (16-bit cache of q's type,
-// page >= 8, unpacked q); the caller keeps the mma.sync kernel otherwise.
+// page >= 8; packed q needs 32 heads); the caller keeps the mma.sync kernel
+// otherwise.
 bool indexer_tc_eligible(int k_format, int q_bf16, int page_size, int n_ihead, int64_t n_kv_rows, int B,
                          int max_kv);
 int launch_indexer_logits_tc(const IndexerTcArgs& a, cudaStream_t s);

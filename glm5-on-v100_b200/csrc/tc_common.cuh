@@ -22,6 +22,14 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr, uint32_t lbo_byte
          ((uint64_t)((sbo_bytes >> 4) & 0x3FFFu) << 32) | (1ull << 46) | (2ull << 61);
 }
 
+// The same descriptor for a 32-byte-swizzled K-major operand: rows of 32
+// bytes (16 fp16 of K, one MMA K-step) in 256-byte atoms of 8 rows; the
+// stride byte offset steps from one 8-row group to the next (layout type 6).
+__device__ __forceinline__ uint64_t sw32_desc(uint32_t saddr, uint32_t sbo_bytes) {
+  return (uint64_t)((saddr >> 4) & 0x3FFFu) | (1ull << 16) | ((uint64_t)((sbo_bytes >> 4) & 0x3FFFu) << 32) |
+         (1ull << 46) | (6ull << 61);
+}
+
 // Instruction descriptor, kind::f16 with f32 accumulation:
 //   [4,6) D format (1 = f32) | [7,10) A format | [10,13) B format (0 = f16,
 //   1 = bf16) | [15] A major | [16] B major (0 = K, 1 = MN) |
@@ -189,6 +197,14 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, uint64_t tmap, int x, 
       "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
       "[%4];" ::"r"(dst),
       "l"(tmap), "r"(x), "r"(y), "r"(mbar)
+      : "memory");
+}
+__device__ __forceinline__ void tma_load_5d(uint32_t dst, uint64_t tmap, int c0, int c1, int c2, int c3, int c4,
+                                            uint32_t mbar) {
+  asm volatile(
+      "cp.async.bulk.tensor.5d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5, "
+      "%6}], [%7];" ::"r"(dst),
+      "l"(tmap), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4), "r"(mbar)
       : "memory");
 }
 __device__ __forceinline__ void tma_load_3d(uint32_t dst, uint64_t tmap, int x, int y, int z, uint32_t mbar) {

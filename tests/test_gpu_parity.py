@@ -465,18 +465,22 @@ def test_indexer_tc_kernel_edges(dsa, fmt, Hi, page, B, S, pad, holes):
         assert torch.isnan(buf[:, c["max_kv"]:]).all()
 
 
-def test_indexer_packed_equals_unpacked(dsa):
+@pytest.mark.parametrize("B", [70, 300])
+def test_indexer_packed_equals_unpacked(dsa, B):
     # the fp8 cache runs the same mma.sync kernel for both q layouts: bit-identical
-    c = logits_case(300, B=70, Hi=32, S=1500, page=64, shared_bt=True, causal=True)
+    c = logits_case(300 + B, B=B, Hi=32, S=1500, page=64, shared_bt=True, causal=True)
     s1, ref, _ = run_logits(dsa, c, "fp8")
     s2, _, _ = run_logits(dsa, c, "fp8", packed=True)
     np.testing.assert_array_equal(s1, s2)
     assert_scores_close(s2, ref)
-    # with a 16-bit cache the unpacked layout runs the tcgen05 kernel
-    s3, ref3, _ = run_logits(dsa, c, "f16")
-    s4, _, _ = run_logits(dsa, c, "f16", packed=True)
-    assert_scores_close(s3, ref3)
-    assert_scores_close(s4, ref3)
+    # with a 16-bit cache both layouts run the tcgen05 kernel (packed q through
+    # 32-byte-swizzled boxes of a 5-D tensor map, one per MMA K-step): the
+    # same products in the same order, bit-identical
+    for fmt, qd in (("f16", torch.float16), ("bf16", torch.bfloat16)):
+        s3, ref3, _ = run_logits(dsa, c, fmt, qd)
+        s4, _, _ = run_logits(dsa, c, fmt, qd, packed=True)
+        assert_scores_close(s3, ref3)
+        np.testing.assert_array_equal(s3, s4)
 
 
 def test_indexer_prefill_full_size_sampled_rows(dsa):
