@@ -1,5 +1,5 @@
-"""Two-GPU tests of the key-sharded indexer's exact merge (skipped with fewer
-than two GPUs): two processes, one per GPU, merge their local top-K
+"""Multi-GPU tests of the key-sharded indexer's exact merge (2, 4 and 8
+ranks; each skipped with fewer GPUs): one process per GPU, merge their local top-K
 candidates three times in a row through
 
   * the P2P exchange: payloads staged in CUDA IPC slots, read by the merge
@@ -63,11 +63,11 @@ def _worker(rank, world, port, mode, q):
         dist.destroy_process_group()
 
 
+@pytest.mark.parametrize("world", [2, 4, 8])
 @pytest.mark.parametrize("mode", ["p2p", "fused", "torch"])
-def test_sharded_merge_two_gpus(mode):
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs two GPUs")
-    world = 2
+def test_sharded_merge_gpus(mode, world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()  # both ranks rendezvous on it
@@ -146,16 +146,16 @@ def _decode_worker(rank, world, port, mode, q):
         dist.destroy_process_group()
 
 
+@pytest.mark.parametrize("world", [2, 4, 8])
 @pytest.mark.parametrize("mode", ["p2p", "fused"])
-def test_sharded_decode_layer_two_gpus(mode):
-    """Key-sharded decode indexer (each rank scores half of every row's keys;
+def test_sharded_decode_layer_gpus(mode, world):
+    """Key-sharded decode indexer (each rank scores its 1/world share of every row's keys;
     device-sequenced P2P exchange, or NCCL all-gather + fused merge) and
     head-split sparse MLA decode: every rank's global top-K equals the
     oracle's top-K over all keys, and its head slice of o / lse matches the
     oracle (2e-3 relative; bf16 output rounding included in the bound)."""
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs two GPUs")
-    world = 2
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
