@@ -8,21 +8,25 @@
 //
 // One CTA = one query row x up to 4096 positions (fewer when the rows x keys
 // would not fill whole waves of the GPU), in sub-tiles of 128 keys (two
-// pages), 8 warps, two CTAs per SM:
+// pages), 8 warps, two CTAs per SM, software-pipelined one sub-tile deep:
 //   * a page is 64 x 132 = 8,448 contiguous bytes, so each arrives with one
 //     bulk copy (cp.async.bulk, completing on an mbarrier), DSTAGES sub-tiles
-//     ahead;
-//   * all warps expand the staged e4m3 bytes exactly to fp16 into a
-//     128-byte-swizzled key tile (and the key scales into shared memory);
+//     ahead; the page bases come from the block table once per CTA;
+//   * every thread expands half of one key's staged e4m3 bytes exactly to
+//     fp16 and stores them with tcgen05.st straight into the MMA's A operand
+//     in tensor memory (row = key, two fp16 per 32-bit column), double
+//     buffered, so the bytes cross shared memory once;
 //   * one thread issues S^T[128 keys x NQ heads] = K . Q^T as eight M=128,
-//     N=NQ, K=16 tcgen05 MMAs (fp32 accumulation in TMEM);
-//   * each thread of the epilogue owns one key and half of the heads: one
-//     tcgen05.ld, then w * relu(s) summed over its heads, the halves combined
-//     through shared memory, times the key's scale.
+//     N=NQ, K=16 tcgen05 MMAs (A from TMEM, q from shared memory, fp32
+//     accumulation into one of two TMEM accumulators) and goes on;
+//   * while sub-tile i's MMAs run, every thread reads sub-tile i-1's
+//     accumulator for its key (half of the heads): w * relu(s) summed, the
+//     second half parked in shared memory and added, times the key's scale,
+//     one iteration later (after the next block barrier).
 // q and w are loaded once per CTA and the histogram is accumulated in shared
 // memory and added to the global one once per CTA. Every wait is bounded by
 // device time; on expiry the CTA records DSA_ERR_TIMEOUT in the sticky status
-// word, drains its own MMAs, frees TMEM and returns.
+// word, drains its own copies and MMAs, frees TMEM and returns.
 #include <algorithm>
 
 #include "indexer_tc.cuh"
@@ -40,28 +44,28 @@ constexpr int NBIN = 4096;
 constexpr int DP = 64;                        // page size served
 constexpr int DP_BYTES = DP * IDXK_ROW;       // 8,448
 constexpr int DSUB = 128;                     // keys per sub-tile (MMA M)
-constexpr int DSTAGES = 3;                    // staged sub-tiles
+constexpr int DSTAGES = 4;                    // staged sub-tiles
 constexpr int DCTA_KEYS = 4096;               // most positions per CTA
 constexpr int DNT = 256;                      // 8 warps
-constexpr uint32_t KT_REGION = DSUB * 128;    // one 64-dim region of the key tile: 16 KB
+constexpr uint32_t TMEM_COLS = 256;           // A0 | A1 | D0 | D1
+constexpr uint32_t A_COLS = HD / 2;           // 128 fp16 per key: 64 columns
 constexpr uint64_t kWaitTimeoutNs = 2000000000ull;
 
 template <int NQ>
 struct DecodeTcLayout {
   static constexpr uint32_t Q_REGION = NQ * 128;                 // one 64-dim region of q
-  static constexpr uint32_t OFF_K = 0;                           // key tile, 2 regions
-  static constexpr uint32_t OFF_Q = OFF_K + 2 * KT_REGION;       // q, 2 regions
+  static constexpr uint32_t OFF_Q = 0;                           // q, 2 regions
   static constexpr uint32_t OFF_STAGE = OFF_Q + 2 * Q_REGION;    // [DSTAGES][2 pages]
   static constexpr uint32_t OFF_HIST = OFF_STAGE + DSTAGES * 2 * DP_BYTES;
   static constexpr uint32_t OFF_W = OFF_HIST + NBIN * 4;         // [NQ]
-  static constexpr uint32_t OFF_SCALE = OFF_W + NQ * 4;          // [DSUB] key scales
-  static constexpr uint32_t OFF_PART = OFF_SCALE + DSUB * 4;     // [DSUB] second-half head sums
-  static constexpr uint32_t OFF_BASE = OFF_PART + DSUB * 4;      // [DSTAGES][2] int64 page bases
-  static constexpr uint32_t OFF_MBAR = OFF_BASE + DSTAGES * 2 * 8;  // [DSTAGES] copies, mma, done
-  static constexpr uint32_t OFF_SLOT = OFF_MBAR + (DSTAGES + 2) * 8;
+  static constexpr uint32_t OFF_PART = OFF_W + NQ * 4;           // [2][DSUB] second-half head sums
+  static constexpr uint32_t OFF_BASE = OFF_PART + 2 * DSUB * 4;  // [DCTA_KEYS / DP] int64 page bases
+  static constexpr uint32_t OFF_MBAR = OFF_BASE + (DCTA_KEYS / DP) * 8;  // [DSTAGES] copies, [2] mma, drain
+  static constexpr uint32_t OFF_SLOT = OFF_MBAR + (DSTAGES + 3) * 8;
   static constexpr uint32_t BYTES = OFF_SLOT + 16 + 1024;        // + alignment slack
-  static constexpr uint32_t TMEM_COLS = NQ < 32 ? 32 : NQ;
+  static constexpr uint32_t D_COL = 2 * A_COLS;                  // accumulator p at D_COL + p * NQ
   static_assert(Q_REGION % 1024 == 0 && OFF_STAGE % 1024 == 0, "swizzled regions stay 1024-aligned");
+  static_assert(D_COL + 2 * NQ <= TMEM_COLS, "two A tiles and two accumulators fit the allocation");
 };
 
 __device__ __forceinline__ float load_weight(const IndexerDecodeTcArgs& a, int64_t i) {
@@ -92,19 +96,17 @@ __global__ void __launch_bounds__(DNT, 2) indexer_decode_tc_kernel(const Indexer
   const uint32_t raw_base = smem_u32(smem_raw);
   const uint32_t base = (raw_base + 1023u) & ~1023u;
   uint8_t* sm = smem_raw + (base - raw_base);
-  uint8_t* ktile = sm + Lay::OFF_K;
   uint8_t* stage = sm + Lay::OFF_STAGE;
   uint32_t* sHist = reinterpret_cast<uint32_t*>(sm + Lay::OFF_HIST);
   float* sW = reinterpret_cast<float*>(sm + Lay::OFF_W);
-  float* sScale = reinterpret_cast<float*>(sm + Lay::OFF_SCALE);
   float* sPart = reinterpret_cast<float*>(sm + Lay::OFF_PART);
   int64_t* sBase = reinterpret_cast<int64_t*>(sm + Lay::OFF_BASE);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + Lay::OFF_SLOT);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + Lay::OFF_SLOT + 4);
   uint32_t* q_bits = reinterpret_cast<uint32_t*>(sm + Lay::OFF_SLOT + 8);  // largest |q| bf16 pattern
   const uint32_t mb0 = base + Lay::OFF_MBAR;        // copies of stage s at mb0 + 8 s
-  const uint32_t mb_mma = mb0 + 8u * DSTAGES;      // MMAs of a sub-tile done
-  const uint32_t mb_done = mb_mma + 8u;            // drain on abort
+  const uint32_t mb_mma = mb0 + 8u * DSTAGES;      // MMAs of sub-tile i done: mb_mma + 8 (i & 1)
+  const uint32_t mb_done = mb_mma + 16u;           // drain on abort
 
   const int b = blockIdx.x;
   const int p0 = blockIdx.y * a.cta_keys;
@@ -118,10 +120,8 @@ __global__ void __launch_bounds__(DNT, 2) indexer_decode_tc_kernel(const Indexer
   const int nsub = (v_end - p0 + DSUB - 1) / DSUB;
   const int32_t* bt_row = a.bt + (int64_t)b * a.bt_stride;
 
-  // Thread 0: bulk copies of sub-tile i's two pages into stage i % DSTAGES.
-  // Page base codes: row of the page's first key (whole page in the cache);
-  // -1: no key of the page is read; -2: the page runs past the cache end
-  // (keys copied one by one).
+  // Thread 0: bulk copies of sub-tile i's two pages into stage i % DSTAGES,
+  // from the page base codes in sBase.
   auto issue = [&](int i) {
     const int st = i % DSTAGES;
     const uint32_t mb = mb0 + 8u * (uint32_t)st;
@@ -129,19 +129,7 @@ __global__ void __launch_bounds__(DNT, 2) indexer_decode_tc_kernel(const Indexer
     int64_t pb[2];
 #pragma unroll
     for (int j = 0; j < 2; ++j) {
-      const int pos = p0 + DSUB * i + DP * j;
-      pb[j] = -1;
-      if (pos < v_end) {
-        const int blk_i = pos / DP;
-        if (blk_i < a.max_blocks) {
-          const int64_t r = (int64_t)bt_row[blk_i] * DP;
-          if (r >= 0 && r + DP <= a.n_kv_rows)
-            pb[j] = r;
-          else if (r >= 0 && r < a.n_kv_rows)
-            pb[j] = -2;
-        }
-      }
-      sBase[2 * st + j] = pb[j];  // read after the mbarrier wait
+      pb[j] = sBase[2 * i + j];
       if (pb[j] >= 0) bytes += DP_BYTES;
     }
     mbar_arrive_expect_tx(mb, bytes);
@@ -159,14 +147,33 @@ __global__ void __launch_bounds__(DNT, 2) indexer_decode_tc_kernel(const Indexer
     if (lane == 0) {
       for (int s = 0; s < DSTAGES; ++s) mbar_init(mb0 + 8u * s, 1);
       mbar_init(mb_mma, 1);
+      mbar_init(mb_mma + 8u, 1);
       mbar_init(mb_done, 1);
       mbar_init_fence();
       *abort_flag = 0;
     }
     __syncwarp();
-    tmem_alloc(smem_u32(tmem_slot), Lay::TMEM_COLS);
+    tmem_alloc(smem_u32(tmem_slot), TMEM_COLS);
   }
   for (int i = tid; i < NBIN; i += DNT) sHist[i] = 0;
+  // Page base codes of the CTA's pages: row of the page's first key (whole
+  // page in the cache); -1: no key of the page is read; -2: the page runs
+  // past the cache end (keys read one by one).
+  for (int j = tid; j < 2 * nsub; j += DNT) {
+    const int pos = p0 + DP * j;
+    int64_t pb = -1;
+    if (pos < v_end) {
+      const int blk_i = pos / DP;
+      if (blk_i < a.max_blocks) {
+        const int64_t r = (int64_t)bt_row[blk_i] * DP;
+        if (r >= 0 && r + DP <= a.n_kv_rows)
+          pb = r;
+        else if (r >= 0 && r < a.n_kv_rows)
+          pb = -2;
+      }
+    }
+    sBase[j] = pb;
+  }
   // bf16 q beyond fp16's range: the row's q is scaled by 2^-qe for the MMA
   // and every score by 2^qe after it (both exact; relu commutes with them)
   int qe = 0;
@@ -201,114 +208,125 @@ __global__ void __launch_bounds__(DNT, 2) indexer_decode_tc_kernel(const Indexer
   __syncthreads();
   fence_after_sync();
   const uint32_t tmem = *tmem_slot;
+  int n_issued = 0;  // thread 0: sub-tiles whose copies were issued
   if (tid == 0)
-    for (int i = 0; i < DSTAGES && i < nsub; ++i) issue(i);
-  const uint64_t desc_k = sw128_desc(base + Lay::OFF_K, 16, 1024);
+    for (; n_issued < DSTAGES && n_issued < nsub; ++n_issued) issue(n_issued);
   const uint64_t desc_q = sw128_desc(base + Lay::OFF_Q, 16, 1024);
   constexpr uint32_t IDESC = idesc_f16(DSUB, NQ, false, false);
 
+  // this thread: key kq = 32 (warp & 3) + lane of every sub-tile (the TMEM
+  // lane its warp may access), dims / heads half hh
+  const int kq = 32 * (warp & 3) + lane, hh = warp >> 2;
+  const uint32_t lane_base = (uint32_t)(32 * (warp & 3)) << 16;
   bool ok = true;
   bool issued = false;
-  const int sp = warp & 3, half = warp >> 2;  // epilogue: key 32 sp + lane, heads [half NQ/2, +NQ/2)
-  for (int i = 0; i < nsub; ++i) {
-    const int st = i % DSTAGES;
-    const int k0 = p0 + DSUB * i;
-    ok = ok && mbar_wait(mb0 + 8u * (uint32_t)st, (uint32_t)((i / DSTAGES) & 1), abort_flag, err, kWaitTimeoutNs);
-    const uint8_t* sst = stage + 2 * st * DP_BYTES;
-    // expand: item = (key, 16-dim chunk); 4 words in, two 16-byte fp16 chunks out
+  int n_done = 0;        // thread 0: sub-tiles whose copies were seen complete
+  float sc_prev = 0.f, sc_cur = 0.f;  // hh == 0: the key's scale for sub-tiles i-1, i
+  float s_prev = 0.f;    // hh == 0: first-half head sum of sub-tile i-2 (finished at iteration i)
+  for (int it = 0; it < nsub + 2; ++it) {
+    // ---- expand sub-tile it into A[it & 1]
+    float sc_new = 0.f;
+    if (it < nsub) {
+      const int st = it % DSTAGES;
+      ok = ok && mbar_wait(mb0 + 8u * (uint32_t)st, (uint32_t)((it / DSTAGES) & 1), abort_flag, err, kWaitTimeoutNs);
+      if (tid == 0 && ok) n_done = it + 1;
+      const int pos = p0 + DSUB * it + kq;
+      const int j = kq >> 6;
+      const int64_t pbase = sBase[2 * it + j];
+      uint32_t w[16];
 #pragma unroll
-    for (int it = tid; it < DSUB * 8; it += DNT) {
-      const int key = it >> 3, c16 = it & 7;
-      const int j = key >> 6;
-      const int64_t pbase = sBase[2 * st + j];
-      uint32_t w[4] = {0u, 0u, 0u, 0u};
-      float sc = 0.f;
-      if (ok && k0 + key < v_end && pbase != -1) {
-        if (pbase >= 0) {  // the staged page (shared-memory loads)
-          // 132-byte rows are only 4-byte aligned: four 32-bit loads
-          const uint32_t src = smem_u32(sst + j * DP_BYTES + (key & 63) * IDXK_ROW) + 16 * c16;
+      for (int e = 0; e < 16; ++e) w[e] = 0u;
+      if (ok && pos < v_end && pbase != -1) {
+        if (pbase >= 0) {  // the staged page: 132-byte rows are only 4-byte aligned
+          const uint32_t src = smem_u32(stage + (2 * st + j) * DP_BYTES + (kq & 63) * IDXK_ROW) + 64 * hh;
 #pragma unroll
-          for (int e = 0; e < 4; ++e) asm volatile("ld.shared.u32 %0, [%1];" : "=r"(w[e]) : "r"(src + 4 * e));
-          if (c16 == 0)
-            asm volatile("ld.shared.f32 %0, [%1];" : "=f"(sc) : "r"(smem_u32(sst + j * DP_BYTES + (key & 63) * IDXK_ROW) + 128));
+          for (int e = 0; e < 16; ++e) asm volatile("ld.shared.u32 %0, [%1];" : "=r"(w[e]) : "r"(src + 4 * e));
+          if (hh == 0) asm volatile("ld.shared.f32 %0, [%1];" : "=f"(sc_new) : "r"(src + 128));
         } else {  // a page that runs past the cache end: this key's own row, if inside
-          const int pos = k0 + key;
           const int64_t r = (int64_t)bt_row[pos / DP] * DP + (pos % DP);
           if (r < a.n_kv_rows) {
-            const uint32_t* g = reinterpret_cast<const uint32_t*>(a.k + r * IDXK_ROW + 16 * c16);
+            const uint32_t* g = reinterpret_cast<const uint32_t*>(a.k + r * IDXK_ROW + 64 * hh);
 #pragma unroll
-            for (int e = 0; e < 4; ++e) w[e] = __ldg(g + e);
-            if (c16 == 0) sc = __ldg(reinterpret_cast<const float*>(a.k + r * IDXK_ROW + 128));
+            for (int e = 0; e < 16; ++e) w[e] = __ldg(g + e);
+            if (hh == 0) sc_new = __ldg(reinterpret_cast<const float*>(a.k + r * IDXK_ROW + 128));
           }
         }
       }
-      uint32_t hv[8];
+      uint32_t hv[32];
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        e4m3x4_to_half2x2_div256(w[e], hv[2 * e], hv[2 * e + 1]);  // keys / 256, exact
-      }
-      uint8_t* region = ktile + (c16 >> 2) * KT_REGION;
-      *reinterpret_cast<uint4*>(region + sw128_off(key, 2 * (c16 & 3))) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
-      *reinterpret_cast<uint4*>(region + sw128_off(key, 2 * (c16 & 3) + 1)) =
-          make_uint4(hv[4], hv[5], hv[6], hv[7]);
-      if (c16 == 0) sScale[key] = sc * 256.0f;  // the keys' 1/256 undone with their scale
+      for (int e = 0; e < 16; ++e) e4m3x4_to_half2x2_div256(w[e], hv[2 * e], hv[2 * e + 1]);  // keys / 256, exact
+      tmem_st32(tmem + lane_base + (uint32_t)((it & 1) * A_COLS + 32 * hh), hv);
+      tmem_wait_st();
     }
-    fence_proxy_async();
     fence_before_sync();
-    __syncthreads();  // key tile written; stage st fully read
-    if (tid == 0) {
-      if (i + DSTAGES < nsub) issue(i + DSTAGES);
+    __syncthreads();  // A[it & 1] written, stage it consumed; sPart of sub-tile it-2 visible
+    fence_after_sync();
+    // ---- thread 0: the MMAs of sub-tile it, then the freed stage's copies
+    if (tid == 0 && it < nsub) {
       if (ok) {
-        fence_after_sync();
+        const uint32_t a_tm = tmem + (uint32_t)((it & 1) * A_COLS);
+        const uint32_t d_tm = tmem + Lay::D_COL + (uint32_t)((it & 1) * NQ);
 #pragma unroll
-        for (int kb = 0; kb < 2; ++kb)
-#pragma unroll
-          for (int k = 0; k < 4; ++k)
-            mma_f16_ss(tmem, desc_k + ((kb * KT_REGION + 32 * k) >> 4), desc_q + ((kb * Lay::Q_REGION + 32 * k) >> 4),
-                       IDESC, (kb | k) != 0);
-        mma_commit(mb_mma);
+        for (int kk = 0; kk < HD / 16; ++kk)
+          mma_f16_ts(d_tm, a_tm + 8u * kk, desc_q + (((kk >> 2) * Lay::Q_REGION + 32 * (kk & 3)) >> 4), IDESC,
+                     kk != 0);
+        mma_commit(mb_mma + 8u * (uint32_t)(it & 1));
         issued = true;
       }
+      if (ok && n_issued < nsub) issue(n_issued++);
     }
-    // the commit is skipped only after an abort, which every later wait sees
-    ok = ok && mbar_wait(mb_mma, (uint32_t)(i & 1), abort_flag, err, kWaitTimeoutNs);
-    ok = __all_sync(0xffffffffu, ok);  // tcgen05.ld below is warp-wide
-    fence_after_sync();
-    float s = 0.f;
-    if (ok) {
-      uint32_t acc[NQ / 2];
-      tmem_ld_cols<NQ / 2>(tmem + ((uint32_t)(32 * sp) << 16) + (uint32_t)(half * (NQ / 2)), acc);
-      tmem_wait_ld();
-#pragma unroll
-      for (int h = 0; h < NQ / 2; ++h) s += sW[half * (NQ / 2) + h] * fmaxf(__uint_as_float(acc[h]), 0.f);
-    }
-    const int key = 32 * sp + lane;
-    if (half == 1) sPart[key] = s;
-    __syncthreads();
-    if (half == 0) {
-      const int pos = k0 + key;
+    // ---- finish sub-tile it-2: both head halves, scale, histogram, store
+    if (it >= 2 && hh == 0) {
+      const int pos = p0 + DSUB * (it - 2) + kq;
       if (pos < v_end) {
-        const float v = (s + sPart[key]) * sScale[key] * qmul;
+        const float v = (s_prev + sPart[((it - 2) & 1) * DSUB + kq]) * (sc_prev * 256.0f) * qmul;
         atomicAdd(&sHist[monotone32(v) >> 20], 1u);
         score_row[pos] = v;
       }
     }
-    fence_before_sync();
-    __syncthreads();  // the key tile, scales and partial sums are rewritten next
+    // ---- half-head sums of sub-tile it-1 from its accumulator
+    if (it >= 1 && it <= nsub) {
+      const int i1 = it - 1;
+      ok = ok && mbar_wait(mb_mma + 8u * (uint32_t)(i1 & 1), (uint32_t)((i1 >> 1) & 1), abort_flag, err,
+                           kWaitTimeoutNs);
+      ok = __all_sync(0xffffffffu, ok);  // tcgen05.ld below is warp-wide
+      fence_after_sync();
+      float s = 0.f;
+      if (ok) {
+        uint32_t acc[NQ / 2];
+        tmem_ld_cols<NQ / 2>(tmem + lane_base + Lay::D_COL + (uint32_t)((i1 & 1) * NQ + hh * (NQ / 2)), acc);
+        tmem_wait_ld();
+#pragma unroll
+        for (int h = 0; h < NQ / 2; ++h) s += sW[hh * (NQ / 2) + h] * fmaxf(__uint_as_float(acc[h]), 0.f);
+      }
+      if (hh == 1)
+        sPart[(i1 & 1) * DSUB + kq] = s;
+      else
+        s_prev = s;
+    }
+    if (hh == 0) {  // the scales ride along with the sub-tiles they belong to
+      sc_prev = sc_cur;
+      sc_cur = sc_new;
+    }
   }
+  __syncthreads();  // the last sub-tile's histogram counts are in
   for (int i = tid; i < NBIN; i += DNT) {
     const uint32_t c = sHist[i];
     if (c && a.hist) atomicAdd(a.hist + (int64_t)b * NBIN + i, (int)c);
   }
-  if (tid == 0 && issued && *abort_flag) {  // drain this thread's MMAs before TMEM is freed
-    mma_commit(mb_done);
-    mbar_wait_drain(mb_done, 0, kWaitTimeoutNs);
+  if (tid == 0 && *abort_flag) {  // drain this CTA's copies and MMAs before its memory is released
+    for (int j = n_done; j < n_issued; ++j)
+      mbar_wait_drain(mb0 + 8u * (uint32_t)(j % DSTAGES), (uint32_t)((j / DSTAGES) & 1), kWaitTimeoutNs);
+    if (issued) {
+      mma_commit(mb_done);
+      mbar_wait_drain(mb_done, 0, kWaitTimeoutNs);
+    }
   }
   fence_before_sync();
   __syncthreads();
   if (warp == 0) {
     fence_after_sync();
-    tmem_dealloc(tmem, Lay::TMEM_COLS);
+    tmem_dealloc(tmem, TMEM_COLS);
   }
 }
 
