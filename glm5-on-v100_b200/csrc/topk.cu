@@ -27,6 +27,8 @@
 #include <cooperative_groups.h>
 
 #include "common.cuh"
+#include "sparse_mla.cuh"
+#include "tc_common.cuh"
 
 namespace cg = cooperative_groups;
 
@@ -69,6 +71,7 @@ struct TopkParams {
   int64_t slot_bytes;
   int64_t timeout_ns;
   int32_t* err;
+  int32_t* dev_err;  // the library's sticky device status word (staging waits)
 };
 
 // Where the selected positions of one row go.
@@ -100,7 +103,10 @@ struct TopkSmem {
   uint32_t above, total;
   int ok;
   uint32_t cl_cnt[8];  // cluster mode: every CTA's (sure | candidates << 16) counts
-  uint32_t cl_nsel;    // cluster mode (rank 0): selected candidates
+  int cl_ok[8];        // cluster mode: every CTA's staging waits succeeded
+  uint32_t cl_lo;      // cluster mode: selected candidates before this CTA's range
+  uint32_t cl_nsel;    // cluster mode: selected candidates in this CTA's range
+  uint32_t cl_total;   // cluster mode: selected candidates of the row
 };
 
 // Block-wide: find the largest bin T with count(bins >= T) >= need, scanning
@@ -261,13 +267,18 @@ __device__ void select_global(const float* row, int n, int K, uint32_t T1, uint3
 // position order in s.cand_key / s.cand_pos): two more radix levels (12 + 8
 // bits), then the selected candidates (key > kth, or == kth among the first
 // such keys) compacted in position order into s.sel. Returns their count.
+// With have_hist2, s.hist already holds the candidates' level-2 histogram
+// (bits 19..8), built by the caller.
 template <int NT>
-__device__ uint32_t resolve_candidates(TopkSmem& s, uint32_t n_cand, uint32_t need2, uint32_t T1) {
+__device__ uint32_t resolve_candidates(TopkSmem& s, uint32_t n_cand, uint32_t need2, uint32_t T1,
+                                       bool have_hist2 = false) {
   const int tid = threadIdx.x;
-  for (int i = tid; i < NBIN1; i += NT) s.hist[i] = 0;
-  __syncthreads();
-  for (int i = tid; i < (int)n_cand; i += NT) atomicAdd(&s.hist[(s.cand_key[i] >> 8) & 0xFFFu], 1u);
-  __syncthreads();
+  if (!have_hist2) {
+    for (int i = tid; i < NBIN1; i += NT) s.hist[i] = 0;
+    __syncthreads();
+    for (int i = tid; i < (int)n_cand; i += NT) atomicAdd(&s.hist[(s.cand_key[i] >> 8) & 0xFFFu], 1u);
+    __syncthreads();
+  }
   find_threshold<NT>(s.hist, NBIN1, need2, s.warp, &s.T, &s.above);
   const uint32_t T2 = (uint32_t)s.T;
   const uint32_t need3 = need2 - s.above;
@@ -517,22 +528,47 @@ __global__ void __launch_bounds__(NT, 1024 / NT) topk_rows_kernel(const TopkPara
 
 // ---------------------------------------------------------- cluster mode
 // Few long rows (decode batches with the logits kernel's histogram): the CL
-// CTAs of one thread-block cluster share a row, each sweeping a contiguous
-// CL-th of it, so a batch of 8 rows keeps 64 SMs busy instead of 8. Every CTA
-// derives the same threshold bin T1 from the row's histogram; after a count
-// pass the CTAs exchange their counts through distributed shared memory,
-// write their "sure" positions to their own shared memory and their
-// candidates (bin T1) into rank 0's candidate lists at their prefix offsets,
-// in position order. Rank 0 resolves the K-th key among the candidates;
-// every CTA then emits its own sure positions and the selected candidates
-// that fall in its range, ranked against rank 0's selected list and its own
-// sure list. Rows whose bin T1 overflows the candidate buffer are done by
-// rank 0 alone with the one-CTA path.
+// CTAs of one thread-block cluster share a row, each owning a contiguous
+// CL-th of it, so a batch of 8 rows keeps 64 SMs busy instead of 8.
+//   * At entry every CTA starts bulk copies of the row's histogram and of its
+//     own range of scores into shared memory (when the range fits STAGE_F
+//     floats and the row is 16-byte aligned; else both passes below read
+//     global memory), so the scores are read from global memory once, with
+//     all of the CTA's loads in flight together.
+//   * Every CTA derives the same threshold bin T1 from the histogram; a count
+//     pass gives each CTA its sure (bin > T1) and candidate (bin == T1)
+//     counts, exchanged through distributed shared memory.
+//   * The write pass keeps the sure positions in the CTA's own shared memory
+//     and writes the candidates into rank 0's candidate lists at their
+//     prefix offsets, in position order, adding each to rank 0's level-2
+//     histogram (bits 19..8) with a distributed shared-memory atomic.
+//   * Rank 0 resolves the K-th key among the candidates, then pushes to every
+//     CTA the selected candidates of its range (and their offset); every CTA
+//     then emits its sure and selected positions from its own shared memory.
+// Rows whose bin T1 overflows the candidate buffer are done by rank 0 alone
+// with the one-CTA path. Every CTA of a cluster takes the same sequence of
+// cluster barriers on every path (no CTA waits on a barrier another skips).
 constexpr int CL = 8;
 constexpr int NT_CL = 512;
+constexpr int STAGE_F = 28672;                  // staged scores per CTA (112 KB)
+constexpr int STAGE_CHUNK = 4096;               // floats per bulk copy
+constexpr int NCHUNK = STAGE_F / STAGE_CHUNK;   // 7
+constexpr uint64_t kStageTimeoutNs = 2000000000ull;
+
+struct ClusterStage {
+  uint64_t mbar[NCHUNK + 1];  // score chunks, histogram
+  int abort;
+  int pad[3];
+  float sc[STAGE_F];
+};
+constexpr size_t CLUSTER_SMEM = (sizeof(TopkSmem) + 15) / 16 * 16 + sizeof(ClusterStage);
+
+__device__ __forceinline__ ClusterStage& cluster_stage(unsigned char* smem_raw) {
+  return *reinterpret_cast<ClusterStage*>(smem_raw + (sizeof(TopkSmem) + 15) / 16 * 16);
+}
 
 template <int NT>
-__device__ void topk_row_cluster(const TopkParams& p, int b, const Emit& out, TopkSmem& s,
+__device__ void topk_row_cluster(const TopkParams& p, int b, const Emit& out, TopkSmem& s, ClusterStage& cs,
                                  cg::cluster_group& cl, int rank) {
   constexpr int NWARP = NT / 32;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -547,31 +583,66 @@ __device__ void topk_row_cluster(const TopkParams& p, int b, const Emit& out, To
     }
     return;
   }
-  for (int i = tid; i < NBIN1; i += NT) s.hist[i] = (uint32_t)p.hist[(int64_t)b * NBIN1 + i];
-  __syncthreads();
+  const bool vec = (reinterpret_cast<uintptr_t>(row) & 15) == 0;
+  const int per = ((n + CL * 128 - 1) / (CL * 128)) * 128;  // positions per CTA, 128-aligned
+  const int r0 = min(n, rank * per), r1 = min(n, r0 + per);
+  const int r1v = r0 + ((r1 - r0) & ~3);          // staged part [r0, r1v); the tail < 4 from global
+  const bool staged = vec && (r1 - r0) <= STAGE_F;  // same for every CTA of the row (n, per, row)
+  const int nchunk = staged ? (r1v - r0 + STAGE_CHUNK - 1) / STAGE_CHUNK : 0;
+
+  // ---- bulk copies: histogram row and this CTA's scores
+  const uint32_t mb = smem_u32(&cs.mbar[0]);
+  if (tid == 0) {
+    for (int c = 0; c <= NCHUNK; ++c) tc::mbar_init(mb + 8u * c, 1);
+    tc::mbar_init_fence();
+    cs.abort = 0;
+    tc::mbar_arrive_expect_tx(mb + 8u * NCHUNK, NBIN1 * 4);
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     smem_u32(s.hist)),
+                 "l"(p.hist + (int64_t)b * NBIN1), "r"((uint32_t)(NBIN1 * 4)), "r"(mb + 8u * NCHUNK)
+                 : "memory");
+    for (int c = 0; c < nchunk; ++c) {
+      const int c0 = r0 + c * STAGE_CHUNK, c1 = min(r1v, c0 + STAGE_CHUNK);
+      const uint32_t bytes = (uint32_t)(c1 - c0) * 4u;
+      tc::mbar_arrive_expect_tx(mb + 8u * c, bytes);
+      asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                       smem_u32(cs.sc + (c0 - r0))),
+                   "l"(row + c0), "r"(bytes), "r"(mb + 8u * c)
+                   : "memory");
+    }
+  }
+  __syncthreads();  // barriers initialised before anyone waits on them
+  bool ok = tc::mbar_wait(mb + 8u * NCHUNK, 0, &cs.abort, p.dev_err, kStageTimeoutNs);
   find_threshold<NT>(s.hist, NBIN1, (uint32_t)K, s.warp, &s.T, &s.above);
   const uint32_t T1 = (uint32_t)s.T;
   const uint32_t need2 = (uint32_t)K - s.above;
   const uint32_t cnt1 = s.hist[T1];
   const bool overflow = cnt1 > (uint32_t)CAP || s.above > (uint32_t)KMAX;
+  for (int c = 0; c < nchunk; ++c) ok = tc::mbar_wait(mb + 8u * c, 0, &cs.abort, p.dev_err, kStageTimeoutNs) && ok;
   __syncthreads();
-  if (overflow) {  // the same decision in every CTA (same histogram)
-    cl.sync();     // every CTA has read the histogram before rank 0 may clear it
-    if (rank == 0) topk_row<NT>(p, b, out, s);
-    return;
-  }
-  const bool vec = (reinterpret_cast<uintptr_t>(row) & 15) == 0;
-  const int per = ((n + CL * 128 - 1) / (CL * 128)) * 128;  // positions per CTA, 128-aligned
-  const int r0 = min(n, rank * per), r1 = min(n, r0 + per);
+  if (rank == 0 && !overflow)  // rank 0's histogram becomes the candidates' level-2 histogram
+    for (int i = tid; i < NBIN1; i += NT) s.hist[i] = 0;
   const int run = ((r1 - r0 + NWARP * 128 - 1) / (NWARP * 128)) * 128;
   const int w0 = r0 + warp * run, w1 = min(r1, w0 + run);
+  // four keys at positions i..i+3 of this CTA's range (staged or global)
+  auto keys4 = [&](int i, uint32_t (&k)[4]) {
+    if (staged && i + 4 <= r1v) {
+      const float4 v = *reinterpret_cast<const float4*>(cs.sc + (i - r0));
+      k[0] = monotone32(v.x);
+      k[1] = monotone32(v.y);
+      k[2] = monotone32(v.z);
+      k[3] = monotone32(v.w);
+    } else {
+      load4(row, i, w1, vec, k);
+    }
+  };
 
   // count pass
   uint32_t ns = 0, nc = 0;
   for (int i0 = w0; i0 < w1; i0 += 128 * SWEEP_U) {
     uint32_t kq[SWEEP_U][4];
 #pragma unroll
-    for (int u = 0; u < SWEEP_U; ++u) load4(row, i0 + 128 * u + 4 * lane, w1, vec, kq[u]);
+    for (int u = 0; u < SWEEP_U; ++u) keys4(i0 + 128 * u + 4 * lane, kq[u]);
 #pragma unroll
     for (int u = 0; u < SWEEP_U; ++u) {
       const int i = i0 + 128 * u + 4 * lane;
@@ -588,7 +659,7 @@ __device__ void topk_row_cluster(const TopkParams& p, int b, const Emit& out, To
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) packed += __shfl_xor_sync(0xffffffffu, packed, off);
   if (lane == 0) s.warp_off[warp] = packed;
-  __syncthreads();
+  const int cta_ok = __syncthreads_and(ok ? 1 : 0);
   if (warp == 0) {
     const uint32_t v = lane < NWARP ? s.warp_off[lane] : 0u;
     uint32_t inc_s = v & 0xFFFFu, inc_c = v >> 16;
@@ -604,10 +675,29 @@ __device__ void topk_row_cluster(const TopkParams& p, int b, const Emit& out, To
     if (lane < NWARP) s.warp[lane] = (inc_s - (v & 0xFFFFu)) | ((inc_c - (v >> 16)) << 16);
     if (lane == NWARP - 1) {
       const uint32_t tot = inc_s | (inc_c << 16);
-      for (int r = 0; r < CL; ++r) *cl.map_shared_rank(&s.cl_cnt[rank], r) = tot;
+      for (int r = 0; r < CL; ++r) {
+        *cl.map_shared_rank(&s.cl_cnt[rank], r) = tot;
+        *cl.map_shared_rank(&s.cl_ok[rank], r) = cta_ok;
+      }
     }
   }
-  cl.sync();  // counts exchanged; every CTA has read the histogram
+  cl.sync();  // counts and staging verdicts exchanged; every CTA has read the histogram
+  // From here every branch is uniform over the cluster: the verdicts are the
+  // same everywhere, and with every copy complete so is the histogram.
+  bool row_ok = true;
+#pragma unroll
+  for (int r = 0; r < CL; ++r) row_ok = row_ok && s.cl_ok[r] != 0;
+  if (!row_ok) {  // a staging wait expired (recorded in the status word): nothing is emitted
+    if (tid == 0 && !ok)  // this CTA's copies may still be in flight: drain them (bounded) first
+      for (int c = 0; c <= NCHUNK; ++c)
+        if (c < nchunk || c == NCHUNK) tc::mbar_wait_drain(mb + 8u * c, 0, kStageTimeoutNs);
+    __syncthreads();
+    return;
+  }
+  if (overflow) {       // rank 0 alone, from global memory (it reads the histogram, then clears it)
+    if (rank == 0) topk_row<NT>(p, b, out, s);
+    return;
+  }
   if (rank == 0 && p.hist_clear)
     for (int i = tid; i < NBIN1; i += NT) p.hist_clear[(int64_t)b * NBIN1 + i] = 0;
   uint32_t sure_base = 0, cand_base = 0, n_cand = 0;
@@ -624,32 +714,33 @@ __device__ void topk_row_cluster(const TopkParams& p, int b, const Emit& out, To
   n_cand = min(n_cand, (uint32_t)CAP);
   uint32_t* key0 = cl.map_shared_rank(s.cand_key, 0);
   int32_t* pos0 = cl.map_shared_rank(s.cand_pos, 0);
+  uint32_t* hist0 = cl.map_shared_rank(s.hist, 0);
 
   // write pass: sure positions here, candidates into rank 0, in order
   uint32_t off_s = s.warp[warp] & 0xFFFFu, off_c = cand_base + (s.warp[warp] >> 16);
   for (int i0 = w0; i0 < w1; i0 += 128 * SWEEP_U) {
     uint32_t kq[SWEEP_U][4];
 #pragma unroll
-    for (int u = 0; u < SWEEP_U; ++u) load4(row, i0 + 128 * u + 4 * lane, w1, vec, kq[u]);
+    for (int u = 0; u < SWEEP_U; ++u) keys4(i0 + 128 * u + 4 * lane, kq[u]);
 #pragma unroll
     for (int u = 0; u < SWEEP_U; ++u) {
       const int i = i0 + 128 * u + 4 * lane;
       const uint32_t* k = kq[u];
-      uint32_t cs = 0, cc = 0;
+      uint32_t cs4 = 0, cc = 0;
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         if (i + e >= w1) continue;
-        cs += (k[e] >> 20) > T1;
+        cs4 += (k[e] >> 20) > T1;
         cc += (k[e] >> 20) == T1;
       }
-      uint32_t inc = cs | (cc << 16);
+      uint32_t inc = cs4 | (cc << 16);
 #pragma unroll
       for (int off = 1; off < 32; off <<= 1) {
         const uint32_t up = __shfl_up_sync(0xffffffffu, inc, off);
         if (lane >= off) inc += up;
       }
       const uint32_t tot = __shfl_sync(0xffffffffu, inc, 31);
-      const uint32_t ex = inc - (cs | (cc << 16));
+      const uint32_t ex = inc - (cs4 | (cc << 16));
       uint32_t ps = off_s + (ex & 0xFFFFu), pc = off_c + (ex >> 16);
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
@@ -662,6 +753,7 @@ __device__ void topk_row_cluster(const TopkParams& p, int b, const Emit& out, To
           if (pc < (uint32_t)CAP) {
             key0[pc] = k[e];
             pos0[pc] = i + e;
+            atomicAdd(hist0 + ((k[e] >> 8) & 0xFFFu), 1u);
           }
           ++pc;
         }
@@ -670,20 +762,25 @@ __device__ void topk_row_cluster(const TopkParams& p, int b, const Emit& out, To
       off_c += tot >> 16;
     }
   }
-  cl.sync();  // all candidates have landed in rank 0
+  cl.sync();  // all candidates and the level-2 histogram have landed in rank 0
   if (rank == 0) {
-    const uint32_t n_sel = resolve_candidates<NT>(s, n_cand, need2, T1);
-    if (tid == 0) s.cl_nsel = n_sel;
+    const uint32_t n_sel = resolve_candidates<NT>(s, n_cand, need2, T1, true);
+    // push every CTA its selected candidates (ascending) and their offset
+    for (int q = warp; q < CL; q += NWARP) {
+      const int q0 = min(n, q * per), q1 = min(n, q0 + per);
+      const int lo = count_below(s.sel, (int)n_sel, q0), hi = count_below(s.sel, (int)n_sel, q1);
+      TopkSmem* d = cl.map_shared_rank(&s, q);
+      for (int j = lane; j < hi - lo; j += 32) d->cand_pos[j] = s.sel[lo + j];
+      if (lane == 0) {
+        d->cl_lo = (uint32_t)lo;
+        d->cl_nsel = (uint32_t)(hi - lo);
+        d->cl_total = n_sel;
+      }
+    }
   }
-  cl.sync();  // rank 0's selected list is ready
-  const int32_t* sel0 = cl.map_shared_rank(s.sel, 0);
-  const int n_sel = (int)*cl.map_shared_rank(&s.cl_nsel, 0);
-  const int lo = count_below(sel0, n_sel, r0), hi = count_below(sel0, n_sel, r1);
-  // this CTA's selected candidates, copied next to its sure list
-  int32_t* mine = s.cand_pos;  // rank 0's candidates are consumed; other CTAs never used theirs
-  for (int j = tid; j < hi - lo; j += NT) mine[j] = sel0[lo + j];
-  __syncthreads();
-  const int nm = hi - lo;
+  cl.sync();  // every CTA holds its selected candidates; no shared memory of another CTA is used after this
+  const int lo = (int)s.cl_lo, nm = (int)s.cl_nsel;
+  const int32_t* mine = s.cand_pos;
   const int n_my_sure = (int)min(my_sure, (uint32_t)KMAX);
   for (int i = tid; i < n_my_sure; i += NT) {
     const int32_t P = s.sure[i];
@@ -696,16 +793,16 @@ __device__ void topk_row_cluster(const TopkParams& p, int b, const Emit& out, To
     if (o < K) out(o, P);
   }
   if (rank == CL - 1) {  // only for an inconsistent histogram: pad the tail
-    int total = 0;
+    int total = (int)s.cl_total;
     for (int r = 0; r < CL; ++r) total += (int)(s.cl_cnt[r] & 0xFFFFu);
-    for (int i = total + n_sel + tid; i < K; i += NT) out(i, -1);
+    for (int i = total + tid; i < K; i += NT) out(i, -1);
   }
-  cl.sync();  // no CTA leaves while another still reads rank 0's lists
 }
 
 __global__ void __launch_bounds__(NT_CL, 1) topk_cluster_kernel(const TopkParams p) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   TopkSmem& s = *reinterpret_cast<TopkSmem*>(smem_raw);
+  ClusterStage& cs = cluster_stage(smem_raw);
   cg::cluster_group cl = cg::this_cluster();
   const int rank = (int)cl.block_rank();
   const int b = blockIdx.y;
@@ -737,7 +834,7 @@ __global__ void __launch_bounds__(NT_CL, 1) topk_cluster_kernel(const TopkParams
     e.idx = p.idx + (int64_t)b * p.idx_stride;
   }
   if (ok) {
-    topk_row_cluster<NT_CL>(p, b, e, s, cl, rank);
+    topk_row_cluster<NT_CL>(p, b, e, s, cs, cl, rank);
   } else if (p.hist_clear && rank == 0) {
     for (int i = tid; i < NBIN1; i += NT_CL) p.hist_clear[(int64_t)b * NBIN1 + i] = 0;
   }
@@ -775,13 +872,13 @@ int run_topk(const TopkParams& p, int B, cudaStream_t s) {
                                (int)sizeof(TopkSmem));
     if (e == cudaSuccess)
       e = cudaFuncSetAttribute(topk_cluster_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               (int)sizeof(TopkSmem));
+                               (int)CLUSTER_SMEM);
     g_status[dev] = (int)e;
     if (e == cudaSuccess) {  // can clusters of CL such CTAs be resident at all?
       cudaLaunchConfig_t cfg{};
       cfg.gridDim = dim3(CL, 1, 1);
       cfg.blockDim = dim3(NT_CL);
-      cfg.dynamicSmemBytes = sizeof(TopkSmem);
+      cfg.dynamicSmemBytes = CLUSTER_SMEM;
       cudaLaunchAttribute attr{};
       attr.id = cudaLaunchAttributeClusterDimension;
       attr.val.clusterDim.x = CL;
@@ -802,11 +899,15 @@ int run_topk(const TopkParams& p, int B, cudaStream_t s) {
     return DSA_ERR_CUDA;
   }
   // few long rows with the logits kernel's histogram: a cluster of CL CTAs per row
-  if (p.hist && g_cluster_ok[dev] && B < sm_count(dev) && p.max_kv >= CL * 1024 && p.K <= KMAX) {
+  if (p.hist && (reinterpret_cast<uintptr_t>(p.hist) & 15) == 0 && g_cluster_ok[dev] && B < sm_count(dev) &&
+      p.max_kv >= CL * 1024 && p.K <= KMAX) {
+    TopkParams q = p;
+    const int st = tc_error_word(dev, &q.dev_err);
+    if (st != DSA_OK) return st;
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(CL, B, 1);
     cfg.blockDim = dim3(NT_CL);
-    cfg.dynamicSmemBytes = sizeof(TopkSmem);
+    cfg.dynamicSmemBytes = CLUSTER_SMEM;
     cfg.stream = s;
     cudaLaunchAttribute attr{};
     attr.id = cudaLaunchAttributeClusterDimension;
@@ -815,7 +916,7 @@ int run_topk(const TopkParams& p, int B, cudaStream_t s) {
     attr.val.clusterDim.z = 1;
     cfg.attrs = &attr;
     cfg.numAttrs = 1;
-    const cudaError_t e = cudaLaunchKernelEx(&cfg, topk_cluster_kernel, p);
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, topk_cluster_kernel, q);
     if (e != cudaSuccess) {
       set_error("topk_cluster_kernel launch: %s", cudaGetErrorString(e));
       return DSA_ERR_CUDA;

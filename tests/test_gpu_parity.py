@@ -629,11 +629,13 @@ def cluster_topk_rows(rng, S):
     return s, lens
 
 
-@pytest.mark.parametrize("S", [9000, 70000, 180224])
+@pytest.mark.parametrize("S", [9000, 9001, 70000, 180224, 240000])
 def test_decode_topk_cluster_mode_exact(dsa, S):
     """Few long rows with the fused histogram run as a cluster of CTAs per row;
     exact (lowest-position ties, ascending, -1 padded) and the histogram is
-    left as given (sm70_decode_topk does not clear it)."""
+    left as given (sm70_decode_topk does not clear it). S = 9001 leaves most
+    rows off 16-byte alignment and 240000 gives each CTA more scores than it
+    stages in shared memory: both read the scores from global memory."""
     rng = np.random.default_rng(S)
     s, lens = cluster_topk_rows(rng, S)
     K = 2048
