@@ -8,7 +8,8 @@
 //
 // One CTA = one query row x up to 4096 positions (fewer when the rows x keys
 // would not fill whole waves of the GPU), in sub-tiles of 128 keys (two
-// pages), 8 warps, two CTAs per SM, software-pipelined one sub-tile deep:
+// pages), 8 worker warps + one issuer warp, two CTAs per SM, software-pipelined
+// one sub-tile deep:
 //   * a page is 64 x 132 = 8,448 contiguous bytes, so each arrives with one
 //     bulk copy (cp.async.bulk, completing on an mbarrier), DSTAGES sub-tiles
 //     ahead; the page bases come from the block table once per CTA;
@@ -16,9 +17,10 @@
 //     fp16 and stores them with tcgen05.st straight into the MMA's A operand
 //     in tensor memory (row = key, two fp16 per 32-bit column), double
 //     buffered, so the bytes cross shared memory once;
-//   * one thread issues S^T[128 keys x NQ heads] = K . Q^T as eight M=128,
-//     N=NQ, K=16 tcgen05 MMAs (A from TMEM, q from shared memory, fp32
-//     accumulation into one of two TMEM accumulators) and goes on;
+//   * one thread of the issuer warp issues S^T[128 keys x NQ heads] = K . Q^T
+//     as eight M=128, N=NQ, K=16 tcgen05 MMAs (A from TMEM, q from shared
+//     memory, fp32 accumulation into one of two TMEM accumulators), then the
+//     copies of the stage just freed, while the workers move on;
 //   * while sub-tile i's MMAs run, every thread reads sub-tile i-1's
 //     accumulator for its key (half of the heads): w * relu(s) summed, the
 //     second half parked in shared memory and added, times the key's scale,
@@ -46,7 +48,9 @@ constexpr int DP_BYTES = DP * IDXK_ROW;       // 8,448
 constexpr int DSUB = 128;                     // keys per sub-tile (MMA M)
 constexpr int DSTAGES = 4;                    // staged sub-tiles
 constexpr int DCTA_KEYS = 4096;               // most positions per CTA
-constexpr int DNT = 256;                      // 8 warps
+constexpr int NWORK = 256;                    // 8 warps: expansion and epilogue
+constexpr int ISSUER = NWORK;                 // warp 8, lane 0: MMAs and copies
+constexpr int DNT = NWORK + 32;
 constexpr uint32_t TMEM_COLS = 256;           // A0 | A1 | D0 | D1
 constexpr uint32_t A_COLS = HD / 2;           // 128 fp16 per key: 64 columns
 constexpr uint64_t kWaitTimeoutNs = 2000000000ull;
@@ -208,8 +212,8 @@ __global__ void __launch_bounds__(DNT, 2) indexer_decode_tc_kernel(const Indexer
   __syncthreads();
   fence_after_sync();
   const uint32_t tmem = *tmem_slot;
-  int n_issued = 0;  // thread 0: sub-tiles whose copies were issued
-  if (tid == 0)
+  int n_issued = 0;  // issuer: sub-tiles whose copies were issued
+  if (tid == ISSUER)
     for (; n_issued < DSTAGES && n_issued < nsub; ++n_issued) issue(n_issued);
   const uint64_t desc_q = sw128_desc(base + Lay::OFF_Q, 16, 1024);
   constexpr uint32_t IDESC = idesc_f16(DSUB, NQ, false, false);
@@ -217,19 +221,21 @@ __global__ void __launch_bounds__(DNT, 2) indexer_decode_tc_kernel(const Indexer
   // this thread: key kq = 32 (warp & 3) + lane of every sub-tile (the TMEM
   // lane its warp may access), dims / heads half hh
   const int kq = 32 * (warp & 3) + lane, hh = warp >> 2;
+  const bool worker = tid < NWORK;
   const uint32_t lane_base = (uint32_t)(32 * (warp & 3)) << 16;
   bool ok = true;
   bool issued = false;
-  int n_done = 0;        // thread 0: sub-tiles whose copies were seen complete
+  volatile int* n_done = abort_flag + 2;  // thread 0: sub-tiles whose copies were seen complete
+  if (tid == 0) *n_done = 0;
   float sc_prev = 0.f, sc_cur = 0.f;  // hh == 0: the key's scale for sub-tiles i-1, i
   float s_prev = 0.f;    // hh == 0: first-half head sum of sub-tile i-2 (finished at iteration i)
   for (int it = 0; it < nsub + 2; ++it) {
     // ---- expand sub-tile it into A[it & 1]
     float sc_new = 0.f;
-    if (it < nsub) {
+    if (it < nsub && worker) {
       const int st = it % DSTAGES;
       ok = ok && mbar_wait(mb0 + 8u * (uint32_t)st, (uint32_t)((it / DSTAGES) & 1), abort_flag, err, kWaitTimeoutNs);
-      if (tid == 0 && ok) n_done = it + 1;
+      if (tid == 0 && ok) *n_done = it + 1;
       const int pos = p0 + DSUB * it + kq;
       const int j = kq >> 6;
       const int64_t pbase = sBase[2 * it + j];
@@ -261,8 +267,10 @@ __global__ void __launch_bounds__(DNT, 2) indexer_decode_tc_kernel(const Indexer
     fence_before_sync();
     __syncthreads();  // A[it & 1] written, stage it consumed; sPart of sub-tile it-2 visible
     fence_after_sync();
-    // ---- thread 0: the MMAs of sub-tile it, then the freed stage's copies
-    if (tid == 0 && it < nsub) {
+    // ---- issuer: the MMAs of sub-tile it, then the freed stage's copies; the
+    // workers go on with the epilogue of sub-tile it-1 meanwhile
+    if (tid == ISSUER && it < nsub) {
+      ok = ok && *abort_flag == 0;
       if (ok) {
         const uint32_t a_tm = tmem + (uint32_t)((it & 1) * A_COLS);
         const uint32_t d_tm = tmem + Lay::D_COL + (uint32_t)((it & 1) * NQ);
@@ -285,7 +293,7 @@ __global__ void __launch_bounds__(DNT, 2) indexer_decode_tc_kernel(const Indexer
       }
     }
     // ---- half-head sums of sub-tile it-1 from its accumulator
-    if (it >= 1 && it <= nsub) {
+    if (worker && it >= 1 && it <= nsub) {
       const int i1 = it - 1;
       ok = ok && mbar_wait(mb_mma + 8u * (uint32_t)(i1 & 1), (uint32_t)((i1 >> 1) & 1), abort_flag, err,
                            kWaitTimeoutNs);
@@ -314,8 +322,8 @@ __global__ void __launch_bounds__(DNT, 2) indexer_decode_tc_kernel(const Indexer
     const uint32_t c = sHist[i];
     if (c && a.hist) atomicAdd(a.hist + (int64_t)b * NBIN + i, (int)c);
   }
-  if (tid == 0 && *abort_flag) {  // drain this CTA's copies and MMAs before its memory is released
-    for (int j = n_done; j < n_issued; ++j)
+  if (tid == ISSUER && *abort_flag) {  // drain this CTA's copies and MMAs before its memory is released
+    for (int j = *n_done; j < n_issued; ++j)
       mbar_wait_drain(mb0 + 8u * (uint32_t)(j % DSTAGES), (uint32_t)((j / DSTAGES) & 1), kWaitTimeoutNs);
     if (issued) {
       mma_commit(mb_done);
