@@ -8,23 +8,25 @@
 //
 // One CTA = one query row x up to 4096 positions (fewer when the rows x keys
 // would not fill whole waves of the GPU), in sub-tiles of 128 keys (two
-// pages), 8 worker warps + one issuer warp, two CTAs per SM, software-pipelined
-// one sub-tile deep:
-//   * a page is 64 x 132 = 8,448 contiguous bytes, so each arrives with one
-//     bulk copy (cp.async.bulk, completing on an mbarrier), DSTAGES sub-tiles
-//     ahead; the page bases come from the block table once per CTA;
-//   * every thread expands half of one key's staged e4m3 bytes exactly to
-//     fp16 and stores them with tcgen05.st straight into the MMA's A operand
-//     in tensor memory (row = key, two fp16 per 32-bit column), double
-//     buffered, so the bytes cross shared memory once;
-//   * one thread of the issuer warp issues S^T[128 keys x NQ heads] = K . Q^T
-//     as eight M=128, N=NQ, K=16 tcgen05 MMAs (A from TMEM, q from shared
-//     memory, fp32 accumulation into one of two TMEM accumulators), then the
-//     copies of the stage just freed, while the workers move on;
-//   * while sub-tile i's MMAs run, every thread reads sub-tile i-1's
+// pages), two CTAs per SM, three roles that meet only at mbarriers, so none
+// waits for another's instruction issue:
+//   * copy thread (warp 9): a page is 64 x 132 = 8,448 contiguous bytes, so
+//     each arrives with one bulk copy (cp.async.bulk, completing on a "stage
+//     full" mbarrier), DSTAGES sub-tiles ahead, reissued into a stage as soon
+//     as the workers mark it read; the page bases come from the block table
+//     once per CTA;
+//   * workers (warps 0-7): every thread expands half of one key's staged
+//     e4m3 bytes exactly to fp16 and stores them with tcgen05.st straight
+//     into the MMA's A operand in tensor memory (row = key, two fp16 per
+//     32-bit column), double buffered, so the bytes cross shared memory once;
+//     each warp then arrives on "A full" and "stage free";
+//   * MMA thread (warp 8): on "A full" it issues S^T[128 keys x NQ heads] =
+//     K . Q^T as eight M=128, N=NQ, K=16 tcgen05 MMAs (A from TMEM, q from
+//     shared memory, fp32 accumulation into one of two TMEM accumulators);
+//   * while sub-tile i's MMAs run, every worker reads sub-tile i-1's
 //     accumulator for its key (half of the heads): w * relu(s) summed, the
 //     second half parked in shared memory and added, times the key's scale,
-//     one iteration later (after the next block barrier).
+//     one iteration later (after the workers' next named barrier).
 // q and w are loaded once per CTA and the histogram is accumulated in shared
 // memory and added to the global one once per CTA. Every wait is bounded by
 // device time; on expiry the CTA records DSA_ERR_TIMEOUT in the sticky status
@@ -48,9 +50,10 @@ constexpr int DP_BYTES = DP * IDXK_ROW;       // 8,448
 constexpr int DSUB = 128;                     // keys per sub-tile (MMA M)
 constexpr int DSTAGES = 4;                    // staged sub-tiles
 constexpr int DCTA_KEYS = 4096;               // most positions per CTA
-constexpr int NWORK = 256;                    // 8 warps: expansion and epilogue
-constexpr int ISSUER = NWORK;                 // warp 8, lane 0: MMAs and copies
-constexpr int DNT = NWORK + 32;
+constexpr int NWORK = 256;                    // warps 0-7: expansion and epilogue
+constexpr int MMA_WARP = NWORK / 32;          // warp 8, lane 0: the MMAs
+constexpr int COPY_WARP = MMA_WARP + 1;       // warp 9, lane 0: the page copies
+constexpr int DNT = NWORK + 64;
 constexpr uint32_t TMEM_COLS = 256;           // A0 | A1 | D0 | D1
 constexpr uint32_t A_COLS = HD / 2;           // 128 fp16 per key: 64 columns
 constexpr uint64_t kWaitTimeoutNs = 2000000000ull;
@@ -64,8 +67,9 @@ struct DecodeTcLayout {
   static constexpr uint32_t OFF_W = OFF_HIST + NBIN * 4;         // [NQ]
   static constexpr uint32_t OFF_PART = OFF_W + NQ * 4;           // [2][DSUB] second-half head sums
   static constexpr uint32_t OFF_BASE = OFF_PART + 2 * DSUB * 4;  // [DCTA_KEYS / DP] int64 page bases
-  static constexpr uint32_t OFF_MBAR = OFF_BASE + (DCTA_KEYS / DP) * 8;  // [DSTAGES] copies, [2] mma, drain
-  static constexpr uint32_t OFF_SLOT = OFF_MBAR + (DSTAGES + 3) * 8;
+  // mbarriers: [DSTAGES] stage full, [DSTAGES] stage free, [2] A full, [2] MMAs done, drain
+  static constexpr uint32_t OFF_MBAR = OFF_BASE + (DCTA_KEYS / DP) * 8;
+  static constexpr uint32_t OFF_SLOT = OFF_MBAR + (2 * DSTAGES + 5) * 8;
   static constexpr uint32_t BYTES = OFF_SLOT + 16 + 1024;        // + alignment slack
   static constexpr uint32_t D_COL = 2 * A_COLS;                  // accumulator p at D_COL + p * NQ
   static_assert(Q_REGION % 1024 == 0 && OFF_STAGE % 1024 == 0, "swizzled regions stay 1024-aligned");
@@ -108,9 +112,12 @@ __global__ void __launch_bounds__(DNT, 2) indexer_decode_tc_kernel(const Indexer
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + Lay::OFF_SLOT);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + Lay::OFF_SLOT + 4);
   uint32_t* q_bits = reinterpret_cast<uint32_t*>(sm + Lay::OFF_SLOT + 8);  // largest |q| bf16 pattern
-  const uint32_t mb0 = base + Lay::OFF_MBAR;        // copies of stage s at mb0 + 8 s
-  const uint32_t mb_mma = mb0 + 8u * DSTAGES;      // MMAs of sub-tile i done: mb_mma + 8 (i & 1)
-  const uint32_t mb_done = mb_mma + 16u;           // drain on abort
+  const uint32_t mb0 = base + Lay::OFF_MBAR;
+  auto mb_full = [&](int st) { return mb0 + 8u * (uint32_t)st; };                  // stage's copies landed
+  auto mb_free = [&](int st) { return mb0 + 8u * (uint32_t)(DSTAGES + st); };      // stage read by the workers
+  auto mb_afull = [&](int x) { return mb0 + 8u * (uint32_t)(2 * DSTAGES + x); };  // A[x] written
+  auto mb_mma = [&](int x) { return mb0 + 8u * (uint32_t)(2 * DSTAGES + 2 + x); }; // MMAs into D[x] done
+  const uint32_t mb_done = mb0 + 8u * (2 * DSTAGES + 4);                           // drain on abort
 
   const int b = blockIdx.x;
   const int p0 = blockIdx.y * a.cta_keys;
@@ -124,11 +131,11 @@ __global__ void __launch_bounds__(DNT, 2) indexer_decode_tc_kernel(const Indexer
   const int nsub = (v_end - p0 + DSUB - 1) / DSUB;
   const int32_t* bt_row = a.bt + (int64_t)b * a.bt_stride;
 
-  // Thread 0: bulk copies of sub-tile i's two pages into stage i % DSTAGES,
-  // from the page base codes in sBase.
+  // The copy thread: bulk copies of sub-tile i's two pages into stage
+  // i % DSTAGES, from the page base codes in sBase.
   auto issue = [&](int i) {
     const int st = i % DSTAGES;
-    const uint32_t mb = mb0 + 8u * (uint32_t)st;
+    const uint32_t mb = mb_full(st);
     uint32_t bytes = 0;
     int64_t pb[2];
 #pragma unroll
@@ -149,12 +156,18 @@ __global__ void __launch_bounds__(DNT, 2) indexer_decode_tc_kernel(const Indexer
 
   if (warp == 0) {
     if (lane == 0) {
-      for (int s = 0; s < DSTAGES; ++s) mbar_init(mb0 + 8u * s, 1);
-      mbar_init(mb_mma, 1);
-      mbar_init(mb_mma + 8u, 1);
+      for (int st = 0; st < DSTAGES; ++st) {
+        mbar_init(mb_full(st), 1);
+        mbar_init(mb_free(st), NWORK / 32);
+      }
+      for (int x = 0; x < 2; ++x) {
+        mbar_init(mb_afull(x), NWORK / 32);
+        mbar_init(mb_mma(x), 1);
+      }
       mbar_init(mb_done, 1);
       mbar_init_fence();
       *abort_flag = 0;
+      abort_flag[2] = 0;  // n_done below
     }
     __syncwarp();
     tmem_alloc(smem_u32(tmem_slot), TMEM_COLS);
@@ -212,120 +225,136 @@ __global__ void __launch_bounds__(DNT, 2) indexer_decode_tc_kernel(const Indexer
   __syncthreads();
   fence_after_sync();
   const uint32_t tmem = *tmem_slot;
-  int n_issued = 0;  // issuer: sub-tiles whose copies were issued
-  if (tid == ISSUER)
-    for (; n_issued < DSTAGES && n_issued < nsub; ++n_issued) issue(n_issued);
   const uint64_t desc_q = sw128_desc(base + Lay::OFF_Q, 16, 1024);
   constexpr uint32_t IDESC = idesc_f16(DSUB, NQ, false, false);
-
-  // this thread: key kq = 32 (warp & 3) + lane of every sub-tile (the TMEM
-  // lane its warp may access), dims / heads half hh
-  const int kq = 32 * (warp & 3) + lane, hh = warp >> 2;
-  const bool worker = tid < NWORK;
-  const uint32_t lane_base = (uint32_t)(32 * (warp & 3)) << 16;
-  bool ok = true;
-  bool issued = false;
   volatile int* n_done = abort_flag + 2;  // thread 0: sub-tiles whose copies were seen complete
-  if (tid == 0) *n_done = 0;
-  float sc_prev = 0.f, sc_cur = 0.f;  // hh == 0: the key's scale for sub-tiles i-1, i
-  float s_prev = 0.f;    // hh == 0: first-half head sum of sub-tile i-2 (finished at iteration i)
-  for (int it = 0; it < nsub + 2; ++it) {
-    // ---- expand sub-tile it into A[it & 1]
-    float sc_new = 0.f;
-    if (it < nsub && worker) {
-      const int st = it % DSTAGES;
-      ok = ok && mbar_wait(mb0 + 8u * (uint32_t)st, (uint32_t)((it / DSTAGES) & 1), abort_flag, err, kWaitTimeoutNs);
-      if (tid == 0 && ok) *n_done = it + 1;
-      const int pos = p0 + DSUB * it + kq;
-      const int j = kq >> 6;
-      const int64_t pbase = sBase[2 * it + j];
-      uint32_t w[16];
-#pragma unroll
-      for (int e = 0; e < 16; ++e) w[e] = 0u;
-      if (ok && pos < v_end && pbase != -1) {
-        if (pbase >= 0) {  // the staged page: 132-byte rows are only 4-byte aligned
-          const uint32_t src = smem_u32(stage + (2 * st + j) * DP_BYTES + (kq & 63) * IDXK_ROW) + 64 * hh;
-#pragma unroll
-          for (int e = 0; e < 16; ++e) asm volatile("ld.shared.u32 %0, [%1];" : "=r"(w[e]) : "r"(src + 4 * e));
-          if (hh == 0) asm volatile("ld.shared.f32 %0, [%1];" : "=f"(sc_new) : "r"(src + 128));
-        } else {  // a page that runs past the cache end: this key's own row, if inside
-          const int64_t r = (int64_t)bt_row[pos / DP] * DP + (pos % DP);
-          if (r < a.n_kv_rows) {
-            const uint32_t* g = reinterpret_cast<const uint32_t*>(a.k + r * IDXK_ROW + 64 * hh);
-#pragma unroll
-            for (int e = 0; e < 16; ++e) w[e] = __ldg(g + e);
-            if (hh == 0) sc_new = __ldg(reinterpret_cast<const float*>(a.k + r * IDXK_ROW + 128));
-          }
-        }
+  int n_issued = 0;                       // copy thread: sub-tiles whose copies were issued
+  bool issued = false;                    // MMA thread: at least one MMA issued
+
+  if (warp == COPY_WARP) {
+    // ---- page copies, DSTAGES sub-tiles ahead of the workers
+    if (lane == 0) {
+      for (; n_issued < nsub; ++n_issued) {
+        const int j = n_issued;
+        if (j >= DSTAGES &&
+            !mbar_wait(mb_free(j % DSTAGES), (uint32_t)(((j - DSTAGES) / DSTAGES) & 1), abort_flag, err,
+                       kWaitTimeoutNs))
+          break;
+        if (*abort_flag) break;
+        issue(j);
       }
-      uint32_t hv[32];
-#pragma unroll
-      for (int e = 0; e < 16; ++e) e4m3x4_to_half2x2_div256(w[e], hv[2 * e], hv[2 * e + 1]);  // keys / 256, exact
-      tmem_st32(tmem + lane_base + (uint32_t)((it & 1) * A_COLS + 32 * hh), hv);
-      tmem_wait_st();
     }
-    fence_before_sync();
-    __syncthreads();  // A[it & 1] written, stage it consumed; sPart of sub-tile it-2 visible
-    fence_after_sync();
-    // ---- issuer: the MMAs of sub-tile it, then the freed stage's copies; the
-    // workers go on with the epilogue of sub-tile it-1 meanwhile
-    if (tid == ISSUER && it < nsub) {
-      ok = ok && *abort_flag == 0;
-      if (ok) {
+  } else if (warp == MMA_WARP) {
+    // ---- S^T(it) = K(it) . Q^T as soon as the workers have written A[it & 1]
+    if (lane == 0) {
+      for (int it = 0; it < nsub; ++it) {
+        if (!mbar_wait(mb_afull(it & 1), (uint32_t)((it >> 1) & 1), abort_flag, err, kWaitTimeoutNs)) break;
+        if (*abort_flag) break;
+        fence_after_sync();
         const uint32_t a_tm = tmem + (uint32_t)((it & 1) * A_COLS);
         const uint32_t d_tm = tmem + Lay::D_COL + (uint32_t)((it & 1) * NQ);
 #pragma unroll
         for (int kk = 0; kk < HD / 16; ++kk)
           mma_f16_ts(d_tm, a_tm + 8u * kk, desc_q + (((kk >> 2) * Lay::Q_REGION + 32 * (kk & 3)) >> 4), IDESC,
                      kk != 0);
-        mma_commit(mb_mma + 8u * (uint32_t)(it & 1));
+        mma_commit(mb_mma(it & 1));
         issued = true;
       }
-      if (ok && n_issued < nsub) issue(n_issued++);
     }
-    // ---- finish sub-tile it-2: both head halves, scale, histogram, store
-    if (it >= 2 && hh == 0) {
-      const int pos = p0 + DSUB * (it - 2) + kq;
-      if (pos < v_end) {
-        const float v = (s_prev + sPart[((it - 2) & 1) * DSUB + kq]) * (sc_prev * 256.0f) * qmul;
-        atomicAdd(&sHist[monotone32(v) >> 20], 1u);
-        score_row[pos] = v;
-      }
-    }
-    // ---- half-head sums of sub-tile it-1 from its accumulator
-    if (worker && it >= 1 && it <= nsub) {
-      const int i1 = it - 1;
-      ok = ok && mbar_wait(mb_mma + 8u * (uint32_t)(i1 & 1), (uint32_t)((i1 >> 1) & 1), abort_flag, err,
-                           kWaitTimeoutNs);
-      ok = __all_sync(0xffffffffu, ok);  // tcgen05.ld below is warp-wide
-      fence_after_sync();
-      float s = 0.f;
-      if (ok) {
-        uint32_t acc[NQ / 2];
-        tmem_ld_cols<NQ / 2>(tmem + lane_base + Lay::D_COL + (uint32_t)((i1 & 1) * NQ + hh * (NQ / 2)), acc);
-        tmem_wait_ld();
+  } else {
+    // ---- workers: key kq = 32 (warp & 3) + lane of every sub-tile (the TMEM
+    // lane quarter its warp may access), dims / heads half hh
+    const int kq = 32 * (warp & 3) + lane, hh = warp >> 2;
+    const uint32_t lane_base = (uint32_t)(32 * (warp & 3)) << 16;
+    bool ok = true;
+    float sc_prev = 0.f, sc_cur = 0.f;  // hh == 0: the key's scale for sub-tiles i-1, i
+    float s_prev = 0.f;                 // hh == 0: first-half head sum of sub-tile i-2 (finished at iteration i)
+    for (int it = 0; it < nsub + 2; ++it) {
+      // expand sub-tile it into A[it & 1] (free: this warp waited for MMA(it-2) last iteration)
+      float sc_new = 0.f;
+      if (it < nsub) {
+        const int st = it % DSTAGES;
+        ok = ok && mbar_wait(mb_full(st), (uint32_t)((it / DSTAGES) & 1), abort_flag, err, kWaitTimeoutNs);
+        if (tid == 0 && ok) *n_done = it + 1;
+        const int pos = p0 + DSUB * it + kq;
+        const int j = kq >> 6;
+        const int64_t pbase = sBase[2 * it + j];
+        uint32_t w[16];
 #pragma unroll
-        for (int h = 0; h < NQ / 2; ++h) s += sW[hh * (NQ / 2) + h] * fmaxf(__uint_as_float(acc[h]), 0.f);
+        for (int e = 0; e < 16; ++e) w[e] = 0u;
+        if (ok && pos < v_end && pbase != -1) {
+          if (pbase >= 0) {  // the staged page: 132-byte rows are only 4-byte aligned
+            const uint32_t src = smem_u32(stage + (2 * st + j) * DP_BYTES + (kq & 63) * IDXK_ROW) + 64 * hh;
+#pragma unroll
+            for (int e = 0; e < 16; ++e) asm volatile("ld.shared.u32 %0, [%1];" : "=r"(w[e]) : "r"(src + 4 * e));
+            if (hh == 0) asm volatile("ld.shared.f32 %0, [%1];" : "=f"(sc_new) : "r"(src + 128));
+          } else {  // a page that runs past the cache end: this key's own row, if inside
+            const int64_t r = (int64_t)bt_row[pos / DP] * DP + (pos % DP);
+            if (r < a.n_kv_rows) {
+              const uint32_t* g = reinterpret_cast<const uint32_t*>(a.k + r * IDXK_ROW + 64 * hh);
+#pragma unroll
+              for (int e = 0; e < 16; ++e) w[e] = __ldg(g + e);
+              if (hh == 0) sc_new = __ldg(reinterpret_cast<const float*>(a.k + r * IDXK_ROW + 128));
+            }
+          }
+        }
+        uint32_t hv[32];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) e4m3x4_to_half2x2_div256(w[e], hv[2 * e], hv[2 * e + 1]);  // keys / 256, exact
+        tmem_st32(tmem + lane_base + (uint32_t)((it & 1) * A_COLS + 32 * hh), hv);
+        tmem_wait_st();
+        fence_before_sync();
+        __syncwarp();
+        if (lane == 0) {  // A[it & 1] rows of this warp written; stage st read
+          mbar_arrive(mb_afull(it & 1));
+          mbar_arrive(mb_free(st));
+        }
       }
-      if (hh == 1)
-        sPart[(i1 & 1) * DSUB + kq] = s;
-      else
-        s_prev = s;
-    }
-    if (hh == 0) {  // the scales ride along with the sub-tiles they belong to
-      sc_prev = sc_cur;
-      sc_cur = sc_new;
+      named_bar(1, NWORK);  // the workers' sPart of sub-tile it-2 visible
+      // finish sub-tile it-2: both head halves, scale, histogram, store
+      if (it >= 2 && hh == 0) {
+        const int pos = p0 + DSUB * (it - 2) + kq;
+        if (pos < v_end) {
+          const float v = (s_prev + sPart[((it - 2) & 1) * DSUB + kq]) * (sc_prev * 256.0f) * qmul;
+          atomicAdd(&sHist[monotone32(v) >> 20], 1u);
+          score_row[pos] = v;
+        }
+      }
+      // half-head sums of sub-tile it-1 from its accumulator
+      if (it >= 1 && it <= nsub) {
+        const int i1 = it - 1;
+        ok = ok && mbar_wait(mb_mma(i1 & 1), (uint32_t)((i1 >> 1) & 1), abort_flag, err, kWaitTimeoutNs);
+        ok = __all_sync(0xffffffffu, ok);  // tcgen05.ld below is warp-wide
+        fence_after_sync();
+        float sum = 0.f;
+        if (ok) {
+          uint32_t acc[NQ / 2];
+          tmem_ld_cols<NQ / 2>(tmem + lane_base + Lay::D_COL + (uint32_t)((i1 & 1) * NQ + hh * (NQ / 2)), acc);
+          tmem_wait_ld();
+#pragma unroll
+          for (int h = 0; h < NQ / 2; ++h) sum += sW[hh * (NQ / 2) + h] * fmaxf(__uint_as_float(acc[h]), 0.f);
+        }
+        if (hh == 1)
+          sPart[(i1 & 1) * DSUB + kq] = sum;
+        else
+          s_prev = sum;
+      }
+      if (hh == 0) {  // the scales ride along with the sub-tiles they belong to
+        sc_prev = sc_cur;
+        sc_cur = sc_new;
+      }
     }
   }
-  __syncthreads();  // the last sub-tile's histogram counts are in
+  __syncthreads();  // every role is done; the last sub-tile's histogram counts are in
   for (int i = tid; i < NBIN; i += DNT) {
     const uint32_t c = sHist[i];
     if (c && a.hist) atomicAdd(a.hist + (int64_t)b * NBIN + i, (int)c);
   }
-  if (tid == ISSUER && *abort_flag) {  // drain this CTA's copies and MMAs before its memory is released
-    for (int j = *n_done; j < n_issued; ++j)
-      mbar_wait_drain(mb0 + 8u * (uint32_t)(j % DSTAGES), (uint32_t)((j / DSTAGES) & 1), kWaitTimeoutNs);
-    if (issued) {
+  if (*abort_flag) {  // drain this CTA's copies and MMAs before its memory is released
+    if (warp == COPY_WARP && lane == 0)
+      for (int j = *n_done; j < n_issued; ++j)
+        mbar_wait_drain(mb_full(j % DSTAGES), (uint32_t)((j / DSTAGES) & 1), kWaitTimeoutNs);
+    if (warp == MMA_WARP && lane == 0 && issued) {
       mma_commit(mb_done);
       mbar_wait_drain(mb_done, 0, kWaitTimeoutNs);
     }
