@@ -40,6 +40,7 @@ SIGNATURES = {
     "dsa_last_error": (ctypes.c_char_p, []),
     "dsa_version": (_i, []),
     "dsa_device_error": (_i, [_i]),
+    "dsa_selftest_wait_timeout": (_i, [_i64, _p]),
     "dsa_sparse_mla_decode_workspace_bytes": (_sz, [_i, _i, _i]),
     "dsa_sparse_mla_decode_plan": (_i, [_i, _i, _i, _i, ctypes.POINTER(_i), ctypes.POINTER(_i),
                                         ctypes.POINTER(_sz), ctypes.POINTER(_i)]),
@@ -110,6 +111,13 @@ def lib() -> ctypes.CDLL:
     return _lib
 
 
+# Debug mode (DSA_B200_CHECK_DEVICE=1): after every successful call the hook
+# that ops.py installs synchronises the device and raises if a bounded wait
+# inside a kernel expired (the sticky status word of dsa_device_error).
+CHECK_DEVICE = os.environ.get("DSA_B200_CHECK_DEVICE", "0") not in ("", "0")
+post_call_hook = None
+
+
 def call(name: str, *args) -> None:
     """Call a status-returning entry point; raise DsaError on failure."""
     fn = getattr(lib(), name)
@@ -117,3 +125,5 @@ def call(name: str, *args) -> None:
     if st != DSA_OK:
         msg = lib().dsa_last_error().decode(errors="replace")
         raise DsaError(name, st, msg)
+    if CHECK_DEVICE and post_call_hook is not None:
+        post_call_hook(name)

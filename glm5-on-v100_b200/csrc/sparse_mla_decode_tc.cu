@@ -997,6 +997,39 @@ int tc_error_word(int dev, int32_t** out) {
 
 }  // namespace dsa
 
+namespace dsa {
+namespace {
+// One mbarrier whose phase needs two arrivals and gets one: every thread's
+// bounded wait runs out, records DSA_ERR_TIMEOUT in the status word and
+// returns (the same wait every tensor-core kernel of the library uses).
+__global__ void selftest_wait_kernel(int32_t* err, int64_t timeout_ns) {
+  __shared__ __align__(8) uint64_t mbar;
+  __shared__ int abort_flag;
+  const uint32_t mb = smem_u32(&mbar);
+  if (threadIdx.x == 0) {
+    tc::mbar_init(mb, 2);
+    tc::mbar_init_fence();
+    abort_flag = 0;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) tc::mbar_arrive(mb);
+  tc::mbar_wait(mb, 0, &abort_flag, err, (uint64_t)timeout_ns);
+}
+}  // namespace
+}  // namespace dsa
+
+extern "C" int dsa_selftest_wait_timeout(int64_t timeout_ns, void* stream) {
+  dsa::clear_error();
+  DSA_REQUIRE(timeout_ns >= 1000 && timeout_ns <= 1000000000LL, DSA_ERR_INVALID,
+              "selftest_wait_timeout: timeout must be in [1 us, 1 s]");
+  const int dev = dsa::current_device();
+  int32_t* err = nullptr;
+  const int st = dsa::tc_error_word(dev, &err);
+  if (st != DSA_OK) return st;
+  dsa::selftest_wait_kernel<<<1, 32, 0, dsa::as_stream(stream)>>>(err, timeout_ns);
+  return dsa::check_launch("selftest_wait_kernel");
+}
+
 extern "C" int dsa_device_error(int reset) {
   dsa::clear_error();
   int32_t v = 0;

@@ -236,6 +236,55 @@ def p2p_error_flag(device) -> torch.Tensor:
     return t
 
 
+class DsaDeviceError(RuntimeError):
+    """A bounded wait inside a kernel of this library expired: the launch
+    returned without finishing its output (the status word of
+    dsa_device_error)."""
+
+
+def device_error(device=None, reset: bool = False) -> int:
+    """The library's sticky device status on `device` (0, or DSA_ERR_TIMEOUT
+    after an expired wait); synchronises with the device. reset clears it."""
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    with torch.cuda.device(dev):
+        v = int(L.lib().dsa_device_error(1 if reset else 0))
+    if v < 0:
+        raise L.DsaError("dsa_device_error", -v, L.lib().dsa_last_error().decode(errors="replace"))
+    return v
+
+
+def check_device_status(device=None) -> None:
+    """Synchronise `device` and raise DsaDeviceError (clearing the status) if
+    a bounded wait in one of this library's kernels expired since the last
+    check."""
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    torch.cuda.synchronize(dev)
+    v = device_error(dev, reset=True)
+    if v != 0:
+        raise DsaDeviceError(f"a bounded device wait expired on {dev}: status {L.STATUS_NAMES.get(v, v)}; "
+                             "the outputs of the launches since the last check are incomplete")
+
+
+def selftest_wait_timeout(timeout_s: float = 0.01, device=None) -> None:
+    """Launch one block whose mbarrier wait cannot complete: after timeout_s of
+    device time it records DSA_ERR_TIMEOUT and returns (tests the bounded-wait
+    path without a fault)."""
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    with torch.cuda.device(dev):
+        L.call("dsa_selftest_wait_timeout", int(timeout_s * 1e9), _stream(dev))
+
+
+def _check_after_call(name: str) -> None:
+    # debug mode only; never inside a CUDA-graph capture (no synchronisation there)
+    if name in ("dsa_device_error", "dsa_selftest_wait_timeout") or name.startswith("dsa_ipc"):
+        return
+    if torch.cuda.is_available() and not torch.cuda.is_current_stream_capturing():
+        check_device_status()
+
+
+L.post_call_hook = _check_after_call
+
+
 def check_p2p_status(device) -> None:
     """Raise if a bounded P2P wait on `device` timed out (synchronises)."""
     f = p2p_error_flag(device)

@@ -59,6 +59,12 @@ int dsa_version(void);
  * -DSA_ERR_CUDA. No counterpart in the reference, whose waits never expire. */
 int dsa_device_error(int reset);
 
+/* Test entry for the bounded waits: one block whose mbarrier wait can never
+ * complete runs for timeout_ns (1 us .. 1 s) of device time, then records
+ * DSA_ERR_TIMEOUT in the status word that dsa_device_error reads and returns,
+ * leaving the context usable. No reference counterpart. */
+int dsa_selftest_wait_timeout(int64_t timeout_ns, void* stream);
+
 /* =====================================================================
  * Sparse MLA decode / prefill attention.
  * Replaces sm70_sparse_mla_decode (dsa.cu:2457-2616; schema binds

@@ -735,6 +735,38 @@ def test_shard_merge_reference_fixture(dsa):
     np.testing.assert_array_equal(out.cpu().numpy(), O.shard_merge(allf, K))
 
 
+def test_bounded_mbarrier_wait_expiry_is_reported(dsa, monkeypatch):
+    """An mbarrier wait that can never complete (one of two arrivals) runs out
+    after 10 ms of device time: the status word reads TIMEOUT, the torch layer
+    raises DsaDeviceError (and clears it), the debug mode raises at the next
+    op call, and the context stays usable for real work."""
+    from importlib import import_module
+
+    L = import_module("glm5-on-v100_b200._lib")
+    ops = dsa.ops
+    ops.device_error(reset=True)
+    ops.selftest_wait_timeout(0.01)
+    torch.cuda.synchronize()
+    assert ops.device_error() == L.DSA_ERR_TIMEOUT
+    with pytest.raises(ops.DsaDeviceError):
+        ops.check_device_status()
+    assert ops.device_error() == 0
+    # debug mode: the next op call synchronises and raises
+    ops.selftest_wait_timeout(0.01)
+    monkeypatch.setattr(L, "CHECK_DEVICE", True)
+    rng = np.random.default_rng(4)
+    s = rng.standard_normal((3, 5000)).astype(np.float32)
+    lens = np.array([5000, 4000, 100], np.int32)
+    out = torch.empty(3, 256, dtype=torch.int32, device=DEV)
+    with pytest.raises(ops.DsaDeviceError):
+        dsa.persistent_topk(to_dev(s), to_dev(lens), out, torch.empty(0, device=DEV), 256, 5000)
+    # the same call again: clean status, exact result
+    dsa.persistent_topk(to_dev(s), to_dev(lens), out, torch.empty(0, device=DEV), 256, 5000)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(out.cpu().numpy(), O.topk_rows(s, lens, 256))
+    assert ops.device_error() == 0
+
+
 def test_shard_merge_p2p_local_slots_and_timeout(dsa):
     """The P2P merge over pointer arrays (two slabs on this GPU stand in for
     peers), then a bounded wait on a flag nothing sets: the kernel returns,
