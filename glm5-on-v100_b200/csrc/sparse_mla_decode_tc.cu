@@ -706,7 +706,10 @@ __global__ void __launch_bounds__(NTHREADS, 1) sparse_mla_decode_tc_kernel(const
   fence_after_sync();
   if (csize == 1 && p.n_splits > 1) {
     // ------------------------------------------- partial state of this slice
+    // O^T is staged as [64 heads][512 dims] f32 (128 KB) in the free tile
+    // buffers, then each head's 2 KB row leaves with one bulk copy.
     __syncthreads();
+    float* stg = reinterpret_cast<float*>(sm + SM_KV);
     const int hb = 16 * ((warp >> 2) & 3);  // heads [hb, hb + 16), for warps 0-15
 #pragma unroll 1
     for (int j = 0; j < 4 && warp < 16; ++j) {
@@ -719,12 +722,18 @@ __global__ void __launch_bounds__(NTHREADS, 1) sparse_mla_decode_tc_kernel(const
         for (int h = 0; h < 16; ++h) o[h] = 0u;
       }
       const int d = 128 * j + 32 * sp + lane;
-#pragma unroll 4
-      for (int h = 0; h < 16; ++h) {
-        const int head = h0 + hb + h;
-        if (head >= p.n_head) break;
-        p.part_o[(((int64_t)b * p.n_head + head) * p.n_splits + split) * DV + d] = __uint_as_float(o[h]);
-      }
+#pragma unroll
+      for (int h = 0; h < 16; ++h) stg[(hb + h) * DV + d] = __uint_as_float(o[h]);
+    }
+    fence_proxy_async();  // the staged rows are read by the bulk copies
+    __syncthreads();
+    if ((int)threadIdx.x < min(NH, p.n_head - h0)) {
+      float* dst = p.part_o + (((int64_t)b * p.n_head + h0 + threadIdx.x) * p.n_splits + split) * DV;
+      asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst),
+                   "r"(smem_u32(stg + threadIdx.x * DV)), "r"((uint32_t)(DV * 4))
+                   : "memory");
+      asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+      asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");  // written before the CTA moves on
     }
     if (threadIdx.x < NH && h0 + (int)threadIdx.x < p.n_head) {
       const int64_t bh = (int64_t)b * p.n_head + h0 + threadIdx.x;
