@@ -1034,6 +1034,7 @@ def measure(wl, dsa, args, world, rank, dev, steps, warmup, e2e_steps, cpu):
     the dominant kernel alone for the roofline; the end-to-end leg through the
     public op with pinned host buffers; the CPU baseline on rank 0 at N = 1."""
     wl.setup(dev, seed=1234 + rank)
+    torch.cuda.synchronize()  # inputs are made on the default stream; the steps run on their own stream
     hbm_peak, tf_burst, tf_sustained, peak_kind = load_peaks()
     stream = torch.cuda.Stream(dev)
     graphs = []
@@ -1074,6 +1075,7 @@ def measure(wl, dsa, args, world, rank, dev, steps, warmup, e2e_steps, cpu):
     alg, unit, bound = wl.algorithmic()
     if part is not None:
         fn, alg = part
+        torch.cuda.synchronize()  # the part's buffers are made on the default stream
         with torch.cuda.stream(stream):
             pg = [capture(lambda: fn(dsa), stream)]
             pg[0].replay()
