@@ -63,6 +63,10 @@ def load_peaks():
     return 6650.0, 1590.0, 1400.0, "fallback"
 
 
+def scaled(x, f):
+    return None if x is None else x * f
+
+
 def profile_traffic(name):
     """Per-launch DRAM bytes recorded in profiles/<name>.md ('traffic_bytes_per_launch: N')."""
     if name is None:
@@ -208,6 +212,11 @@ class Workload:
 
     def after_timing(self, dsa, dev):
         """Checks that the timed work ran as claimed (raises otherwise)."""
+
+    def traffic_scale(self):
+        """Units of this run's dominant launch per unit of the profiled one
+        (the profile's DRAM bytes scale with it)."""
+        return 1.0
 
     def roofline_part(self):
         """None, or (graph-capturable callable, its algorithmic amount) for the
@@ -636,13 +645,15 @@ class ShardMergeWorkload(Workload):
     traffic_profile = "shard_merge_r4096_tp8"
     TP, R, TOPK, S = 8, 4096, 2048, 184320
     nsets = 2
+    sorted_runs = True  # False: shuffled lists (the merge sorts the selected positions itself)
 
     def bytes_per_row(self):
         return self.TP * 2 * self.TOPK * 4 + self.TOPK * 4
 
     def config(self):
         return {"workload": "shard_merge", "shards": self.TP, "rows": self.R, "topk": self.TOPK,
-                "keys": self.S, "l2": f"inputs larger than L2: {self.nsets} candidate sets of "
+                "keys": self.S, "runs": "ascending per shard" if self.sorted_runs else "shuffled",
+                "l2": f"inputs larger than L2: {self.nsets} candidate sets of "
                 f"{self.TP * self.R * 2 * self.TOPK * 4 / 1e6:.0f} MB"}
 
     def _candidates(self, dev, g, R):
@@ -651,6 +662,8 @@ class ShardMergeWorkload(Workload):
         base = torch.arange(self.TP, device=dev).view(self.TP, 1, 1) * span
         off = torch.randint(0, span, (self.TP, R, 1), device=dev, generator=g)
         pos = (base + (torch.arange(self.TOPK, device=dev).view(1, 1, -1) * 89 + off) % span).to(torch.int32)
+        if self.sorted_runs:  # each shard's list ascending, as the top-k kernels of this build emit it
+            pos = torch.sort(pos, dim=2).values
         return torch.cat([vals, pos.view(torch.float32)], dim=2).contiguous()
 
     def setup(self, dev, seed):
@@ -916,6 +929,7 @@ class ShardedLayerWorkload(DecodeLayerWorkload):
     scaling = "strong"
     B, H, HI, S, PAGE, TOPK, NSETS = 8, 64, 32, 180224, 64, 2048, 4
     nsets = NSETS
+    traffic_profile = "indexer_decode_tc_b8_ctx180k"  # the logits launch over 8 rows x 180,224 keys
 
     def config(self):
         tp = getattr(self, "tp", 1)
@@ -968,6 +982,9 @@ class ShardedLayerWorkload(DecodeLayerWorkload):
 
     def indexer_bytes(self):
         return self.B * (self.span * (132 + 4) + self.HI * 128 * 2 + self.HI * 4)
+
+    def traffic_scale(self):
+        return self.B * self.span / (8 * 180224)  # keys this rank's logits launch reads vs the profiled launch
 
     def roofline_part(self):
         """The indexer logits with the fused histogram over this rank's key
@@ -1115,7 +1132,8 @@ def measure(wl, dsa, args, world, rank, dev, steps, warmup, e2e_steps, cpu):
         "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": wl.scaling, "data": wl.data,
         "config": wl.config(), "e2e": e2e, "gpu_launches": int(steps * wl.launches_per_step(dsa)),
         "roofline": {"bound": bound, "achieved": achieved, "peak": peak, "unit": unit, "frac": achieved / peak,
-                     "traffic": profile_traffic(wl.traffic_profile), "note": wl.roofline_note(peak_kind)},
+                     "traffic": scaled(profile_traffic(wl.traffic_profile), wl.traffic_scale()),
+                     "note": wl.roofline_note(peak_kind)},
         "clocks": sampler.summary(),
     }
     if cpu and rank == 0 and world == 1 and not args.no_cpu_baseline:

@@ -27,8 +27,9 @@
 //      shared memory. When every shard's run is ascending (always so for lists
 //      the top-k kernels write), the output rank of a position is its index in
 //      its run plus, per other run, a count found from the run's first/last
-//      entries (disjoint key shards) or a binary search. Runs that are not
-//      ascending are ranked by counting over all selected positions.
+//      entries (disjoint key shards) or a binary search. When a run is not
+//      ascending, all selected positions are sorted instead (a bitonic
+//      network over 2048 entries, mostly in registers and shuffles).
 // The P2P variant checks the error word once, waits (bounded) on every peer's
 // staged flag with acquire loads, and then reads the peers' slots with
 // relaxed system-scope loads (plain peer loads; no TMA, no multicast).
@@ -192,6 +193,59 @@ __device__ __forceinline__ int count_run(const int32_t* a, int n, int32_t x, boo
       hi = mid;
   }
   return lo;
+}
+
+// Ascending sort of a[0, n), n <= MAX_K = 4 * MT, in shared memory, by the MT
+// threads of the block: a bitonic network over MAX_K entries (the padding is
+// INT_MAX) with thread t holding entries 4t..4t+3 in registers. Partners at
+// distance 1 or 2 are in the same thread, up to 64 in the same warp
+// (shuffles); only the ten steps at distance >= 128 go through shared memory.
+// Used when a shard's positions do not arrive ascending (the output lists
+// positions in order; equal positions are the same value, so their relative
+// order does not show).
+__device__ __noinline__ void sort_positions(int32_t* a, int n) {
+  static_assert(MAX_K == 4 * MT, "four entries per thread");
+  const int t = threadIdx.x;
+  int32_t v[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) v[e] = 4 * t + e < n ? a[4 * t + e] : INT_MAX;
+  __syncthreads();  // every entry is in registers before shared memory is reused
+  for (int k = 2; k <= MAX_K; k <<= 1) {
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      int32_t w[4];  // the partners' values
+      if (j >= 128) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) a[4 * t + e] = v[e];
+        __syncthreads();
+#pragma unroll
+        for (int e = 0; e < 4; ++e) w[e] = a[(4 * t + e) ^ j];
+        __syncthreads();
+      } else if (j >= 4) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) w[e] = __shfl_xor_sync(0xffffffffu, v[e], j >> 2);
+      } else if (j == 2) {
+        w[0] = v[2];
+        w[1] = v[3];
+        w[2] = v[0];
+        w[3] = v[1];
+      } else {
+        w[0] = v[1];
+        w[1] = v[0];
+        w[2] = v[3];
+        w[3] = v[2];
+      }
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int i = 4 * t + e;
+        const bool keep_min = ((i & j) == 0) == ((i & k) == 0);
+        v[e] = keep_min ? min(v[e], w[e]) : max(v[e], w[e]);
+      }
+    }
+  }
+#pragma unroll
+  for (int e = 0; e < 4; ++e)
+    if (4 * t + e < n) a[4 * t + e] = v[e];
+  __syncthreads();
 }
 
 __device__ void merge_row(const MergeArgs& a, int r, int64_t soff, MergeSmem& s) {
@@ -437,23 +491,9 @@ __device__ void merge_row(const MergeArgs& a, int r, int64_t soff, MergeSmem& s)
       out[n_neg + rank] = p;
     }
   } else {
-    // runs in arbitrary order: rank = #smaller + #equal at a lower slot
-    int32_t mine[PER];
-    int rk[PER];
-#pragma unroll
-    for (int k = 0; k < PER; ++k) {
-      const int i = tid + k * MT;
-      mine[k] = i < n_sel ? s.pos[i] : 0;
-      rk[k] = 0;
-    }
-    for (int j = 0; j < n_sel; ++j) {
-      const int32_t v = s.pos[j];
-#pragma unroll
-      for (int k = 0; k < PER; ++k) rk[k] += v < mine[k] || (v == mine[k] && j < tid + k * MT);
-    }
-#pragma unroll
-    for (int k = 0; k < PER; ++k)
-      if (tid + k * MT < n_sel) out[n_neg + rk[k]] = mine[k];
+    // a run out of order: sort all selected positions
+    sort_positions(s.pos, n_sel);
+    for (int i = tid; i < n_sel; i += MT) out[n_neg + i] = s.pos[i];
   }
 }
 
@@ -505,8 +545,8 @@ __global__ void __launch_bounds__(MT, 2) shard_merge_kernel(const MergeArgs a) {
 //     is also column order;
 //   * each CTA ranks the positions of its own run against the other runs
 //     (bounds first, a binary search over DSMEM otherwise) and writes them;
-//     runs that are not ascending are gathered into rank 0, which ranks all
-//     by counting.
+//     runs that are not ascending are gathered into rank 0, which sorts
+//     them all.
 struct ClusterMergeSmem {
   uint32_t hist[NBIN];
   int32_t pos[MAX_K];        // this CTA's run; rank 0: all runs in the unsorted fallback
@@ -834,22 +874,10 @@ __device__ void merge_row_cluster(const MergeArgs& a, int r, int64_t soff, Clust
     }
     cl.sync();
     if (rank == 0) {
-      int32_t v[PER];
-      int rk[PER];
-#pragma unroll
-      for (int k = 0; k < PER; ++k) {
-        const int i = tid + k * MT;
-        v[k] = i < total ? s.pos[i] : 0;
-        rk[k] = 0;
-      }
-      for (int j = 0; j < total; ++j) {
-        const int32_t u = s.pos[j];
-#pragma unroll
-        for (int k = 0; k < PER; ++k) rk[k] += u < v[k] || (u == v[k] && j < tid + k * MT);
-      }
-#pragma unroll
-      for (int k = 0; k < PER; ++k)
-        if (tid + k * MT < total && n_neg + rk[k] < K) out[n_neg + rk[k]] = v[k];
+      const int n = min(total, MAX_K);
+      sort_positions(s.pos, n);
+      for (int i = tid; i < n; i += MT)
+        if (n_neg + i < K) out[n_neg + i] = s.pos[i];
     }
   }
   cl.sync();  // no CTA leaves while another reads its run

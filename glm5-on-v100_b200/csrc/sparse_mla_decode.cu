@@ -388,16 +388,27 @@ __global__ void __launch_bounds__(128) sparse_mla_merge_kernel(const float* __re
   float L = 0.f;
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
   const int d = threadIdx.x * 4;
-  for (int s = 0; s < n_splits; ++s) {
-    const float l = ml[2 * s + 1];
-    if (l > 0.f) {
-      const float w = exp2f(ml[2 * s] - M);
-      L += l * w;
-      const float4 v = *reinterpret_cast<const float4*>(part_o + (bh * n_splits + s) * DV + d);
-      acc.x += w * v.x;
-      acc.y += w * v.y;
-      acc.z += w * v.z;
-      acc.w += w * v.w;
+  // eight slices' loads in flight at a time, all inside the workspace; a
+  // slice that counted nothing (l = 0) is loaded but not used
+  constexpr int U = 8;
+  for (int s0 = 0; s0 < n_splits; s0 += U) {
+    float4 v[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u)
+      v[u] = s0 + u < n_splits ? *reinterpret_cast<const float4*>(part_o + (bh * n_splits + s0 + u) * DV + d)
+                               : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int s = s0 + u;
+      const float l = s < n_splits ? ml[2 * s + 1] : 0.f;
+      if (l > 0.f) {
+        const float w = exp2f(ml[2 * s] - M);
+        L += l * w;
+        acc.x += w * v[u].x;
+        acc.y += w * v[u].y;
+        acc.z += w * v[u].z;
+        acc.w += w * v[u].w;
+      }
     }
   }
   const float inv = L > 0.f ? 1.f / L : 0.f;
