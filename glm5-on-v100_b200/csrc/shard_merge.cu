@@ -498,11 +498,13 @@ __device__ void merge_row(const MergeArgs& a, int r, int64_t soff, MergeSmem& s)
 }
 
 // Exchange mode: the last CTA to finish publishes merged = seq and advances
-// the rank's sequence counter (every CTA arrives, even after an error).
+// the rank's sequence counter (every CTA arrives, even after an error). Each
+// CTA orders its work at GPU scope before its arrival; the last one orders
+// them all at system scope before the release store.
 __device__ void finish_exchange(const MergeArgs& a, int seq) {
   __syncthreads();
   if (threadIdx.x != 0) return;
-  __threadfence_system();
+  __threadfence();
   if (atomicAdd(a.ctl + 2, 1) == (int)(gridDim.x * gridDim.y) - 1) {
     a.ctl[2] = 0;
     __threadfence_system();

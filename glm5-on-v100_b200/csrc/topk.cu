@@ -62,11 +62,13 @@ struct TopkParams {
   int pos_off;
   int32_t* hist_clear;  // when set (== hist): each hist row is zeroed once read
   // exchange staging (ctl != null): the payload goes to slot (seq & 1) of
-  // this rank's exchange buffer, seq = ctl[0] + 1, after every peer merged
-  // seq - 2; the last CTA publishes staged = seq on my_flags[0]
+  // this rank's exchange buffer, seq = ctl[0] + 1; the last CTA publishes
+  // staged = seq on my_flags[0] unless the error word is set. Slot seq & 1
+  // is free without a wait: this rank's merge of step seq - 1 saw every
+  // peer's staged(seq - 1), which each peer publishes only after its merge of
+  // step seq - 2, the last reader of this slot, has completed (stream order).
   int* ctl;
   int* my_flags;
-  const int* peer_merged[MAX_TP];
   int tp;
   int64_t slot_bytes;
   int64_t timeout_ns;
@@ -481,25 +483,33 @@ __device__ void topk_row(const TopkParams& p, int b, const Emit& out, TopkSmem& 
   for (int i = (int)(n_sure + n_sel) + tid; i < K; i += NT) out(i, -1);  // only for an inconsistent histogram
 }
 
+// Exchange staging: the last CTA of the grid publishes staged = seq (nothing
+// once the error word is set). Every CTA orders its payload writes at GPU
+// scope before its arrival; the last one, having seen every arrival, orders
+// them all at system scope before the release store peers acquire.
+__device__ __forceinline__ void publish_staged(const TopkParams& p, int seq, int n_ctas) {
+  __syncthreads();
+  if (threadIdx.x != 0) return;
+  __threadfence();
+  if (atomicAdd(p.ctl + 1, 1) == n_ctas - 1) {
+    p.ctl[1] = 0;
+    __threadfence_system();
+    if (read_err_word(p.err) == 0) st_release_sys_s32(p.my_flags, seq);
+  }
+}
+
 template <int NT>
 __global__ void __launch_bounds__(NT, 1024 / NT) topk_rows_kernel(const TopkParams p) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   TopkSmem& s = *reinterpret_cast<TopkSmem*>(smem_raw);
   const int b = blockIdx.x;
-  const int tid = threadIdx.x;
   Emit e{};
   e.row = p.score + (int64_t)b * p.score_stride;
   float* pay = p.pay;
   int seq = 0;
-  bool ok = true;
-  if (p.ctl) {  // exchange staging: wait until every peer is done with this slot
+  if (p.ctl) {  // exchange staging into slot seq & 1 (free, see TopkParams)
     seq = *reinterpret_cast<const volatile int*>(p.ctl) + 1;
     pay += (int64_t)(seq & 1) * (p.slot_bytes / 4);
-    if (tid == 0) s.ok = read_err_word(p.err) == 0;
-    __syncthreads();
-    if (seq > 2 && s.ok && tid < p.tp && !wait_flag_geq(p.peer_merged[tid], seq - 2, p.timeout_ns, p.err)) s.ok = 0;
-    __syncthreads();
-    ok = s.ok != 0;
   }
   if (pay) {
     e.val = pay + (int64_t)b * p.pay_stride;
@@ -508,22 +518,8 @@ __global__ void __launch_bounds__(NT, 1024 / NT) topk_rows_kernel(const TopkPara
   } else {
     e.idx = p.idx + (int64_t)b * p.idx_stride;
   }
-  if (ok) {
-    topk_row<NT>(p, b, e, s);
-  } else if (p.hist_clear) {
-    for (int i = tid; i < NBIN1; i += NT) p.hist_clear[(int64_t)b * NBIN1 + i] = 0;
-  }
-  if (p.ctl) {  // the last CTA publishes staged = seq (nothing after an error)
-    __syncthreads();
-    if (tid == 0) {
-      __threadfence_system();
-      if (atomicAdd(p.ctl + 1, 1) == (int)gridDim.x - 1) {
-        p.ctl[1] = 0;
-        __threadfence_system();
-        if (read_err_word(p.err) == 0) st_release_sys_s32(p.my_flags, seq);
-      }
-    }
-  }
+  topk_row<NT>(p, b, e, s);
+  if (p.ctl) publish_staged(p, seq, (int)gridDim.x);
 }
 
 // ---------------------------------------------------------- cluster mode
@@ -806,25 +802,13 @@ __global__ void __launch_bounds__(NT_CL, 1) topk_cluster_kernel(const TopkParams
   cg::cluster_group cl = cg::this_cluster();
   const int rank = (int)cl.block_rank();
   const int b = blockIdx.y;
-  const int tid = threadIdx.x;
   Emit e{};
   e.row = p.score + (int64_t)b * p.score_stride;
   float* pay = p.pay;
   int seq = 0;
-  bool ok = true;
-  if (p.ctl) {  // exchange staging: rank 0 waits for the slot, the cluster follows its verdict
+  if (p.ctl) {  // exchange staging into slot seq & 1 (free, see TopkParams)
     seq = *reinterpret_cast<const volatile int*>(p.ctl) + 1;
     pay += (int64_t)(seq & 1) * (p.slot_bytes / 4);
-    if (rank == 0) {
-      if (tid == 0) s.ok = read_err_word(p.err) == 0;
-      __syncthreads();
-      if (seq > 2 && s.ok && tid < p.tp && !wait_flag_geq(p.peer_merged[tid], seq - 2, p.timeout_ns, p.err))
-        s.ok = 0;
-      __syncthreads();
-    }
-    cl.sync();
-    ok = *cl.map_shared_rank(&s.ok, 0) != 0;
-    cl.sync();  // rank 0's verdict is read before its shared memory is reused
   }
   if (pay) {
     e.val = pay + (int64_t)b * p.pay_stride;
@@ -833,22 +817,8 @@ __global__ void __launch_bounds__(NT_CL, 1) topk_cluster_kernel(const TopkParams
   } else {
     e.idx = p.idx + (int64_t)b * p.idx_stride;
   }
-  if (ok) {
-    topk_row_cluster<NT_CL>(p, b, e, s, cs, cl, rank);
-  } else if (p.hist_clear && rank == 0) {
-    for (int i = tid; i < NBIN1; i += NT_CL) p.hist_clear[(int64_t)b * NBIN1 + i] = 0;
-  }
-  if (p.ctl) {  // the last CTA of the grid publishes staged = seq (nothing after an error)
-    __syncthreads();
-    if (tid == 0) {
-      __threadfence_system();
-      if (atomicAdd(p.ctl + 1, 1) == (int)(gridDim.x * gridDim.y) - 1) {
-        p.ctl[1] = 0;
-        __threadfence_system();
-        if (read_err_word(p.err) == 0) st_release_sys_s32(p.my_flags, seq);
-      }
-    }
-  }
+  topk_row_cluster<NT_CL>(p, b, e, s, cs, cl, rank);
+  if (p.ctl) publish_staged(p, seq, (int)(gridDim.x * gridDim.y));
 }
 
 std::once_flag g_once[kMaxDevices];
@@ -995,10 +965,8 @@ extern "C" int dsa_shard_exchange_topk(const float* score, int64_t score_stride,
   p.slot_bytes = slot_bytes;
   p.timeout_ns = timeout_ns;
   p.err = err_flag;
-  for (int s = 0; s < tp; ++s) {
+  for (int s = 0; s < tp; ++s)
     DSA_REQUIRE(flag_ptrs[s] != 0, DSA_ERR_INVALID, "shard_exchange_topk: null flag pointer %d", s);
-    p.peer_merged[s] = reinterpret_cast<const int*>(flag_ptrs[s]) + 1;
-  }
   p.my_flags = reinterpret_cast<int*>(flag_ptrs[rank]);
   return run_topk(p, B, as_stream(stream));
 }

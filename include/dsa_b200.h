@@ -363,12 +363,15 @@ int dsa_indexer_shard_stage(float* slot, const float* vals,
  * sequence number, [1] and [2] CTA arrival counters).
  *
  * Step seq = ctl[0] + 1:
- *   dsa_shard_exchange_topk: every peer's merged flag >= seq - 2 (slot
- *     reuse, bounded wait), then the exact top-K of each score row (as
+ *   dsa_shard_exchange_topk: the exact top-K of each score row (as
  *     dsa_decode_topk; hist, if given, is consumed and zeroed for the next
  *     step) is written as a payload row of slot (seq & 1) of slot_base: K
  *     values then K positions + pos_off (-inf / -1 pads); the last CTA
- *     publishes staged = seq.
+ *     publishes staged = seq unless *err_flag is set. The slot needs no
+ *     wait: this rank's merge of step seq - 1 saw every peer's staged
+ *     flag of seq - 1, which a peer publishes only after its merge of step
+ *     seq - 2 (the slot's last reader) has completed in stream order; the
+ *     merged flags stay published for callers that check them.
  *   dsa_shard_exchange_merge: every peer's staged flag >= seq (bounded), the
  *     merge of dsa_indexer_shard_merge over the tp peer slots (plain
  *     relaxed system-scope peer loads) into out rows 0..R-1; the last CTA

@@ -15,7 +15,7 @@ short timeout, and a rank leaves only between merges.
 import datetime
 import importlib
 import os
-import socket
+import tempfile
 
 import numpy as np
 import pytest
@@ -27,18 +27,19 @@ from oracle import dsa_oracle as O
 pytestmark = pytest.mark.gpu
 
 
-def _free_port():
-    with socket.socket() as s:
-        s.bind(("127.0.0.1", 0))
-        return s.getsockname()[1]
+def _rendezvous():
+    """A fresh file-store path for one test's process group (no TCP port that
+    a previous test's store may still hold)."""
+    return os.path.join(tempfile.mkdtemp(prefix="dsa_pg_"), "store")
 
 
-def _worker(rank, world, port, mode, q):
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+def _worker(rank, world, store, mode, q):
+    os.environ.update(NCCL_NVLS_ENABLE="0")
     import torch.distributed as dist
 
     torch.cuda.set_device(rank)
-    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+    dist.init_process_group("nccl", init_method="file://" + store, rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60),
                             device_id=torch.device("cuda", rank))
     cpu = dist.new_group(backend="gloo", timeout=datetime.timedelta(seconds=60))
     try:
@@ -70,8 +71,8 @@ def test_sharded_merge_gpus(mode, world):
         pytest.skip(f"needs {world} GPUs")
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    port = _free_port()  # both ranks rendezvous on it
-    procs = [ctx.Process(target=_worker, args=(r, world, port, mode, q)) for r in range(world)]
+    store = _rendezvous()  # both ranks rendezvous on it
+    procs = [ctx.Process(target=_worker, args=(r, world, store, mode, q)) for r in range(world)]
     for p in procs:
         p.start()
     res = [q.get(timeout=180) for _ in range(world)]
@@ -88,16 +89,17 @@ def test_sharded_merge_gpus(mode, world):
                 np.testing.assert_array_equal(got, exp)
 
 
-def _decode_worker(rank, world, port, mode, q):
+def _decode_worker(rank, world, store, mode, q):
     """One rank of the key-sharded decode layer: this rank scores its key span
     of every row, the exchange merges the local top-K lists into the global
     top-K on every rank, and sparse MLA decode runs on this rank's heads."""
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    os.environ.update(NCCL_NVLS_ENABLE="0")
     import torch.distributed as dist
 
     torch.cuda.set_device(rank)
     dev = torch.device("cuda", rank)
-    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+    dist.init_process_group("nccl", init_method="file://" + store, rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60),
                             device_id=dev)
     cpu = dist.new_group(backend="gloo", timeout=datetime.timedelta(seconds=60))
     try:
@@ -158,8 +160,8 @@ def test_sharded_decode_layer_gpus(mode, world):
         pytest.skip(f"needs {world} GPUs")
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    port = _free_port()
-    procs = [ctx.Process(target=_decode_worker, args=(r, world, port, mode, q)) for r in range(world)]
+    store = _rendezvous()
+    procs = [ctx.Process(target=_decode_worker, args=(r, world, store, mode, q)) for r in range(world)]
     for p in procs:
         p.start()
     res = [q.get(timeout=180) for _ in range(world)]

@@ -889,9 +889,9 @@ def test_topk_rows_payload_matches_topk(dsa):
 def test_decode_exchange_single_rank_steps_and_timeout(dsa):
     """The device-sequenced decode exchange with one rank (its own slots):
     five steps in a row (slots alternate, ctl[0] advances, staged/merged
-    flags follow), each exact against the oracle; then a slot-reuse wait that
-    runs out (merged flag forced behind): TIMEOUT is reported, nothing is
-    published, and the context stays usable."""
+    flags follow), each exact against the oracle; then the merge's wait on a
+    staged flag that runs out (the flag forced back after the stage): TIMEOUT
+    is reported, merged is not published, and the context stays usable."""
     from importlib import import_module
 
     ops = import_module("glm5-on-v100_b200.ops")
@@ -919,13 +919,13 @@ def test_decode_exchange_single_rank_steps_and_timeout(dsa):
     old = ops.P2P_TIMEOUT_NS
     ops.P2P_TIMEOUT_NS = 50_000_000  # 50 ms
     try:
-        ex.fbuf.view(torch.int32)[1] = 0  # merged flag behind: the step-6 slot wait (merged >= 4) cannot finish
         s = rng.standard_normal((B, S)).astype(np.float32)
         ex.topk_stage(to_dev(s), dl, to_dev(O.level1_hist(s, lens)), 0)
+        ex.fbuf.view(torch.int32)[0] = 0  # staged flag forced back: the step-6 merge wait (staged >= 6) cannot finish
         ex.merge(torch.empty(B, K, dtype=torch.int32, device=DEV), B)
         torch.cuda.synchronize()
         assert ops.p2p_failed(DEV)
-        assert ex.fbuf.view(torch.int32)[:2].tolist() == [5, 0]  # neither flag published
+        assert ex.fbuf.view(torch.int32)[:2].tolist() == [0, 5]  # merged not published
     finally:
         ops.P2P_TIMEOUT_NS = old
     x = torch.ones(4, device=DEV) * 2
