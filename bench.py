@@ -872,12 +872,17 @@ class ShardMergeP2PWorkload(ShardMergeWorkload):
         span = self.S // max(self.tp, 1)
         self.vals = [torch.randn(self.R, self.TOPK, device=dev, generator=g) for _ in range(self.nsets)]
         off = torch.randint(0, span, (self.R, 1), device=dev, generator=g)
-        self.pos = ((self.rank * span + (torch.arange(self.TOPK, device=dev).view(1, -1) * 89 + off) % span)
-                    .to(torch.int32).contiguous())
+        pos = (self.rank * span + (torch.arange(self.TOPK, device=dev).view(1, -1) * 89 + off) % span).to(torch.int32)
+        self.pos = torch.sort(pos, dim=1).values.contiguous()  # ascending, as this build's top-k emits its lists
         self.out = torch.empty(self.R, self.TOPK, dtype=torch.int32, device=dev)
 
     def bytes_per_row(self):
         return self.tp * 2 * self.TOPK * 4 + self.TOPK * 4
+
+    def after_timing(self, dsa, dev):
+        if self.shard.p2p_failed:
+            raise RuntimeError("the P2P merge fell back to the all-gather path during the run: the figure would not "
+                               "be a P2P one")
 
     def step_on(self, dsa, vals):
         self._merge([(0, self.R, vals, self.pos)], self.out, self.TOPK, self.shard)
