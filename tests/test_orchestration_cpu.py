@@ -1,8 +1,9 @@
 """Host logic of the indexer orchestration and the MLA glue, on CPU (no GPU):
 shard spans, sub-blocks, payload packing, merge destinations, the torch merge
 epilogue, spec-row expansion, per-token prefill metadata, the P2P exchange's
-slot and flag protocol against a fake IPC backend (two ranks as threads), and
-the key-sharded merge across two gloo ranks (separate processes).
+slot and flag protocol against a fake IPC backend (two ranks as threads), a
+schedule model of the decode exchange's slot reuse, and the key-sharded merge
+across two gloo ranks (separate processes).
 
 Mirrors the reference's orchestration (reference/sparse_attn_indexer.py:
 44-106, :726-1030; reference/triton_mla.py:261-279, :414-466).
@@ -375,3 +376,68 @@ def test_key_sharded_merge_two_gloo_ranks():
         assert p.exitcode == 0
     for rank, got, exp in res:
         np.testing.assert_array_equal(np.sort(got, axis=1), np.sort(exp, axis=1))
+
+
+# ------------------------------------------- decode exchange slot reuse
+def _run_decode_exchange_schedule(tp, steps, rng, merge_waits=True):
+    """Random interleaving of tp ranks running the device-sequenced decode
+    exchange (csrc/topk.cu exchange staging, csrc/shard_merge.cu exchange
+    merge), each rank's kernels in stream order: stage(seq) writes this rank's
+    slot seq & 1 and then publishes staged = seq; merge(seq) waits until every
+    rank's staged >= seq, then reads every rank's slot seq & 1 (the reads may
+    stay in flight across other ranks' events) and completes. Stage(seq + 1)
+    of a rank starts only after its merge(seq) completed. Returns the slot
+    conflicts seen: a stage writing a slot that some rank is still reading,
+    or will still read, for an older step. merge_waits=False drops the
+    merge's wait on the staged flags (the check must then find conflicts)."""
+    staged = [0] * tp
+    seq = [1] * tp                 # next step of each rank
+    phase = ["stage"] * tp         # stage -> merge_wait -> merge_read -> done
+    reading = {}                   # (reader, owner) -> step whose slot is being read
+    reads_left = [set() for _ in range(tp)]
+    conflicts = []
+    while min(seq) <= steps or any(p != "stage" for p in phase):
+        r = int(rng.integers(tp))
+        s = seq[r]
+        if phase[r] == "stage":
+            if s > steps:
+                continue
+            slot = s & 1
+            for (reader, owner), rs in reading.items():
+                if owner == r and (rs & 1) == slot and rs < s:
+                    conflicts.append((r, s, reader, rs))
+            staged[r] = s
+            phase[r] = "merge_wait"
+        elif phase[r] == "merge_wait":
+            if not merge_waits or all(x >= s for x in staged):
+                phase[r] = "merge_read"
+                reads_left[r] = set(range(tp))
+                for q in range(tp):
+                    reading[(r, q)] = s
+        elif phase[r] == "merge_read":
+            q = int(rng.choice(sorted(reads_left[r])))
+            reads_left[r].discard(q)
+            del reading[(r, q)]
+            if not reads_left[r]:
+                phase[r] = "stage"
+                seq[r] += 1
+    return conflicts
+
+
+@pytest.mark.parametrize("tp", [2, 3, 8])
+def test_decode_exchange_slot_reuse_needs_no_wait(tp):
+    """The exchange top-k writes its slot seq & 1 without waiting on the
+    peers' merged flags: over many random interleavings of the ranks, no
+    stage ever overwrites a slot a peer is still reading (the peer's staged
+    flag of the previous step, which this rank's merge waited for, is only
+    published after that peer finished reading the slot)."""
+    rng = np.random.default_rng(tp)
+    for _ in range(200):
+        assert _run_decode_exchange_schedule(tp, steps=6, rng=rng) == []
+
+
+def test_decode_exchange_model_detects_a_missing_wait():
+    """The same model with the merge's staged-flag wait removed does see
+    conflicts, so the check above can fail."""
+    rng = np.random.default_rng(5)
+    assert any(_run_decode_exchange_schedule(2, steps=6, rng=rng, merge_waits=False) for _ in range(200))
