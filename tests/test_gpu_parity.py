@@ -115,8 +115,11 @@ def test_decode_formats(dsa, fmt, q_dtype, o_dtype):
 
 
 @pytest.mark.parametrize("B,H,topk", [(1, 8, 2048), (2, 16, 512), (3, 128, 256), (6, 72, 64), (200, 64, 96),
-                                      (64, 64, 2048)])
+                                      (64, 64, 2048), (8, 64, 2048), (16, 64, 2048)])
 def test_decode_shapes_and_splits(dsa, B, H, topk):
+    """Shapes across the slice plans: 32, 16 and 8 slices with partial
+    states and the slice merge (B = 1, 8, 16 at top-2048), two slices merged
+    in a cluster (B = 64), one slice (B = 200)."""
     rng = np.random.default_rng(B * 1000 + H)
     seq = rng.integers(1, 6000, size=B)
     c = cases.decode_case(31 + B, B=B, H=H, page=64, seq_lens=seq, topk=topk, blocks_per_seq=94)
