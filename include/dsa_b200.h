@@ -376,8 +376,10 @@ int dsa_indexer_shard_stage(float* slot, const float* vals,
  *     merge of dsa_indexer_shard_merge over the tp peer slots (plain
  *     relaxed system-scope peer loads) into out rows 0..R-1; the last CTA
  *     publishes merged = seq and sets ctl[0] = seq.
- * A wait that expires sets *err_flag = DSA_ERR_TIMEOUT; later calls then
- * publish nothing and the host must rebuild the exchange.
+ * Every rank calls stage then merge, step after step, on one stream (the
+ * slot reuse above relies on that order). A wait that expires sets
+ * *err_flag = DSA_ERR_TIMEOUT; later calls then publish nothing and the host
+ * must rebuild the exchange.
  * ===================================================================== */
 int dsa_shard_exchange_topk(const float* score, int64_t score_stride,
                             int max_kv, const int32_t* lens, int32_t* hist,
